@@ -1,0 +1,222 @@
+/*
+ * moe_b200 — B200 (sm_100a) MoE feed-forward operator, C ABI.
+ *
+ * Drop-in replacement for the grouped-MoE operator surface that the
+ * happyme531/open_rknpu2_lm_infer Rust crate binds through bindgen
+ * (build.rs:137-145 over the absent native/rk_npu_matmul include/rk_npu_moe_w8.h;
+ * call sites in src/npu/moe.rs and src/npu.rs). Each declaration names the
+ * reference entry point it replaces. Plain pointers and sizes only; every
+ * function returns 0 on success or a negative MOE_B200_ERR_* code, and
+ * creators return NULL on failure (as Handle::new expects, src/npu.rs:176-180).
+ *
+ * Weight layout at the boundary is the reference's QuantMatrix
+ * (src/npu.rs:135-157): codes int8 [k][n] (row k holds the n output channels),
+ * f32 per-output-channel scales [n]. gate_up has n = 2*intermediate with the
+ * gate columns first (src/model/checkpoint.rs:573-605); down has k =
+ * intermediate, n = hidden. The group-32 fp16 scale format is an extension
+ * (the reference loader rejects group scales, src/model/checkpoint.rs:251-263).
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- error codes (rk_npu_strerror convention, src/npu.rs:187-193) ------- */
+#define MOE_B200_OK 0
+#define MOE_B200_ERR_INVALID (-1)       /* bad argument / shape */
+#define MOE_B200_ERR_UNSUPPORTED (-2)   /* shape or format outside this build */
+#define MOE_B200_ERR_NOMEM (-3)         /* device or host allocation failed */
+#define MOE_B200_ERR_CUDA (-4)          /* CUDA runtime error */
+#define MOE_B200_ERR_CAPACITY (-5)      /* rows above the workspace max_rows */
+#define MOE_B200_ERR_DEVICE_TIMEOUT (-6) /* a bounded device wait gave up */
+#define MOE_B200_ERR_BAD_EXPERT (-7)    /* expert id outside [0, experts) */
+#define MOE_B200_ERR_NONFINITE (-8)     /* non-finite router logit / activation */
+#define MOE_B200_ERR_BAD_ROUTE (-9)     /* negative or NaN routing weight */
+#define MOE_B200_ERR_NO_DEVICE (-10)    /* no sm_100 device / library built without it */
+
+/* Routed-expert weight formats. */
+#define MOE_B200_W4_PER_CHANNEL 0 /* reference native format: int4 codes, f32 scale per n */
+#define MOE_B200_W4_G32_FP16 1    /* int4 codes, fp16 scale per (32 k, n) group */
+#define MOE_B200_W8_PER_CHANNEL 2 /* int8 codes, f32 scale per n */
+
+/* Router accumulation order (src/model/cpu.rs:96-153, dense_dot). */
+#define MOE_B200_ROUTER_NEON16 0     /* aarch64 F32 branch: 4x4-lane FMA + fixed tree */
+#define MOE_B200_ROUTER_SEQUENTIAL 1 /* x86 scalar loop: separately rounded mul + add */
+
+/* Shared expert arithmetic. */
+#define MOE_B200_SHARED_JOINT 0 /* MoE input quantisation, nearest-even (joint bank) */
+#define MOE_B200_SHARED_DENSE 1 /* separate dense W8A8 FFN, round-away quantisation */
+
+typedef struct moe_b200_weights moe_b200_weights;
+typedef struct moe_b200_workspace moe_b200_workspace;
+typedef struct moe_b200_router moe_b200_router;
+
+/* Replaces rk_npu_moe_w8_weight_config (fields used at src/npu/moe.rs:245-250). */
+typedef struct {
+    int32_t hidden;
+    int32_t intermediate;
+    int32_t routed_experts;
+    int32_t shared_expert;        /* 0 or 1 */
+    int32_t shared_intermediate;  /* extension; 0 = same as intermediate */
+} moe_b200_weight_config;
+
+/* Replaces rk_npu_moe_w8_config (src/npu/moe.rs:179-192). npu_cores and
+ * cpu_threads have no meaning here and are kept only for source parity. */
+typedef struct {
+    moe_b200_weight_config weights;
+    int32_t top;
+    int32_t max_rows;      /* the reference's `chunk` (Moe::max_rows) */
+    int32_t device;        /* CUDA device ordinal */
+    int32_t npu_cores;     /* ignored */
+    int32_t cpu_threads;   /* ignored */
+} moe_b200_config;
+
+/* Replaces rk_npu_moe_w8_expert (src/npu/moe.rs:121-126). The *_group_scales
+ * pointers are read only for MOE_B200_W4_G32_FP16: IEEE fp16 bits laid out
+ * [k/32][n]. */
+typedef struct {
+    const int8_t *gate_up;
+    const float *gate_up_scales;
+    const int8_t *down;
+    const float *down_scales;
+    const uint16_t *gate_up_group_scales;
+    const uint16_t *down_group_scales;
+} moe_b200_expert;
+
+/* Extension: weight formats of one bank. */
+typedef struct {
+    int32_t routed_format;  /* MOE_B200_W4_* / MOE_B200_W8_* */
+    int32_t shared_format;  /* MOE_B200_W8_PER_CHANNEL or MOE_B200_W4_PER_CHANNEL */
+    int32_t shared_mode;    /* MOE_B200_SHARED_* */
+} moe_b200_format;
+
+/* Replaces rk_npu_moe_w8_timings (fields read at src/npu/moe.rs:342-351).
+ * Filled from CUDA events: input_us = activation quantisation, schedule_us =
+ * route histogram + permutation, gather_us = row gather, gate_us = gate/up
+ * GEMM + SwiGLU, middle_cpu_us = middle requantisation, down_us = down GEMM,
+ * combine_us = weighted combine (+ shared + residual), build_us = shared
+ * expert, total_us = whole call. Counters are work items of the launch. */
+typedef struct {
+    double input_us, schedule_us, build_us, sync_us, gather_us, gate_us;
+    double middle_npu_us, middle_cpu_us, down_us, combine_us, lut_load_us, total_us;
+    int64_t gather_tasks, middle_tasks, gemm_tasks;
+    double router_us; /* extension: router logits + top-k (forward only) */
+} moe_b200_timings;
+
+/* ---- configuration / objects ------------------------------------------- */
+
+/* Replaces rk_npu_moe_w8_config_init(cfg, h, f, e, shared, top, chunk). */
+void moe_b200_config_init(moe_b200_config *cfg, int32_t hidden, int32_t intermediate,
+                          int32_t experts, int32_t shared, int32_t top, int32_t max_rows);
+
+/* Replaces rk_npu_moe_quant_weights_create / _full_k / rk_npu_moe_w4_weights_create
+ * (src/npu/moe.rs:131-139). experts[routed_experts] (+ experts[routed_experts]
+ * = the shared expert when shared_expert = 1, as at src/npu/moe.rs:128-130).
+ * Host arrays are copied and packed; the caller may free them afterwards. */
+moe_b200_weights *moe_b200_weights_create(const moe_b200_config *cfg,
+                                          const moe_b200_expert *experts,
+                                          const moe_b200_format *format);
+/* Replaces rk_npu_moe_w8_weights_free. */
+void moe_b200_weights_free(moe_b200_weights *w);
+/* Replaces rk_npu_moe_w8_weights_device_bytes. */
+uint64_t moe_b200_weights_device_bytes(const moe_b200_weights *w);
+
+/* Replaces rk_npu_moe_quant_workspace_create / rk_npu_moe_w4_workspace_create
+ * (src/npu/moe.rs:200-206). One workspace per stream; reusable by every
+ * bank of the same geometry. */
+moe_b200_workspace *moe_b200_workspace_create(const moe_b200_config *cfg);
+/* Replaces rk_npu_moe_w8_workspace_free. */
+void moe_b200_workspace_free(moe_b200_workspace *ws);
+/* Replaces rk_npu_moe_w8_workspace_device_bytes. */
+uint64_t moe_b200_workspace_device_bytes(const moe_b200_workspace *ws);
+/* Moe::max_rows (src/npu/moe.rs:321-323). */
+int32_t moe_b200_max_rows(const moe_b200_workspace *ws);
+
+/* Replaces rk_npu_moe_w8_run_f32 (src/npu/moe.rs:372-386): host pointers,
+ * synchronous. input [rows][hidden] f32, ids/routes [rows][top], output
+ * [rows][hidden] f32 = weighted routed combine (+ shared expert if the bank
+ * has one). timings may be NULL. */
+int moe_b200_run_f32(moe_b200_workspace *ws, const moe_b200_weights *w, int32_t rows,
+                     const float *input, const int32_t *ids, const float *routes,
+                     float *output, moe_b200_timings *timings);
+
+/* Extension: same as moe_b200_run_f32 on device pointers, stream-ordered and
+ * asynchronous (no host synchronisation). stream is a cudaStream_t. */
+int moe_b200_run_device(moe_b200_workspace *ws, const moe_b200_weights *w, int32_t rows,
+                        const float *d_input, const int32_t *d_ids, const float *d_routes,
+                        float *d_output, void *stream);
+
+/* ---- router-inclusive path (extension; replaces the CPU router of
+ * src/model/qwen35/moe.rs:215-241 and the decoder residual add of
+ * src/model/qwen35/decoder.rs:215-217) ------------------------------------ */
+
+/* router [experts][hidden] f32 (row e = expert e); bias [experts] f32 added to
+ * every logit, or NULL; order MOE_B200_ROUTER_*; min_weight = pruning
+ * threshold (src/model/experts/pruning.rs:32-41), 0 = off. */
+moe_b200_router *moe_b200_router_create(const moe_b200_config *cfg, const float *router,
+                                        const float *bias, int32_t order, float min_weight);
+void moe_b200_router_free(moe_b200_router *r);
+
+/* Host pointers, synchronous: output = residual + (routed + shared); residual
+ * may be NULL. ids/routes, if not NULL, receive the routing [rows][top]. */
+int moe_b200_forward_f32(moe_b200_workspace *ws, const moe_b200_weights *w,
+                         const moe_b200_router *r, int32_t rows, const float *input,
+                         const float *residual, float *output, int32_t *ids, float *routes,
+                         moe_b200_timings *timings);
+/* Device pointers, asynchronous on stream. */
+int moe_b200_forward_device(moe_b200_workspace *ws, const moe_b200_weights *w,
+                            const moe_b200_router *r, int32_t rows, const float *d_input,
+                            const float *d_residual, float *d_output, void *stream);
+
+/* ---- stage entry points (extension; for parity checks and expert
+ * parallelism). All device pointers, asynchronous. ---------------------- */
+
+/* Router logits (may be NULL) + top-k/softmax/pruning. */
+int moe_b200_route_device(moe_b200_workspace *ws, const moe_b200_router *r, int32_t rows,
+                          const float *d_input, float *d_logits, int32_t *d_ids,
+                          float *d_routes, void *stream);
+
+/* Reads back the workspace's device status word (after synchronising the
+ * workspace's last stream) and clears it. Returns 0 or an ERR_DEVICE code. */
+int moe_b200_workspace_status(moe_b200_workspace *ws);
+
+/* Device address and size of a workspace buffer, for inspection by tests:
+ * "q_x","s_x","perm","pos","offsets","a_perm","s_perm","middle","rowmax",
+ * "q_m","s_m","y","shared_y","logits". Valid until the next call. */
+int moe_b200_workspace_buffer(moe_b200_workspace *ws, const char *name, void **d_ptr,
+                              uint64_t *bytes);
+
+/* Re-runs one grouped GEMM of the last call in accumulator-dump mode:
+ * which = 0 (routed gate/up), 1 (routed down). Writes the raw int32
+ * accumulators: per-channel [rows][n], group-32 [rows][k/32][n], rows in the
+ * permuted order of "perm". */
+int moe_b200_debug_accumulators(moe_b200_workspace *ws, const moe_b200_weights *w,
+                                int32_t which, int32_t *d_acc, uint64_t capacity_elems,
+                                void *stream);
+
+/* Stage profiling of device-pointer calls (extension). While enabled, every
+ * run/forward call records CUDA events between its stages on the launching
+ * stream into a ring of 256 slots (slot = call index since enabling); no host
+ * synchronisation is added. profile_read synchronises on the slot's last
+ * event and fills the stage fields of *t for call `call` (0-based). */
+int moe_b200_workspace_profile(moe_b200_workspace *ws, int32_t enable);
+int moe_b200_workspace_profile_read(moe_b200_workspace *ws, int32_t call, moe_b200_timings *t);
+
+/* Number of kernels this workspace has launched since creation. */
+int64_t moe_b200_workspace_launches(const moe_b200_workspace *ws);
+
+/* Replaces rk_npu_strerror (src/npu.rs:187-193). */
+const char *moe_b200_strerror(int code);
+
+/* Library build/identity: returns "moe_b200 <version> sm_100a". */
+const char *moe_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOE_B200_H */

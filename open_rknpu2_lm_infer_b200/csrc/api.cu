@@ -1,0 +1,990 @@
+// C ABI of the B200 MoE operator (include/moe_b200.h): weight packing,
+// workspaces, router objects and the stage orchestration of one MoE call.
+//
+// Replaces the grouped-MoE operator behind src/npu/moe.rs (Backend::load_moe*,
+// Moe::run) of happyme531/open_rknpu2_lm_infer. The call sequence of one run:
+//   route_count -> route_scatter -> quant_gather          (dispatch)
+//   gemm<gate/up, SwiGLU> -> requant -> gemm<down>         (routed experts)
+//   [shared expert: quantise -> gemm -> requant -> gemm]
+//   combine (+ shared + residual)
+#include <cudaTypedefs.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/moe_b200.h"
+#include "kernels.cuh"
+
+using namespace moe;
+
+namespace {
+
+// ---- allocation with optional host-side failure injection -----------------
+// MOE_B200_FAIL_ALLOC_AFTER=N makes the N-th device allocation (counted from
+// process start, 1-based) fail with MOE_B200_ERR_NOMEM, like the reference's
+// workspace fault shim (tests/board/workspace_fault_ioctl.c:21-62).
+std::mutex g_alloc_mu;
+long g_alloc_count = 0;
+
+cudaError_t dev_alloc(void** p, size_t bytes) {
+    {
+        std::lock_guard<std::mutex> lk(g_alloc_mu);
+        ++g_alloc_count;
+        const char* env = getenv("MOE_B200_FAIL_ALLOC_AFTER");
+        if (env && atol(env) > 0 && g_alloc_count == atol(env)) {
+            *p = nullptr;
+            return cudaErrorMemoryAllocation;
+        }
+    }
+    if (bytes == 0) bytes = 16;
+    return cudaMalloc(p, bytes);
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int cuda_rc(cudaError_t e) {
+    if (e == cudaSuccess) return MOE_B200_OK;
+    if (e == cudaErrorMemoryAllocation) return MOE_B200_ERR_NOMEM;
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver || e == cudaErrorNoKernelImageForDevice)
+        return MOE_B200_ERR_NO_DEVICE;
+    return MOE_B200_ERR_CUDA;
+}
+
+int check_device(int dev, int* num_sms) {
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || dev < 0 || dev >= count)
+        return MOE_B200_ERR_NO_DEVICE;
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (major != 10) return MOE_B200_ERR_NO_DEVICE;  // built for sm_100a only
+    if (num_sms) cudaDeviceGetAttribute(num_sms, cudaDevAttrMultiProcessorCount, dev);
+    return MOE_B200_OK;
+}
+
+int pad_to(int v, int m) { return (v + m - 1) / m * m; }
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D map over an int8 row-major [rows][cols] buffer, box = 128 bytes x nt rows,
+// 128-byte swizzle (matches the MMA operand layout).
+int make_act_map(CUtensorMap* map, const void* base, int rows, int cols, int nt) {
+    auto enc = get_encode();
+    if (!enc) return MOE_B200_ERR_CUDA;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols};
+    cuuint32_t box[2] = {128, (cuuint32_t)nt};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? MOE_B200_OK : MOE_B200_ERR_CUDA;
+}
+
+constexpr int kNTs[3] = {16, 32, 64};
+int nt_index(int nt) { return nt == 16 ? 0 : nt == 32 ? 1 : 2; }
+// Token tile (MMA N) from the expected rows per expert.
+int choose_nt(long rows, int experts) {
+    const long avg = experts > 0 ? (rows + experts - 1) / experts : rows;
+    if (avg <= 16) return 16;
+    if (avg <= 32) return 32;
+    return 64;
+}
+
+// ---- packed matrices ------------------------------------------------------
+
+struct PackedMat {
+    uint8_t* w = nullptr;
+    void* s = nullptr;
+    size_t w_expert_stride = 0, w_tile_stride = 0;
+    size_t s_expert_stride = 0, s_tile_stride = 0;
+    int fmt = 0, kblocks = 0, row_tiles = 0, experts = 0;
+    int k = 0, n = 0;        // logical K and output channels (n = I for SwiGLU)
+    bool swiglu = false;
+};
+
+// Byte offset of element (row, kbyte) in a 128-row x 128-byte operand tile
+// stored in the 128-byte swizzle layout (8-row atoms of 1024 bytes, 16-byte
+// chunk index XOR row%8).
+inline size_t sw128(int row, int kbyte) {
+    return (size_t)(row / 8) * 1024 + (row % 8) * 128 + (((kbyte / 16) ^ (row % 8)) * 16) +
+           (kbyte % 16);
+}
+
+// Weight channel held by tile row lr of row tile rt, or -1 for padding.
+inline int tile_channel(const PackedMat& m, int rt, int lr) {
+    if (m.swiglu) {
+        const int c = rt * 64 + (lr & 63);
+        if (c >= m.n) return -1;
+        return lr < 64 ? c : m.n + c;  // gate columns first, then up (concatenate order)
+    }
+    const int c = rt * 128 + lr;
+    return c < m.n ? c : -1;
+}
+
+// Packs one reference-layout matrix (codes [K][N], N = 2n for SwiGLU) into
+// tile-major device order. host_w / host_s point at this expert's slot.
+void pack_expert(const PackedMat& m, const int8_t* codes, const float* scales,
+                 const uint16_t* gscales, uint8_t* host_w, uint8_t* host_s) {
+    const int K = m.k;
+    const int N = m.swiglu ? 2 * m.n : m.n;
+    const bool w4 = m.fmt != kFmtW8PC;
+    const size_t tile_bytes = w4 ? 8192 : 16384;
+    for (int rt = 0; rt < m.row_tiles; ++rt) {
+        for (int lr = 0; lr < 128; ++lr) {
+            const int ch = tile_channel(m, rt, lr);
+            for (int kb = 0; kb < m.kblocks; ++kb) {
+                uint8_t* tile = host_w + (size_t)rt * m.w_tile_stride + (size_t)kb * tile_bytes;
+                for (int kbyte = 0; kbyte < 128; ++kbyte) {
+                    const int k = kb * 128 + kbyte;
+                    const int8_t code = (ch >= 0 && k < K) ? codes[(size_t)k * N + ch] : 0;
+                    const size_t o = sw128(lr, kbyte);
+                    if (!w4) {
+                        tile[o] = (uint8_t)code;
+                    } else {
+                        // int8 offset o comes from 32-bit packed word o/8: low nibbles
+                        // give bytes 0..3 of the 8, high nibbles bytes 4..7
+                        const size_t word = o / 8, within = o % 8;
+                        const size_t pb = word * 4 + (within & 3);
+                        const uint8_t nib = (uint8_t)code & 0xF;
+                        if (within < 4)
+                            tile[pb] = (uint8_t)((tile[pb] & 0xF0) | nib);
+                        else
+                            tile[pb] = (uint8_t)((tile[pb] & 0x0F) | (nib << 4));
+                    }
+                }
+            }
+            if (m.fmt == kFmtW4G32) {
+                uint16_t* st = reinterpret_cast<uint16_t*>(host_s + (size_t)rt * m.s_tile_stride);
+                for (int g = 0; g < m.kblocks * 4; ++g)
+                    st[(size_t)g * 128 + lr] =
+                        (ch >= 0 && g * 32 < K) ? gscales[(size_t)g * N + ch] : (uint16_t)0;
+            } else {
+                float* st = reinterpret_cast<float*>(host_s + (size_t)rt * m.s_tile_stride);
+                st[lr] = ch >= 0 ? scales[ch] : 0.0f;
+            }
+        }
+    }
+}
+
+int setup_mat(PackedMat& m, int fmt, int experts, int K, int n, bool swiglu) {
+    m.fmt = fmt;
+    m.experts = experts;
+    m.k = K;
+    m.n = n;
+    m.swiglu = swiglu;
+    m.kblocks = pad_to(K, 128) / 128;
+    m.row_tiles = swiglu ? (n + 63) / 64 : (n + 127) / 128;
+    const size_t tile_bytes = fmt == kFmtW8PC ? 16384 : 8192;
+    m.w_tile_stride = (size_t)m.kblocks * tile_bytes;
+    m.w_expert_stride = (size_t)m.row_tiles * m.w_tile_stride;
+    m.s_tile_stride = fmt == kFmtW4G32 ? (size_t)m.kblocks * 1024 : 512;
+    m.s_expert_stride = (size_t)m.row_tiles * m.s_tile_stride;
+    return MOE_B200_OK;
+}
+
+}  // namespace
+
+// ---- opaque objects ---------------------------------------------------------
+
+struct moe_b200_weights {
+    int device = 0;
+    int H = 0, I = 0, E = 0, shared = 0, Is = 0, top = 0;
+    int shared_mode = MOE_B200_SHARED_DENSE;
+    PackedMat gu, dn, sgu, sdn;
+    uint64_t bytes = 0;
+};
+
+struct moe_b200_router {
+    int device = 0, H = 0, E = 0, order = 0;
+    float min_weight = 0.0f;
+    float* w = nullptr;
+    float* bias = nullptr;
+};
+
+struct moe_b200_workspace {
+    int device = 0, H = 0, I = 0, E = 0, k = 0, max_rows = 0, Is = 0, num_sms = 0;
+    int Kh = 0, Ki = 0, Kis = 0;
+    long n_max = 0;
+    std::vector<void*> allocs;
+    uint64_t bytes = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t last_stream = nullptr;
+    // staging for the host-pointer API
+    float *x = nullptr, *out = nullptr, *res = nullptr, *routes = nullptr;
+    int32_t* ids = nullptr;
+    // dispatch
+    int8_t* q_x = nullptr;
+    float* s_x = nullptr;
+    int32_t *hist = nullptr, *offsets = nullptr, *perm = nullptr, *pos = nullptr;
+    int32_t *shared_offsets = nullptr, *counters = nullptr;
+    int8_t* a_perm = nullptr;
+    float* s_perm = nullptr;
+    // routed experts
+    float* middle = nullptr;
+    uint32_t* rowmax = nullptr;
+    int8_t* q_m = nullptr;
+    float *s_m = nullptr, *y = nullptr;
+    // shared expert
+    int8_t *q_xd = nullptr, *sq_m = nullptr;
+    float *s_xd = nullptr, *s_middle = nullptr, *ss_m = nullptr, *s_y = nullptr;
+    uint32_t* s_rowmax = nullptr;
+    float* logits = nullptr;
+    uint32_t* err = nullptr;
+    CUtensorMap map_a[3], map_qm[3], map_qx[3], map_qxd[3], map_sqm[3];
+    cudaEvent_t ev[12] = {};
+    // stage-profiling ring of device calls
+    static constexpr int kProfSlots = 64, kProfEvents = 9;
+    bool profiling = false;
+    int prof_calls = 0;
+    std::vector<cudaEvent_t> prof_ev;
+    std::vector<int> prof_flags;  // bit0 router ran, bit1 shared ran
+    int64_t launches = 0;
+    // last call, for accumulator dumps
+    int last_rows = 0;
+    int last_nt_gu = 16, last_nt_dn = 16;
+    const moe_b200_weights* last_w = nullptr;
+};
+
+namespace {
+
+template <typename T>
+int ws_alloc(moe_b200_workspace* ws, T** p, size_t count) {
+    void* v = nullptr;
+    const size_t bytes = sizeof(T) * (count > 0 ? count : 1);
+    cudaError_t e = dev_alloc(&v, bytes);
+    if (e != cudaSuccess) return MOE_B200_ERR_NOMEM;
+    ws->allocs.push_back(v);
+    ws->bytes += bytes;
+    *p = static_cast<T*>(v);
+    return MOE_B200_OK;
+}
+
+int map_err_bits(uint32_t bits) {
+    if (bits & kErrWaitTimeout) return MOE_B200_ERR_DEVICE_TIMEOUT;
+    if (bits & kErrBadExpert) return MOE_B200_ERR_BAD_EXPERT;
+    if (bits & kErrBadRoute) return MOE_B200_ERR_BAD_ROUTE;
+    if (bits & kErrNonFinite) return MOE_B200_ERR_NONFINITE;
+    if (bits & kErrCapacity) return MOE_B200_ERR_CAPACITY;
+    return MOE_B200_OK;
+}
+
+GemmArgs gemm_args(moe_b200_workspace* ws, const PackedMat& m, const float* act_scale,
+                   const int32_t* offsets, int experts, long max_rows, float* out, int ldo,
+                   uint32_t* rowmax) {
+    GemmArgs a{};
+    a.act_scale = act_scale;
+    a.offsets = offsets;
+    a.num_experts = experts;
+    a.max_rows = (int)max_rows;
+    a.w = m.w;
+    a.w_expert_stride = m.w_expert_stride;
+    a.w_tile_stride = m.w_tile_stride;
+    a.wscale = m.s;
+    a.ws_expert_stride = m.s_expert_stride;
+    a.ws_tile_stride = m.s_tile_stride;
+    a.kblocks = m.kblocks;
+    a.row_tiles = m.row_tiles;
+    a.out = out;
+    a.ldo = ldo;
+    a.n_valid = m.n;
+    a.rowmax = rowmax;
+    a.swiglu_layout = m.swiglu ? 1 : 0;
+    a.err = ws->err;
+    return a;
+}
+
+// Shared expert FFN over all rows (joint: reuses q_x; dense: own quantisation).
+int run_shared(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
+               cudaStream_t s) {
+    const int rule = w->shared_mode == MOE_B200_SHARED_JOINT ? kQuantMoe : kQuantDense;
+    const int nt = choose_nt(rows, 1);
+    const CUtensorMap* amap = &ws->map_qx[nt_index(nt)];
+    const float* ascale = ws->s_x;
+    if (w->shared_mode != MOE_B200_SHARED_JOINT) {
+        launch_quant_gather(d_x, rows, ws->H, ws->Kh, kQuantDense, 1, nullptr, ws->q_xd, ws->s_xd,
+                            nullptr, nullptr, ws->err, s);
+        amap = &ws->map_qxd[nt_index(nt)];
+        ascale = ws->s_xd;
+    }
+    cudaMemsetAsync(ws->s_rowmax, 0, sizeof(uint32_t) * rows, s);
+    GemmArgs g = gemm_args(ws, w->sgu, ascale, ws->shared_offsets, 1, rows, ws->s_middle, w->Is,
+                           ws->s_rowmax);
+    if (launch_gemm(*amap, g, w->sgu.fmt, kEpiSwiGLU, nt, ws->num_sms, s)) return MOE_B200_ERR_UNSUPPORTED;
+    launch_requant(ws->s_middle, ws->s_rowmax, ws->shared_offsets + 1, rows, w->Is, ws->Kis, rule,
+                   ws->sq_m, ws->ss_m, s);
+    GemmArgs d = gemm_args(ws, w->sdn, ws->ss_m, ws->shared_offsets, 1, rows, ws->s_y, ws->H,
+                           nullptr);
+    if (launch_gemm(ws->map_sqm[nt_index(nt)], d, w->sdn.fmt, kEpiStore, nt, ws->num_sms, s))
+        return MOE_B200_ERR_UNSUPPORTED;
+    return MOE_B200_OK;
+}
+
+int compatible(const moe_b200_workspace* ws, const moe_b200_weights* w) {
+    if (!ws || !w) return MOE_B200_ERR_INVALID;
+    if (ws->H != w->H || ws->I != w->I || ws->E != w->E || ws->k != w->top ||
+        ws->device != w->device)
+        return MOE_B200_ERR_INVALID;
+    if (w->shared && ws->Is < w->Is) return MOE_B200_ERR_INVALID;
+    return MOE_B200_OK;
+}
+
+// Event set of the next profiled device call (nullptr when profiling is off).
+cudaEvent_t* prof_slot(moe_b200_workspace* ws, int flags) {
+    if (!ws->profiling) return nullptr;
+    const int slot = ws->prof_calls % moe_b200_workspace::kProfSlots;
+    ws->prof_flags[slot] = flags;
+    ++ws->prof_calls;
+    return &ws->prof_ev[(size_t)slot * moe_b200_workspace::kProfEvents];
+}
+
+// The whole routed (+ shared) pipeline on device pointers. ev != null records
+// stage events for run_profiled-style timings.
+int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
+                 const int32_t* d_ids, const float* d_routes, const float* d_res, float* d_out,
+                 cudaStream_t s, cudaEvent_t* evs) {
+    const int E = ws->E, k = ws->k, H = ws->H, I = ws->I;
+    const long n = (long)rows * k;
+    auto mark = [&](int i) {
+        if (evs) cudaEventRecord(evs[i], s);
+    };
+    ws->launches += (n + kRouteChunk - 1) / kRouteChunk > 0 ? 6 : 5;
+    if (w->shared) ws->launches += w->shared_mode == MOE_B200_SHARED_JOINT ? 3 : 4;
+    mark(1);
+    launch_route_count(d_ids, d_routes, (int)n, E, ws->hist, ws->err, s);
+    launch_route_scatter(d_ids, d_routes, (int)n, E, ws->hist, ws->offsets, ws->perm, ws->pos,
+                         ws->shared_offsets, rows, s);
+    mark(2);
+    launch_quant_gather(d_x, rows, H, ws->Kh, kQuantMoe, k, ws->pos, ws->q_x, ws->s_x, ws->a_perm,
+                        ws->s_perm, ws->err, s);
+    mark(3);
+    cudaMemsetAsync(ws->rowmax, 0, sizeof(uint32_t) * n, s);
+    const int nt = choose_nt(n, E);
+    GemmArgs g = gemm_args(ws, w->gu, ws->s_perm, ws->offsets, E, n, ws->middle, I, ws->rowmax);
+    if (launch_gemm(ws->map_a[nt_index(nt)], g, w->gu.fmt, kEpiSwiGLU, nt, ws->num_sms, s))
+        return MOE_B200_ERR_UNSUPPORTED;
+    mark(4);
+    launch_requant(ws->middle, ws->rowmax, ws->offsets + E, (int)n, I, ws->Ki, kQuantMoe, ws->q_m,
+                   ws->s_m, s);
+    mark(5);
+    GemmArgs d = gemm_args(ws, w->dn, ws->s_m, ws->offsets, E, n, ws->y, H, nullptr);
+    if (launch_gemm(ws->map_qm[nt_index(nt)], d, w->dn.fmt, kEpiStore, nt, ws->num_sms, s))
+        return MOE_B200_ERR_UNSUPPORTED;
+    mark(6);
+    if (w->shared) {
+        int rc = run_shared(ws, w, rows, d_x, s);
+        if (rc) return rc;
+    }
+    mark(7);
+    launch_combine(ws->y, ws->pos, d_routes, w->shared ? ws->s_y : nullptr, d_res, rows, H, k,
+                   d_out, s);
+    mark(8);
+    ws->last_rows = rows;
+    ws->last_nt_gu = nt;
+    ws->last_nt_dn = nt;
+    ws->last_w = w;
+    ws->last_stream = s;
+    cudaError_t e = cudaPeekAtLastError();
+    return cuda_rc(e);
+}
+
+float ev_ms(cudaEvent_t a, cudaEvent_t b) {
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, a, b);
+    return ms;
+}
+
+void fill_timings_from(const cudaEvent_t* ev, moe_b200_workspace* ws, moe_b200_timings* t,
+                       int rows, bool routed_by_us, bool shared) {
+    memset(t, 0, sizeof(*t));
+    t->router_us = routed_by_us ? 1000.0 * ev_ms(ev[0], ev[1]) : 0.0;
+    t->schedule_us = 1000.0 * ev_ms(ev[1], ev[2]);
+    t->input_us = 1000.0 * ev_ms(ev[2], ev[3]);
+    t->gather_us = 0.0;  // the gather is fused into the input quantisation
+    t->gate_us = 1000.0 * ev_ms(ev[3], ev[4]);
+    t->middle_cpu_us = 1000.0 * ev_ms(ev[4], ev[5]);
+    t->down_us = 1000.0 * ev_ms(ev[5], ev[6]);
+    t->build_us = shared ? 1000.0 * ev_ms(ev[6], ev[7]) : 0.0;
+    t->combine_us = 1000.0 * ev_ms(ev[7], ev[8]);
+    t->total_us = 1000.0 * ev_ms(ev[0], ev[8]);
+    t->gather_tasks = (int64_t)rows * ws->k;
+    t->middle_tasks = (int64_t)rows * ws->k;
+    t->gemm_tasks = 2;
+}
+
+void fill_timings(moe_b200_workspace* ws, moe_b200_timings* t, int rows, bool routed_by_us,
+                  bool shared) {
+    fill_timings_from(ws->ev, ws, t, rows, routed_by_us, shared);
+}
+
+int read_status(moe_b200_workspace* ws, cudaStream_t s) {
+    uint32_t bits = 0;
+    cudaError_t e = cudaMemcpyAsync(&bits, ws->err, sizeof(bits), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_rc(e);
+    if (bits) {
+        cudaMemsetAsync(ws->err, 0, sizeof(uint32_t), s);
+        cudaStreamSynchronize(s);
+    }
+    return map_err_bits(bits);
+}
+
+int validate_host_routes(const moe_b200_workspace* ws, int rows, const int32_t* ids,
+                         const float* routes) {
+    const long n = (long)rows * ws->k;
+    for (long a = 0; a < n; ++a) {
+        if (!(routes[a] >= 0.0f) || !(routes[a] <= 3.4e38f)) return MOE_B200_ERR_BAD_ROUTE;
+        if (routes[a] > 0.0f && (ids[a] < 0 || ids[a] >= ws->E)) return MOE_B200_ERR_BAD_EXPERT;
+    }
+    return MOE_B200_OK;
+}
+
+}  // namespace
+
+// ===================================================================== C ABI
+
+extern "C" {
+
+void moe_b200_config_init(moe_b200_config* cfg, int32_t hidden, int32_t intermediate,
+                          int32_t experts, int32_t shared, int32_t top, int32_t max_rows) {
+    if (!cfg) return;
+    memset(cfg, 0, sizeof(*cfg));
+    cfg->weights.hidden = hidden;
+    cfg->weights.intermediate = intermediate;
+    cfg->weights.routed_experts = experts;
+    cfg->weights.shared_expert = shared ? 1 : 0;
+    cfg->weights.shared_intermediate = 0;
+    cfg->top = top;
+    cfg->max_rows = max_rows;
+    cfg->device = 0;
+    cfg->npu_cores = 0;
+    cfg->cpu_threads = 0;
+}
+
+static int validate_config(const moe_b200_config* cfg) {
+    if (!cfg) return MOE_B200_ERR_INVALID;
+    const moe_b200_weight_config& w = cfg->weights;
+    if (w.hidden <= 0 || w.intermediate <= 0 || w.routed_experts <= 0 || cfg->top <= 0 ||
+        cfg->max_rows <= 0)
+        return MOE_B200_ERR_INVALID;
+    if (cfg->top > w.routed_experts || cfg->top > 32 || w.routed_experts > 1024)
+        return MOE_B200_ERR_UNSUPPORTED;
+    if (w.hidden % 32 || w.intermediate % 32) return MOE_B200_ERR_UNSUPPORTED;
+    const int is = w.shared_intermediate > 0 ? w.shared_intermediate : w.intermediate;
+    if (w.shared_expert && is % 32) return MOE_B200_ERR_UNSUPPORTED;
+    return MOE_B200_OK;
+}
+
+moe_b200_weights* moe_b200_weights_create(const moe_b200_config* cfg,
+                                          const moe_b200_expert* experts,
+                                          const moe_b200_format* format) {
+    if (validate_config(cfg) || !experts) return nullptr;
+    if (check_device(cfg->device, nullptr)) return nullptr;
+    DeviceGuard guard(cfg->device);
+    moe_b200_format fmt{MOE_B200_W4_PER_CHANNEL, MOE_B200_W8_PER_CHANNEL, MOE_B200_SHARED_JOINT};
+    if (format) fmt = *format;
+    const int H = cfg->weights.hidden, I = cfg->weights.intermediate, E = cfg->weights.routed_experts;
+    const int Is = cfg->weights.shared_intermediate > 0 ? cfg->weights.shared_intermediate : I;
+    if (fmt.routed_format < 0 || fmt.routed_format > 2) return nullptr;
+    if (fmt.shared_format != MOE_B200_W8_PER_CHANNEL && fmt.shared_format != MOE_B200_W4_PER_CHANNEL)
+        return nullptr;
+    if (cfg->weights.shared_expert && fmt.shared_mode == MOE_B200_SHARED_JOINT && Is != I)
+        return nullptr;  // joint bank needs the routed intermediate (src/npu/moe.rs:230-233)
+    for (int e = 0; e < E + (cfg->weights.shared_expert ? 1 : 0); ++e) {
+        const moe_b200_expert& x = experts[e];
+        const int f = e < E ? fmt.routed_format : fmt.shared_format;
+        if (!x.gate_up || !x.down) return nullptr;
+        if (f == MOE_B200_W4_G32_FP16 && (!x.gate_up_group_scales || !x.down_group_scales))
+            return nullptr;
+        if (f != MOE_B200_W4_G32_FP16 && (!x.gate_up_scales || !x.down_scales)) return nullptr;
+    }
+
+    auto* w = new moe_b200_weights();
+    w->device = cfg->device;
+    w->H = H;
+    w->I = I;
+    w->E = E;
+    w->top = cfg->top;
+    w->shared = cfg->weights.shared_expert;
+    w->Is = Is;
+    w->shared_mode = fmt.shared_mode;
+    setup_mat(w->gu, fmt.routed_format, E, H, I, true);
+    setup_mat(w->dn, fmt.routed_format, E, I, H, false);
+    if (w->shared) {
+        setup_mat(w->sgu, fmt.shared_format, 1, H, Is, true);
+        setup_mat(w->sdn, fmt.shared_format, 1, Is, H, false);
+    }
+    bool ok = true;
+    auto build = [&](PackedMat& m, int first, int count) {
+        const size_t wb = m.w_expert_stride * count, sb = m.s_expert_stride * count;
+        std::vector<uint8_t> hw(wb, 0), hs(sb, 0);
+        for (int e = 0; e < count; ++e) {
+            const moe_b200_expert& x = experts[first + e];
+            const bool is_gu = m.swiglu;
+            pack_expert(m, is_gu ? x.gate_up : x.down, is_gu ? x.gate_up_scales : x.down_scales,
+                        is_gu ? x.gate_up_group_scales : x.down_group_scales,
+                        hw.data() + m.w_expert_stride * e, hs.data() + m.s_expert_stride * e);
+        }
+        void *dw = nullptr, *ds = nullptr;
+        if (dev_alloc(&dw, wb) != cudaSuccess) { ok = false; return; }
+        if (dev_alloc(&ds, sb) != cudaSuccess) { cudaFree(dw); ok = false; return; }
+        m.w = static_cast<uint8_t*>(dw);
+        m.s = ds;
+        if (cudaMemcpy(dw, hw.data(), wb, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(ds, hs.data(), sb, cudaMemcpyHostToDevice) != cudaSuccess)
+            ok = false;
+        w->bytes += wb + sb;
+    };
+    build(w->gu, 0, E);
+    if (ok) build(w->dn, 0, E);
+    if (ok && w->shared) build(w->sgu, E, 1);
+    if (ok && w->shared) build(w->sdn, E, 1);
+    if (!ok) {
+        moe_b200_weights_free(w);
+        return nullptr;
+    }
+    return w;
+}
+
+void moe_b200_weights_free(moe_b200_weights* w) {
+    if (!w) return;
+    DeviceGuard guard(w->device);
+    for (PackedMat* m : {&w->gu, &w->dn, &w->sgu, &w->sdn}) {
+        if (m->w) cudaFree(m->w);
+        if (m->s) cudaFree(m->s);
+    }
+    delete w;
+}
+
+uint64_t moe_b200_weights_device_bytes(const moe_b200_weights* w) { return w ? w->bytes : 0; }
+
+moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
+    if (validate_config(cfg)) return nullptr;
+    int sms = 0;
+    if (check_device(cfg->device, &sms)) return nullptr;
+    DeviceGuard guard(cfg->device);
+    auto* ws = new moe_b200_workspace();
+    ws->device = cfg->device;
+    ws->H = cfg->weights.hidden;
+    ws->I = cfg->weights.intermediate;
+    ws->E = cfg->weights.routed_experts;
+    ws->k = cfg->top;
+    ws->max_rows = cfg->max_rows;
+    ws->Is = cfg->weights.shared_expert
+                 ? (cfg->weights.shared_intermediate > 0 ? cfg->weights.shared_intermediate : ws->I)
+                 : 0;
+    ws->num_sms = sms;
+    ws->Kh = pad_to(ws->H, 128);
+    ws->Ki = pad_to(ws->I, 128);
+    ws->Kis = pad_to(ws->Is > 0 ? ws->Is : 32, 128);
+    const long T = ws->max_rows, n = T * ws->k;
+    ws->n_max = n;
+    const long nb = (n + kRouteChunk - 1) / kRouteChunk;
+    const long pad_rows = 64;  // tiles may read past the last row
+    int rc = MOE_B200_OK;
+    rc |= ws_alloc(ws, &ws->x, T * ws->H);
+    rc |= ws_alloc(ws, &ws->out, T * ws->H);
+    rc |= ws_alloc(ws, &ws->res, T * ws->H);
+    rc |= ws_alloc(ws, &ws->routes, n);
+    rc |= ws_alloc(ws, &ws->ids, n);
+    rc |= ws_alloc(ws, &ws->q_x, (T + pad_rows) * ws->Kh);
+    rc |= ws_alloc(ws, &ws->s_x, T);
+    rc |= ws_alloc(ws, &ws->hist, (nb > 0 ? nb : 1) * ws->E);
+    rc |= ws_alloc(ws, &ws->offsets, ws->E + 1);
+    rc |= ws_alloc(ws, &ws->perm, n);
+    rc |= ws_alloc(ws, &ws->pos, n);
+    rc |= ws_alloc(ws, &ws->shared_offsets, 2);
+    rc |= ws_alloc(ws, &ws->counters, T);
+    rc |= ws_alloc(ws, &ws->a_perm, (n + pad_rows) * ws->Kh);
+    rc |= ws_alloc(ws, &ws->s_perm, n);
+    rc |= ws_alloc(ws, &ws->middle, n * ws->I);
+    rc |= ws_alloc(ws, &ws->rowmax, n);
+    rc |= ws_alloc(ws, &ws->q_m, (n + pad_rows) * ws->Ki);
+    rc |= ws_alloc(ws, &ws->s_m, n);
+    rc |= ws_alloc(ws, &ws->y, n * ws->H);
+    rc |= ws_alloc(ws, &ws->logits, T * ws->E);
+    rc |= ws_alloc(ws, &ws->err, 1);
+    if (ws->Is > 0 && rc == MOE_B200_OK) {
+        rc |= ws_alloc(ws, &ws->q_xd, (T + pad_rows) * ws->Kh);
+        rc |= ws_alloc(ws, &ws->s_xd, T);
+        rc |= ws_alloc(ws, &ws->s_middle, T * ws->Is);
+        rc |= ws_alloc(ws, &ws->s_rowmax, T);
+        rc |= ws_alloc(ws, &ws->sq_m, (T + pad_rows) * ws->Kis);
+        rc |= ws_alloc(ws, &ws->ss_m, T);
+        rc |= ws_alloc(ws, &ws->s_y, T * ws->H);
+    }
+    if (rc != MOE_B200_OK) {
+        moe_b200_workspace_free(ws);
+        return nullptr;
+    }
+    cudaMemset(ws->counters, 0, sizeof(int) * T);
+    cudaMemset(ws->err, 0, sizeof(uint32_t));
+    cudaMemset(ws->a_perm, 0, (size_t)(n + pad_rows) * ws->Kh);
+    cudaMemset(ws->q_m, 0, (size_t)(n + pad_rows) * ws->Ki);
+    cudaMemset(ws->q_x, 0, (size_t)(T + pad_rows) * ws->Kh);
+    for (int i = 0; i < 3 && rc == MOE_B200_OK; ++i) {
+        const int nt = kNTs[i];
+        rc |= make_act_map(&ws->map_a[i], ws->a_perm, (int)(n + pad_rows), ws->Kh, nt);
+        rc |= make_act_map(&ws->map_qm[i], ws->q_m, (int)(n + pad_rows), ws->Ki, nt);
+        rc |= make_act_map(&ws->map_qx[i], ws->q_x, (int)(T + pad_rows), ws->Kh, nt);
+        if (ws->Is > 0) {
+            rc |= make_act_map(&ws->map_qxd[i], ws->q_xd, (int)(T + pad_rows), ws->Kh, nt);
+            rc |= make_act_map(&ws->map_sqm[i], ws->sq_m, (int)(T + pad_rows), ws->Kis, nt);
+        }
+    }
+    if (rc == MOE_B200_OK && cudaStreamCreateWithFlags(&ws->own_stream, cudaStreamNonBlocking) != cudaSuccess)
+        rc = MOE_B200_ERR_CUDA;
+    for (int i = 0; i < 12 && rc == MOE_B200_OK; ++i)
+        if (cudaEventCreate(&ws->ev[i]) != cudaSuccess) rc = MOE_B200_ERR_CUDA;
+    if (rc != MOE_B200_OK || cudaDeviceSynchronize() != cudaSuccess) {
+        moe_b200_workspace_free(ws);
+        return nullptr;
+    }
+    return ws;
+}
+
+void moe_b200_workspace_free(moe_b200_workspace* ws) {
+    if (!ws) return;
+    DeviceGuard guard(ws->device);
+    if (ws->own_stream) cudaStreamSynchronize(ws->own_stream);
+    for (void* p : ws->allocs) cudaFree(p);
+    for (int i = 0; i < 12; ++i)
+        if (ws->ev[i]) cudaEventDestroy(ws->ev[i]);
+    for (cudaEvent_t e : ws->prof_ev) cudaEventDestroy(e);
+    if (ws->own_stream) cudaStreamDestroy(ws->own_stream);
+    delete ws;
+}
+
+uint64_t moe_b200_workspace_device_bytes(const moe_b200_workspace* ws) { return ws ? ws->bytes : 0; }
+
+int32_t moe_b200_max_rows(const moe_b200_workspace* ws) { return ws ? ws->max_rows : 0; }
+
+int moe_b200_run_device(moe_b200_workspace* ws, const moe_b200_weights* w, int32_t rows,
+                        const float* d_input, const int32_t* d_ids, const float* d_routes,
+                        float* d_output, void* stream) {
+    int rc = compatible(ws, w);
+    if (rc) return rc;
+    if (rows < 0) return MOE_B200_ERR_INVALID;
+    if (rows > ws->max_rows) return MOE_B200_ERR_CAPACITY;
+    if (rows == 0) return MOE_B200_OK;
+    if (!d_input || !d_ids || !d_routes || !d_output) return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ws->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaEvent_t* evs = prof_slot(ws, w->shared ? 2 : 0);
+    if (evs) {
+        cudaEventRecord(evs[0], s);
+        cudaEventRecord(evs[1], s);
+    }
+    return run_pipeline(ws, w, rows, d_input, d_ids, d_routes, nullptr, d_output, s, evs);
+}
+
+int moe_b200_run_f32(moe_b200_workspace* ws, const moe_b200_weights* w, int32_t rows,
+                     const float* input, const int32_t* ids, const float* routes, float* output,
+                     moe_b200_timings* timings) {
+    int rc = compatible(ws, w);
+    if (rc) return rc;
+    if (rows < 0) return MOE_B200_ERR_INVALID;
+    if (rows > ws->max_rows) return MOE_B200_ERR_CAPACITY;
+    if (rows == 0) return MOE_B200_OK;
+    if (!input || !ids || !routes || !output) return MOE_B200_ERR_INVALID;
+    rc = validate_host_routes(ws, rows, ids, routes);
+    if (rc) return rc;
+    DeviceGuard guard(ws->device);
+    cudaStream_t s = ws->own_stream;
+    const size_t xb = sizeof(float) * (size_t)rows * ws->H, nb = (size_t)rows * ws->k;
+    if (timings) cudaEventRecord(ws->ev[0], s);
+    cudaMemcpyAsync(ws->x, input, xb, cudaMemcpyHostToDevice, s);
+    cudaMemcpyAsync(ws->ids, ids, sizeof(int32_t) * nb, cudaMemcpyHostToDevice, s);
+    cudaMemcpyAsync(ws->routes, routes, sizeof(float) * nb, cudaMemcpyHostToDevice, s);
+    rc = run_pipeline(ws, w, rows, ws->x, ws->ids, ws->routes, nullptr, ws->out, s,
+                      timings ? ws->ev : nullptr);
+    if (rc) return rc;
+    cudaMemcpyAsync(output, ws->out, xb, cudaMemcpyDeviceToHost, s);
+    if (timings) cudaEventRecord(ws->ev[9], s);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_rc(e);
+    rc = read_status(ws, s);
+    if (timings) {
+        fill_timings(ws, timings, rows, false, w->shared != 0);
+        timings->sync_us = 1000.0 * ev_ms(ws->ev[8], ws->ev[9]);
+        timings->total_us = 1000.0 * ev_ms(ws->ev[0], ws->ev[9]);
+    }
+    return rc;
+}
+
+moe_b200_router* moe_b200_router_create(const moe_b200_config* cfg, const float* router,
+                                        const float* bias, int32_t order, float min_weight) {
+    if (validate_config(cfg) || !router) return nullptr;
+    if (order != MOE_B200_ROUTER_NEON16 && order != MOE_B200_ROUTER_SEQUENTIAL) return nullptr;
+    if (!(min_weight >= 0.0f && min_weight <= 1.0f)) return nullptr;  // pruning::validate
+    if (check_device(cfg->device, nullptr)) return nullptr;
+    DeviceGuard guard(cfg->device);
+    auto* r = new moe_b200_router();
+    r->device = cfg->device;
+    r->H = cfg->weights.hidden;
+    r->E = cfg->weights.routed_experts;
+    r->order = order;
+    r->min_weight = min_weight;
+    const size_t wb = sizeof(float) * (size_t)r->H * r->E;
+    void* p = nullptr;
+    if (dev_alloc(&p, wb) != cudaSuccess) { delete r; return nullptr; }
+    r->w = static_cast<float*>(p);
+    cudaMemcpy(r->w, router, wb, cudaMemcpyHostToDevice);
+    if (bias) {
+        if (dev_alloc(&p, sizeof(float) * r->E) != cudaSuccess) {
+            moe_b200_router_free(r);
+            return nullptr;
+        }
+        r->bias = static_cast<float*>(p);
+        cudaMemcpy(r->bias, bias, sizeof(float) * r->E, cudaMemcpyHostToDevice);
+    }
+    return r;
+}
+
+void moe_b200_router_free(moe_b200_router* r) {
+    if (!r) return;
+    DeviceGuard guard(r->device);
+    if (r->w) cudaFree(r->w);
+    if (r->bias) cudaFree(r->bias);
+    delete r;
+}
+
+static int route_impl(moe_b200_workspace* ws, const moe_b200_router* r, int rows, const float* d_x,
+                      float* d_logits, int32_t* d_ids, float* d_routes, cudaStream_t s) {
+    RouterArgs a{};
+    a.x = d_x;
+    a.w = r->w;
+    a.bias = r->bias;
+    a.T = rows;
+    a.H = r->H;
+    a.E = r->E;
+    a.k = ws->k;
+    a.order = r->order;
+    a.min_weight = r->min_weight;
+    a.logits = d_logits ? d_logits : ws->logits;
+    a.counters = ws->counters;
+    a.ids = d_ids;
+    a.weights = d_routes;
+    a.err = ws->err;
+    launch_router(a, s);
+    ws->launches += r->order == MOE_B200_ROUTER_SEQUENTIAL ? 2 : 1;
+    return cuda_rc(cudaPeekAtLastError());
+}
+
+int moe_b200_route_device(moe_b200_workspace* ws, const moe_b200_router* r, int32_t rows,
+                          const float* d_input, float* d_logits, int32_t* d_ids, float* d_routes,
+                          void* stream) {
+    if (!ws || !r || r->H != ws->H || r->E != ws->E || r->device != ws->device)
+        return MOE_B200_ERR_INVALID;
+    if (rows < 0) return MOE_B200_ERR_INVALID;
+    if (rows > ws->max_rows) return MOE_B200_ERR_CAPACITY;
+    if (rows == 0) return MOE_B200_OK;
+    DeviceGuard guard(ws->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    ws->last_stream = s;
+    return route_impl(ws, r, rows, d_input, d_logits, d_ids, d_routes, s);
+}
+
+int moe_b200_forward_device(moe_b200_workspace* ws, const moe_b200_weights* w,
+                            const moe_b200_router* r, int32_t rows, const float* d_input,
+                            const float* d_residual, float* d_output, void* stream) {
+    int rc = compatible(ws, w);
+    if (rc) return rc;
+    if (!r || r->H != ws->H || r->E != ws->E) return MOE_B200_ERR_INVALID;
+    if (rows < 0) return MOE_B200_ERR_INVALID;
+    if (rows > ws->max_rows) return MOE_B200_ERR_CAPACITY;
+    if (rows == 0) return MOE_B200_OK;
+    DeviceGuard guard(ws->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaEvent_t* evs = prof_slot(ws, 1 | (w->shared ? 2 : 0));
+    if (evs) cudaEventRecord(evs[0], s);
+    rc = route_impl(ws, r, rows, d_input, nullptr, ws->ids, ws->routes, s);
+    if (rc) return rc;
+    return run_pipeline(ws, w, rows, d_input, ws->ids, ws->routes, d_residual, d_output, s, evs);
+}
+
+int moe_b200_forward_f32(moe_b200_workspace* ws, const moe_b200_weights* w,
+                         const moe_b200_router* r, int32_t rows, const float* input,
+                         const float* residual, float* output, int32_t* ids, float* routes,
+                         moe_b200_timings* timings) {
+    int rc = compatible(ws, w);
+    if (rc) return rc;
+    if (!r || r->H != ws->H || r->E != ws->E) return MOE_B200_ERR_INVALID;
+    if (rows < 0) return MOE_B200_ERR_INVALID;
+    if (rows > ws->max_rows) return MOE_B200_ERR_CAPACITY;
+    if (rows == 0) return MOE_B200_OK;
+    if (!input || !output) return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ws->device);
+    cudaStream_t s = ws->own_stream;
+    const size_t xb = sizeof(float) * (size_t)rows * ws->H, nb = (size_t)rows * ws->k;
+    if (timings) cudaEventRecord(ws->ev[10], s);
+    cudaMemcpyAsync(ws->x, input, xb, cudaMemcpyHostToDevice, s);
+    if (residual) cudaMemcpyAsync(ws->res, residual, xb, cudaMemcpyHostToDevice, s);
+    if (timings) cudaEventRecord(ws->ev[0], s);
+    rc = route_impl(ws, r, rows, ws->x, nullptr, ws->ids, ws->routes, s);
+    if (rc) return rc;
+    rc = run_pipeline(ws, w, rows, ws->x, ws->ids, ws->routes, residual ? ws->res : nullptr,
+                      ws->out, s, timings ? ws->ev : nullptr);
+    if (rc) return rc;
+    cudaMemcpyAsync(output, ws->out, xb, cudaMemcpyDeviceToHost, s);
+    if (ids) cudaMemcpyAsync(ids, ws->ids, sizeof(int32_t) * nb, cudaMemcpyDeviceToHost, s);
+    if (routes) cudaMemcpyAsync(routes, ws->routes, sizeof(float) * nb, cudaMemcpyDeviceToHost, s);
+    if (timings) cudaEventRecord(ws->ev[9], s);
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_rc(e);
+    rc = read_status(ws, s);
+    if (timings) {
+        fill_timings(ws, timings, rows, true, w->shared != 0);
+        timings->sync_us = 1000.0 * ev_ms(ws->ev[8], ws->ev[9]);
+        timings->total_us = 1000.0 * ev_ms(ws->ev[10], ws->ev[9]);
+    }
+    return rc;
+}
+
+int moe_b200_workspace_status(moe_b200_workspace* ws) {
+    if (!ws) return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ws->device);
+    cudaStream_t s = ws->last_stream ? ws->last_stream : ws->own_stream;
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_rc(e);
+    return read_status(ws, ws->own_stream);
+}
+
+int moe_b200_workspace_buffer(moe_b200_workspace* ws, const char* name, void** d_ptr,
+                              uint64_t* bytes) {
+    if (!ws || !name || !d_ptr) return MOE_B200_ERR_INVALID;
+    const long T = ws->max_rows, n = ws->n_max;
+    struct Entry {
+        const char* name;
+        void* p;
+        uint64_t b;
+    } table[] = {
+        {"q_x", ws->q_x, (uint64_t)T * ws->Kh},
+        {"s_x", ws->s_x, sizeof(float) * (uint64_t)T},
+        {"perm", ws->perm, sizeof(int32_t) * (uint64_t)n},
+        {"pos", ws->pos, sizeof(int32_t) * (uint64_t)n},
+        {"offsets", ws->offsets, sizeof(int32_t) * (uint64_t)(ws->E + 1)},
+        {"a_perm", ws->a_perm, (uint64_t)n * ws->Kh},
+        {"s_perm", ws->s_perm, sizeof(float) * (uint64_t)n},
+        {"middle", ws->middle, sizeof(float) * (uint64_t)n * ws->I},
+        {"rowmax", ws->rowmax, sizeof(uint32_t) * (uint64_t)n},
+        {"q_m", ws->q_m, (uint64_t)n * ws->Ki},
+        {"s_m", ws->s_m, sizeof(float) * (uint64_t)n},
+        {"y", ws->y, sizeof(float) * (uint64_t)n * ws->H},
+        {"shared_y", ws->s_y, ws->s_y ? sizeof(float) * (uint64_t)T * ws->H : 0},
+        {"logits", ws->logits, sizeof(float) * (uint64_t)T * ws->E},
+        {"ids", ws->ids, sizeof(int32_t) * (uint64_t)n},
+        {"routes", ws->routes, sizeof(float) * (uint64_t)n},
+    };
+    for (const Entry& e : table)
+        if (strcmp(e.name, name) == 0) {
+            if (!e.p) return MOE_B200_ERR_INVALID;
+            *d_ptr = e.p;
+            if (bytes) *bytes = e.b;
+            return MOE_B200_OK;
+        }
+    return MOE_B200_ERR_INVALID;
+}
+
+int moe_b200_debug_accumulators(moe_b200_workspace* ws, const moe_b200_weights* w, int32_t which,
+                                int32_t* d_acc, uint64_t capacity_elems, void* stream) {
+    int rc = compatible(ws, w);
+    if (rc) return rc;
+    if (!d_acc || (which != 0 && which != 1) || ws->last_w != w || ws->last_rows <= 0)
+        return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ws->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const PackedMat& m = which == 0 ? w->gu : w->dn;
+    const long n = (long)ws->last_rows * ws->k;
+    const int G = m.fmt == kFmtW4G32 ? m.kblocks * 4 : 1;
+    const int ld = which == 0 ? 2 * w->I : w->H;
+    if ((uint64_t)n * G * ld > capacity_elems) return MOE_B200_ERR_CAPACITY;
+    cudaMemsetAsync(d_acc, 0, sizeof(int32_t) * (size_t)n * G * ld, s);
+    const int nt = which == 0 ? ws->last_nt_gu : ws->last_nt_dn;
+    GemmArgs a = which == 0 ? gemm_args(ws, m, ws->s_perm, ws->offsets, ws->E, n, nullptr, 0, nullptr)
+                            : gemm_args(ws, m, ws->s_m, ws->offsets, ws->E, n, nullptr, 0, nullptr);
+    a.acc_out = d_acc;
+    a.acc_ld = ld;
+    a.n_valid = which == 0 ? w->I : w->H;
+    const CUtensorMap& map = which == 0 ? ws->map_a[nt_index(nt)] : ws->map_qm[nt_index(nt)];
+    if (launch_gemm(map, a, m.fmt, kEpiAcc, nt, ws->num_sms, s)) return MOE_B200_ERR_UNSUPPORTED;
+    return cuda_rc(cudaPeekAtLastError());
+}
+
+int moe_b200_workspace_profile(moe_b200_workspace* ws, int32_t enable) {
+    if (!ws) return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ws->device);
+    if (enable && ws->prof_ev.empty()) {
+        const size_t n = (size_t)moe_b200_workspace::kProfSlots * moe_b200_workspace::kProfEvents;
+        ws->prof_ev.resize(n, nullptr);
+        for (size_t i = 0; i < n; ++i)
+            if (cudaEventCreate(&ws->prof_ev[i]) != cudaSuccess) return MOE_B200_ERR_CUDA;
+        ws->prof_flags.assign(moe_b200_workspace::kProfSlots, 0);
+    }
+    ws->profiling = enable != 0;
+    ws->prof_calls = 0;
+    return MOE_B200_OK;
+}
+
+int moe_b200_workspace_profile_read(moe_b200_workspace* ws, int32_t call, moe_b200_timings* t) {
+    if (!ws || !t || ws->prof_ev.empty() || call < 0 || call >= ws->prof_calls ||
+        call < ws->prof_calls - moe_b200_workspace::kProfSlots)
+        return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ws->device);
+    const int slot = call % moe_b200_workspace::kProfSlots;
+    const cudaEvent_t* ev = &ws->prof_ev[(size_t)slot * moe_b200_workspace::kProfEvents];
+    cudaError_t e = cudaEventSynchronize(ev[8]);
+    if (e != cudaSuccess) return cuda_rc(e);
+    const int fl = ws->prof_flags[slot];
+    fill_timings_from(ev, ws, t, ws->last_rows, (fl & 1) != 0, (fl & 2) != 0);
+    return MOE_B200_OK;
+}
+
+int64_t moe_b200_workspace_launches(const moe_b200_workspace* ws) { return ws ? ws->launches : 0; }
+
+const char* moe_b200_strerror(int code) {
+    switch (code) {
+        case MOE_B200_OK: return "success";
+        case MOE_B200_ERR_INVALID: return "invalid argument or shape";
+        case MOE_B200_ERR_UNSUPPORTED: return "shape or format not supported by this build";
+        case MOE_B200_ERR_NOMEM: return "device memory allocation failed";
+        case MOE_B200_ERR_CUDA: return "CUDA runtime error";
+        case MOE_B200_ERR_CAPACITY: return "rows exceed the workspace max_rows";
+        case MOE_B200_ERR_DEVICE_TIMEOUT: return "a bounded device wait timed out";
+        case MOE_B200_ERR_BAD_EXPERT: return "expert id out of range";
+        case MOE_B200_ERR_NONFINITE: return "non-finite router logit or activation";
+        case MOE_B200_ERR_BAD_ROUTE: return "negative or NaN routing weight";
+        case MOE_B200_ERR_NO_DEVICE: return "no sm_100 CUDA device available";
+        default: return "unknown error";
+    }
+}
+
+const char* moe_b200_version(void) { return "moe_b200 0.1.0 sm_100a"; }
+
+}  // extern "C"

@@ -1,0 +1,299 @@
+// Token dispatch and the element-wise stages around the expert GEMMs:
+//   route_count / route_scatter : stable grouping of assignments by expert
+//   quant_gather                : dynamic per-token int8 quantisation, written
+//                                 straight into the permuted GEMM operand
+//   requant                     : SwiGLU middle -> int8 for the down GEMM
+//   combine                     : routing-weighted sum (+ shared, + residual)
+//
+// Reference semantics (happyme531/open_rknpu2_lm_infer):
+//   grouping   : assignment order t*k+r inside an expert group, zero routes
+//                skipped (src/model/experts/paged.rs:586-600)
+//   quantise   : MoE rule s = maxabs/127, round-half-even, zero row -> s = 1
+//                (llm_generated_docs/MOE_CPU_FUSION_20261023.md:13); dense rule
+//                s = max(maxabs/127, FLT_MIN), round-half-away of x * (1/s)
+//                (llm_generated_docs/MODELS.md:26)
+//   combine    : out = sum_r fma(y, w_r, out) over ranks with w > 0
+//                (src/model/experts/paged.rs:495-506), then + shared
+//                (src/model/ling3tiny/moe.rs:378-388), then residual + out
+//                (src/model/qwen35/decoder.rs:215-217)
+#include <float.h>
+
+#include "kernels.cuh"
+
+namespace moe {
+
+__device__ __forceinline__ bool route_kept(float w) { return w > 0.0f; }
+
+__global__ void route_count_kernel(const int32_t* __restrict__ ids, const float* __restrict__ routes,
+                                   int n, int E, int32_t* hist, uint32_t* err) {
+    extern __shared__ int32_t hist_s[];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) hist_s[e] = 0;
+    __syncthreads();
+    const int a0 = blockIdx.x * kRouteChunk;
+    const int a1 = min(n, a0 + kRouteChunk);
+    for (int a = a0 + threadIdx.x; a < a1; a += blockDim.x) {
+        const float w = routes[a];
+        if (!(w >= 0.0f)) atomicOr(err, kErrBadRoute);  // negative or NaN
+        if (!route_kept(w)) continue;
+        const int e = ids[a];
+        if (e < 0 || e >= E) {
+            atomicOr(err, kErrBadExpert);
+            continue;
+        }
+        atomicAdd(&hist_s[e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[(size_t)blockIdx.x * E + e] = hist_s[e];
+}
+
+// 256 threads. smem: off[E+1], base[E], wcnt[8][E].
+__global__ void __launch_bounds__(256)
+route_scatter_kernel(const int32_t* __restrict__ ids, const float* __restrict__ routes, int n,
+                     int E, const int32_t* __restrict__ hist, int32_t* offsets, int32_t* perm,
+                     int32_t* pos, int32_t* shared_offsets, int T) {
+    extern __shared__ int32_t sm[];
+    int32_t* off_s = sm;               // E+1
+    int32_t* base_s = off_s + E + 1;   // E
+    int32_t* wcnt = base_s + E;        // 8*E
+    const int nb = gridDim.x, b = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int tot = 0, pre = 0;
+        for (int bb = 0; bb < nb; ++bb) {
+            const int h = hist[(size_t)bb * E + e];
+            tot += h;
+            if (bb < b) pre += h;
+        }
+        off_s[e] = tot;  // scanned below
+        base_s[e] = pre;
+    }
+    for (int i = threadIdx.x; i < 8 * E; i += blockDim.x) wcnt[i] = 0;
+    __syncthreads();
+    if (warp == 0) {  // exclusive scan of the expert totals
+        const int per = (E + 31) / 32;
+        int local = 0;
+        for (int i = 0; i < per; ++i) {
+            const int e = lane * per + i;
+            if (e < E) local += off_s[e];
+        }
+        int incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int run = incl - local;
+        for (int i = 0; i < per; ++i) {
+            const int e = lane * per + i;
+            if (e < E) {
+                const int c = off_s[e];
+                off_s[e] = run;
+                run += c;
+            }
+        }
+        if (lane == 31) off_s[E] = incl;
+    }
+    __syncthreads();
+    if (b == 0) {
+        for (int e = threadIdx.x; e <= E; e += blockDim.x) offsets[e] = off_s[e];
+        if (shared_offsets && threadIdx.x == 0) {
+            shared_offsets[0] = 0;
+            shared_offsets[1] = T;
+        }
+    }
+    const int a0 = b * kRouteChunk;
+    const int a1 = min(n, a0 + kRouteChunk);
+    const unsigned lt = (1u << lane) - 1u;
+    for (int r0 = a0; r0 < a1; r0 += blockDim.x) {
+        const int a = r0 + threadIdx.x;
+        int e = -1;
+        if (a < a1) {
+            const float w = routes[a];
+            const int id = ids[a];
+            if (route_kept(w) && id >= 0 && id < E) e = id;
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const int rank_w = __popc(peers & lt);
+        if (e >= 0 && rank_w == 0) wcnt[warp * E + e] = __popc(peers);
+        __syncthreads();
+        if (a < a1) {
+            if (e >= 0) {
+                int before = 0;
+                for (int w2 = 0; w2 < warp; ++w2) before += wcnt[w2 * E + e];
+                const int p = off_s[e] + base_s[e] + before + rank_w;
+                perm[p] = a;
+                pos[a] = p;
+            } else {
+                pos[a] = -1;
+            }
+        }
+        __syncthreads();
+        for (int ee = threadIdx.x; ee < E; ee += blockDim.x) {
+            int s = 0;
+            for (int w2 = 0; w2 < 8; ++w2) {
+                s += wcnt[w2 * E + ee];
+                wcnt[w2 * E + ee] = 0;
+            }
+            base_s[ee] += s;
+        }
+        __syncthreads();
+    }
+}
+
+__device__ __forceinline__ int quant_one(float x, float s, float inv, int rule) {
+    float v = rule == kQuantMoe ? __fdiv_rn(x, s) : roundf(__fmul_rn(x, inv));
+    int q = rule == kQuantMoe ? __float2int_rn(v) : (int)v;
+    return q > 127 ? 127 : (q < -127 ? -127 : q);
+}
+
+__device__ __forceinline__ float block_max_256(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float m = red[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+    __syncthreads();
+    return m;
+}
+
+__device__ __forceinline__ float row_scale(float m, int rule) {
+    if (m == 0.0f) return 1.0f;
+    float s = __fdiv_rn(m, 127.0f);
+    if (rule == kQuantDense && !(s >= FLT_MIN)) s = FLT_MIN;
+    return s;
+}
+
+// One CTA per token: quantise the row once, write it to q_rows[t] (if given)
+// and to every kept permuted slot pos[t*k + r] (if pos given).
+__global__ void __launch_bounds__(256)
+quant_gather_kernel(const float* __restrict__ x, int H, int ld_q, int rule, int k,
+                    const int32_t* __restrict__ pos, int8_t* q_rows, float* s_rows,
+                    int8_t* q_perm, float* s_perm, uint32_t* err) {
+    __shared__ float red[8];
+    __shared__ int slots[32];
+    const int t = blockIdx.x;
+    const float* xr = x + (size_t)t * H;
+    float m = 0.0f;
+    for (int c = threadIdx.x; c < H; c += blockDim.x) {
+        const float a = fabsf(xr[c]);
+        if (a > m) m = a;
+    }
+    m = block_max_256(m, red);
+    const float s = row_scale(m, rule);
+    const float inv = __fdiv_rn(1.0f, s);
+    if (!isfinite(s) && threadIdx.x == 0) atomicOr(err, kErrNonFinite);
+    __shared__ int nslot_s;
+    if (threadIdx.x == 0) {
+        int ns = 0;
+        if (pos)
+            for (int r = 0; r < k && r < 32; ++r) {
+                const int p = pos[(size_t)t * k + r];
+                if (p >= 0) slots[ns++] = p;
+            }
+        nslot_s = ns;
+        if (s_rows) s_rows[t] = s;
+        for (int i = 0; i < ns; ++i) s_perm[slots[i]] = s;
+    }
+    __syncthreads();
+    const int nslot = nslot_s;
+    // 4 columns per step -> one 32-bit store per destination
+    for (int c4 = threadIdx.x * 4; c4 < ld_q; c4 += blockDim.x * 4) {
+        uint32_t packed = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int c = c4 + i;
+            const int q = c < H ? quant_one(xr[c], s, inv, rule) : 0;
+            packed |= (uint32_t)(q & 0xFF) << (8 * i);
+        }
+        if (q_rows) *reinterpret_cast<uint32_t*>(q_rows + (size_t)t * ld_q + c4) = packed;
+        for (int i = 0; i < nslot; ++i)
+            *reinterpret_cast<uint32_t*>(q_perm + (size_t)slots[i] * ld_q + c4) = packed;
+    }
+}
+
+// One CTA per permuted row; rows >= *count exit. Scale from the row max that
+// the gate/up epilogue accumulated.
+__global__ void __launch_bounds__(128)
+requant_kernel(const float* __restrict__ mid, const uint32_t* __restrict__ rowmax,
+               const int32_t* __restrict__ count, int I, int ld_q, int rule, int8_t* q,
+               float* sc) {
+    const int row = blockIdx.x;
+    if (row >= *count) return;
+    const float m = __uint_as_float(rowmax[row]);
+    const float s = row_scale(m, rule);
+    const float inv = __fdiv_rn(1.0f, s);
+    if (threadIdx.x == 0) sc[row] = s;
+    const float* mr = mid + (size_t)row * I;
+    for (int c4 = threadIdx.x * 4; c4 < ld_q; c4 += blockDim.x * 4) {
+        uint32_t packed = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int c = c4 + i;
+            const int qv = c < I ? quant_one(mr[c], s, inv, rule) : 0;
+            packed |= (uint32_t)(qv & 0xFF) << (8 * i);
+        }
+        *reinterpret_cast<uint32_t*>(q + (size_t)row * ld_q + c4) = packed;
+    }
+}
+
+__global__ void __launch_bounds__(256)
+combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ pos,
+               const float* __restrict__ routes, const float* __restrict__ shared,
+               const float* __restrict__ residual, int H, int k, float* out) {
+    const int t = blockIdx.x;
+    for (int c = threadIdx.x; c < H; c += blockDim.x) {
+        float acc = 0.0f;
+        for (int r = 0; r < k; ++r) {
+            const size_t a = (size_t)t * k + r;
+            const float w = routes[a];
+            if (route_kept(w)) acc = __fmaf_rn(y[(size_t)pos[a] * H + c], w, acc);
+        }
+        if (shared) acc = __fadd_rn(acc, shared[(size_t)t * H + c]);
+        if (residual) acc = __fadd_rn(residual[(size_t)t * H + c], acc);
+        out[(size_t)t * H + c] = acc;
+    }
+}
+
+void launch_route_count(const int32_t* ids, const float* routes, int n, int E, int32_t* hist,
+                        uint32_t* err, cudaStream_t s) {
+    const int nb = (n + kRouteChunk - 1) / kRouteChunk;
+    if (nb == 0) return;
+    route_count_kernel<<<nb, 256, sizeof(int32_t) * E, s>>>(ids, routes, n, E, hist, err);
+}
+
+void launch_route_scatter(const int32_t* ids, const float* routes, int n, int E,
+                          const int32_t* hist, int32_t* offsets, int32_t* perm, int32_t* pos,
+                          int32_t* shared_offsets, int T, cudaStream_t s) {
+    const int nb = (n + kRouteChunk - 1) / kRouteChunk;
+    const size_t smem = sizeof(int32_t) * (size_t)(E + 1 + E + 8 * E);
+    if (smem > 48 * 1024)
+        cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    route_scatter_kernel<<<nb > 0 ? nb : 1, 256, smem, s>>>(ids, routes, n, E, hist, offsets,
+                                                            perm, pos, shared_offsets, T);
+}
+
+void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k,
+                         const int32_t* pos, int8_t* q_rows, float* s_rows, int8_t* q_perm,
+                         float* s_perm, uint32_t* err, cudaStream_t s) {
+    if (T == 0) return;
+    quant_gather_kernel<<<T, 256, 0, s>>>(x, H, ld_q, rule, k, pos, q_rows, s_rows, q_perm,
+                                          s_perm, err);
+}
+
+void launch_requant(const float* mid, const uint32_t* rowmax, const int32_t* count,
+                    int max_rows, int I, int ld_q, int rule, int8_t* q, float* sc,
+                    cudaStream_t s) {
+    if (max_rows == 0) return;
+    requant_kernel<<<max_rows, 128, 0, s>>>(mid, rowmax, count, I, ld_q, rule, q, sc);
+}
+
+void launch_combine(const float* y, const int32_t* pos, const float* routes, const float* shared,
+                    const float* residual, int T, int H, int k, float* out, cudaStream_t s) {
+    if (T == 0) return;
+    combine_kernel<<<T, 256, 0, s>>>(y, pos, routes, shared, residual, H, k, out);
+}
+
+}  // namespace moe

@@ -1,0 +1,77 @@
+// Kernel entry points and argument blocks shared by the C ABI (api.cu) and
+// the kernel translation units.
+#pragma once
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+
+namespace moe {
+
+// Weight formats (values match MOE_B200_W* in include/moe_b200.h).
+enum { kFmtW4PC = 0, kFmtW4G32 = 1, kFmtW8PC = 2 };
+// GEMM epilogues.
+enum { kEpiSwiGLU = 0, kEpiStore = 1, kEpiAcc = 2 };
+// Activation quantisation rules.
+enum { kQuantMoe = 0, kQuantDense = 1 };
+
+struct RouterArgs {
+    const float* x;       // [T][H]
+    const float* w;       // [E][H]
+    const float* bias;    // [E] or null
+    int T, H, E, k, order;
+    float min_weight;
+    float* logits;        // [T][E] scratch / output
+    int* counters;        // [ceil(T)] zeroed tile counters
+    int32_t* ids;         // [T][k]
+    float* weights;       // [T][k]
+    uint32_t* err;
+};
+
+struct GemmArgs {
+    const float* act_scale;   // per permuted row
+    const int32_t* offsets;   // [E+1] row ranges of the permuted activations
+    int num_experts;
+    int max_rows;             // upper bound of offsets[E] (grid sizing)
+    const uint8_t* w;         // tile-major packed weights
+    size_t w_expert_stride;   // bytes
+    size_t w_tile_stride;     // bytes per 128-row tile (all k-blocks)
+    const void* wscale;       // scales, tile-major
+    size_t ws_expert_stride;  // bytes
+    size_t ws_tile_stride;    // bytes
+    int kblocks;              // K / 128
+    int row_tiles;            // weight row tiles of 128
+    float* out;               // SwiGLU: middle [rows][ldo]; store: y [rows][ldo]
+    int ldo;
+    int n_valid;              // valid output channels (I or H)
+    uint32_t* rowmax;         // SwiGLU: per-row max |middle| as float bits
+    int32_t* acc_out;         // accumulator dump
+    int acc_ld;               // row length of the dump (n or 2I)
+    int swiglu_layout;        // dump channel mapping of the gate/up tiles
+    uint32_t* err;
+};
+
+__device__ void topk_row(const float* row, int E, int k, float min_weight, int32_t* ids,
+                         float* weights, int lane, uint32_t* err);
+
+int launch_router(const RouterArgs& a, cudaStream_t s);
+int launch_gemm(const CUtensorMap& map, const GemmArgs& a, int fmt, int epi, int nt,
+                int num_sms, cudaStream_t s);
+
+// dispatch.cu
+void launch_route_count(const int32_t* ids, const float* routes, int n, int E, int32_t* hist,
+                        uint32_t* err, cudaStream_t s);
+void launch_route_scatter(const int32_t* ids, const float* routes, int n, int E,
+                          const int32_t* hist, int32_t* offsets, int32_t* perm, int32_t* pos,
+                          int32_t* shared_offsets, int T, cudaStream_t s);
+void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k,
+                         const int32_t* pos, int8_t* q_rows, float* s_rows, int8_t* q_perm,
+                         float* s_perm, uint32_t* err, cudaStream_t s);
+void launch_requant(const float* mid, const uint32_t* rowmax, const int32_t* count,
+                    int max_rows, int I, int ld_q, int rule, int8_t* q, float* sc,
+                    cudaStream_t s);
+void launch_combine(const float* y, const int32_t* pos, const float* routes, const float* shared,
+                    const float* residual, int T, int H, int k, float* out, cudaStream_t s);
+
+constexpr int kRouteChunk = 2048;  // assignments per route_count / route_scatter CTA
+
+}  // namespace moe
