@@ -1,0 +1,464 @@
+"""Benchmark of the B200 MoE layer (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the Qwen3-30B-A3B-shaped W4A8 MoE layer
+(H=2048, 128 experts, top-8, I=768, int4 group-32 fp16 scales, per-token int8
+activations), 512 prefill tokens per GPU, seeded synthetic data. One step =
+one router-inclusive layer forward (router + top-k, dispatch, gate/up GEMM +
+SwiGLU, requant, down GEMM, combine + residual) on inputs resident in HBM.
+`e2e` times the same layer through the public host-pointer API with the
+input/residual copied from pinned host memory and the output read back.
+Decode (T=1) and 4096-token prefill are reported under "extra".
+
+With N > 1 (torchrun) every rank runs its own replica of the layer on its own
+512 tokens (weak scaling); the time is the max over ranks.
+`--impl reference` times the CPU restatement of the reference path (the
+oracle, all host threads) on the same workload, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "W4A8 MoE-layer tokens/s"
+CONFIG = "c2"
+TOKENS = 512
+SEED = 1234
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+INT8_DENSE_TOPS = 4500.0  # B200 datasheet dense int8 (TOPS); not yet measured here
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples during the timed region (read-only queries)."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        loaded = [s for s in sm if s > 0.5 * (max(sm) if sm else 1)]
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- traffic
+def measured_traffic(key: str):
+    """DRAM bytes per launch of the dominant kernel from a committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        v = d.get(key)
+        if isinstance(v, dict):
+            return v.get("bytes_per_launch")
+        return v
+    return None
+
+
+def layer_bytes(spec, T, U, A):
+    """Algorithmic HBM bytes of one layer call (weights of the U experts hit,
+    router, activations in/out, residual)."""
+    H, I = spec.hidden, spec.inter
+    w = 3 * H * I // 2 + 3 * H * I // 32 * 2          # int4 codes + fp16 group scales
+    b = U * w + spec.experts * H * 4 + 3 * T * H * 4  # router f32, x in, residual, out
+    b += A * H + A * I * 4 * 2 + A * I + A * H * 4 * 2  # permuted rows, middle, codes, y
+    return b
+
+
+def gate_up_bytes(spec, U, A):
+    """Algorithmic bytes of one gate/up GEMM launch: int4 codes + fp16 scales of
+    the experts hit, the permuted int8 activation rows, the fp32 middle written."""
+    H, I = spec.hidden, spec.inter
+    return U * (2 * I * H // 2 + 2 * I * H // 32 * 2) + A * H + A * I * 4
+
+
+# ---------------------------------------------------------------- ours
+def setup_dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from open_rknpu2_lm_infer_b200 import synthetic as S
+    from open_rknpu2_lm_infer_b200.moe import Backend
+
+    world, rank, local = setup_dist()
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    spec = S.CONFIGS[CONFIG]
+    T = args.tokens
+    layer = S.make_layer(spec, seed=SEED)
+    max_rows = max(T, 4096 if args.extra else T)
+    be = Backend(device=local, max_rows=max_rows)
+    moe = be.load_moe(layer.gate, layer.down, spec.top)
+    router = be.router(layer.router, spec.top, layer.bias)
+    lib, wsp = be.lib, moe.workspace
+
+    def inputs(t, stream_id):
+        return torch.from_numpy(S.make_input(spec, t, seed=SEED + rank, stream=stream_id)).cuda()
+
+    x, res = inputs(T, 4), inputs(T, 5)
+    out = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step(t=T, xx=None, rr=None, oo=None):
+        moe.forward_device(router, t, (xx if xx is not None else x).data_ptr(),
+                           (rr if rr is not None else res).data_ptr(),
+                           (oo if oo is not None else out).data_ptr(), sp)
+
+    for _ in range(args.warmup):
+        step()
+    moe.status()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)  # let the sampler start before the timed region
+    lib.moe_b200_workspace_profile(wsp, 1)
+    launches0 = lib.moe_b200_workspace_launches(wsp)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    launches = lib.moe_b200_workspace_launches(wsp) - launches0
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    moe.status()
+
+    # per-stage device times of the timed calls (events on the launching stream)
+    from open_rknpu2_lm_infer_b200 import _lib as L
+    stages = []
+    for i in range(args.steps):
+        tm = L.Timings()
+        if lib.moe_b200_workspace_profile_read(wsp, i, tm) == 0:
+            stages.append(tm.as_dict())
+    lib.moe_b200_workspace_profile(wsp, 0)
+    stage_avg = {k: statistics.mean(s[k] for s in stages) for k in stages[0]} if stages else {}
+
+    # routing statistics of the last call: experts hit, kept assignments
+    offs_ptr, _ = moe.buffer("offsets")
+    offs = np.empty(spec.experts + 1, np.int32)
+    import ctypes as C
+    torch.cuda.synchronize()
+    cudart_copy(offs, offs_ptr)
+    U = int(np.count_nonzero(np.diff(offs)))
+    A = int(offs[-1])
+
+    pk, pk_kind = peaks()
+    hbm_peak = pk["hbm_gbs"]
+    gu_bytes = gate_up_bytes(spec, U, A)
+    gate_us = stage_avg.get("gate_us", float("nan"))
+    achieved = gu_bytes / (gate_us * 1e-6) / 1e9 if gate_us == gate_us and gate_us > 0 else None
+    traffic = measured_traffic(f"{CONFIG}_T{T}_gate_up")
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": (achieved / hbm_peak) if achieved else None, "traffic": traffic,
+                "kernel": "grouped_gemm_kernel<W4G32, SwiGLU> (gate/up)",
+                "algorithmic_bytes_per_launch": gu_bytes, "kernel_us": gate_us,
+                "peak_kind": f"{pk_kind} (hbm_gbs, STREAM-style copy)"}
+
+    # ---------------------------------------------------------------- e2e
+    e2e = run_e2e(args, moe, router, spec, T, rank, world)
+
+    value = world * T / (ms * 1e-3)
+    lbytes = layer_bytes(spec, T, U, A)
+    ops = 2 * A * 3 * spec.hidden * spec.inter
+    result = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic: seeded activations ~N(0,1); weights ~N(0,0.02) quantised to int4 "
+                "group-32 with fp16 scales",
+        "config": {"workload": f"{CONFIG}: Qwen3-30B-A3B-shaped W4A8 MoE layer, {T}-token prefill "
+                               "per GPU, router-inclusive forward with residual",
+                   "hidden": spec.hidden, "experts": spec.experts, "top_k": spec.top,
+                   "intermediate": spec.inter, "weights": "int4 g32 fp16 scales",
+                   "tokens_per_gpu": T, "global_batch": T * world, "seq_len": T,
+                   "parallelism": f"replica x{world}" if world > 1 else "single GPU",
+                   "l2": "no flush: the expert weights read per step (~340 MB) exceed the "
+                         "126 MB L2"},
+        "roofline": roofline,
+        "e2e": e2e,
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "stage_us": stage_avg,
+        "layer": {"experts_hit": U, "assignments": A,
+                  "algorithmic_bytes": lbytes,
+                  "hbm_frac_layer": lbytes / (ms * 1e-3) / 1e9 / hbm_peak,
+                  "int8_tops": ops / (ms * 1e-3) / 1e12,
+                  "int8_frac_of_datasheet": ops / (ms * 1e-3) / 1e12 / INT8_DENSE_TOPS},
+    }
+    if args.extra and world == 1:
+        result["extra"] = run_extra(args, moe, router, spec, lib, wsp, hbm_peak)
+    if rank == 0 and world == 1 and args.cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(layer, spec, T, budget_s=args.cpu_seconds)
+    moe.close()
+    router.close()
+    be.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def cudart_copy(dst: np.ndarray, src_ptr: int):
+    import torch
+
+    class _CAI:
+        def __init__(self):
+            self.__cuda_array_interface__ = {"shape": dst.shape, "typestr": dst.dtype.str,
+                                             "data": (src_ptr, False), "version": 3}
+    dst[...] = torch.as_tensor(_CAI(), device="cuda").cpu().numpy()
+
+
+def run_e2e(args, moe, router, spec, T, rank, world):
+    """Public host API (moe_b200_forward_f32): pinned input/residual -> device,
+    layer, output + routing -> host, all inside the timed call. Time per call =
+    CUDA events on the library's stream around the copies and the layer."""
+    import torch
+    from open_rknpu2_lm_infer_b200 import synthetic as S
+    xh = torch.empty((T, spec.hidden), dtype=torch.float32, pin_memory=True)
+    rh = torch.empty_like(xh, pin_memory=True)
+    xh.numpy()[...] = S.make_input(spec, T, seed=SEED + rank, stream=4)
+    rh.numpy()[...] = S.make_input(spec, T, seed=SEED + rank, stream=5)
+    x, r = xh.numpy(), rh.numpy()
+    for _ in range(args.warmup):
+        moe.forward(router, x, r)
+    times = []
+    for _ in range(args.steps):
+        *_, tm = moe.forward(router, x, r, timings=True)
+        times.append(tm["total_us"])
+    mean_us = statistics.mean(times)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([mean_us], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        mean_us = float(t.item())
+    h2d = 2 * T * spec.hidden * 4
+    d2h = T * spec.hidden * 4 + 2 * T * spec.top * 4
+    return {"value": world * T / (mean_us * 1e-6), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": mean_us / 1000.0,
+            "api": "moe_b200_forward_f32 (pinned host buffers)"}
+
+
+def run_extra(args, moe, router, spec, lib, wsp, hbm_peak):
+    import torch
+    from open_rknpu2_lm_infer_b200 import _lib as L
+    from open_rknpu2_lm_infer_b200 import synthetic as S
+    out = {}
+    for name, T in (("decode_t1", 1), ("prefill_t4096", 4096)):
+        x = torch.from_numpy(S.make_input(spec, T, seed=SEED, stream=4)).cuda()
+        res = torch.from_numpy(S.make_input(spec, T, seed=SEED, stream=5)).cuda()
+        o = torch.empty_like(x)
+        sp = torch.cuda.current_stream().cuda_stream
+        call = lambda: moe.forward_device(router, T, x.data_ptr(), res.data_ptr(), o.data_ptr(), sp)
+        for _ in range(max(3, args.warmup)):
+            call()
+        steps = max(3, min(args.steps, 20))
+        torch.cuda.synchronize()
+        lib.moe_b200_workspace_profile(wsp, 1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            call()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        st = []
+        for i in range(steps):
+            tm = L.Timings()
+            if lib.moe_b200_workspace_profile_read(wsp, i, tm) == 0:
+                st.append(tm.as_dict())
+        lib.moe_b200_workspace_profile(wsp, 0)
+        avg = {k: statistics.mean(s[k] for s in st) for k in st[0]} if st else {}
+        offs_ptr, _ = moe.buffer("offsets")
+        offs = np.empty(spec.experts + 1, np.int32)
+        cudart_copy(offs, offs_ptr)
+        U, A = int(np.count_nonzero(np.diff(offs))), int(offs[-1])
+        lb = layer_bytes(spec, T, U, A)
+        ops = 2 * A * 3 * spec.hidden * spec.inter
+        gb = gate_up_bytes(spec, U, A)
+        out[name] = {"tokens": T, "ms_per_step": ms, "tokens_per_s": T / (ms * 1e-3),
+                     "experts_hit": U, "hbm_frac_layer": lb / (ms * 1e-3) / 1e9 / hbm_peak,
+                     "int8_tops": ops / (ms * 1e-3) / 1e12,
+                     "int8_frac_of_datasheet": ops / (ms * 1e-3) / 1e12 / INT8_DENSE_TOPS,
+                     "gate_up_us": avg.get("gate_us"), "down_us": avg.get("down_us"),
+                     "gate_up_gbs": gb / (avg["gate_us"] * 1e-6) / 1e9 if avg else None,
+                     "stage_us": avg}
+    return out
+
+
+# ---------------------------------------------------------------- CPU side
+def cpu_baseline(layer, spec, T, budget_s=10.0):
+    """The CPU restatement (oracle/, all host threads) on a bounded sample of
+    the same workload: repeated full forwards of the T-token layer."""
+    from oracle import oracle as O
+    from open_rknpu2_lm_infer_b200 import synthetic as S
+    ol = O.OracleLayer(layer)
+    x = S.make_input(spec, T, seed=SEED, stream=4)
+    res = S.make_input(spec, T, seed=SEED, stream=5)
+    ol.forward(x[:8], res[:8])  # warm-up (thread pool, page-in)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        ol.forward(x, res)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 50:
+            break
+    return {"value": reps * T / el, "unit": "tokens/s", "cores": O.threads(), "kind": "port",
+            "sample": f"{reps} forwards of the {T}-token {CONFIG} layer ({el:.1f} s), "
+                      "CPU restatement of the reference MoE path, OpenMP"}
+
+
+def run_reference(args):
+    """--impl reference: the reference path's CPU implementation (restated in
+    oracle/, since the reference's Rust/NPU code cannot run here) on the host
+    cores, same workload; rank 0 only."""
+    world, rank, _ = setup_dist()
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    from open_rknpu2_lm_infer_b200 import synthetic as S
+    spec = S.CONFIGS[CONFIG]
+    T = args.tokens
+    layer = S.make_layer(spec, seed=SEED)
+    ol = O.OracleLayer(layer)
+    x = S.make_input(spec, T, seed=SEED, stream=4)
+    res = S.make_input(spec, T, seed=SEED, stream=5)
+    # bounded sample per step: tokens of the same layer, sized from a probe
+    t0 = time.perf_counter()
+    ol.forward(x[:64], res[:64])
+    per_tok = (time.perf_counter() - t0) / 64
+    budget = 150.0 / max(1, args.steps + args.warmup)  # whole run within a few minutes
+    ts = int(max(16, min(T, budget / max(per_tok, 1e-9))))
+    for _ in range(args.warmup):
+        ol.forward(x[:ts], res[:ts])
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        ol.forward(x[:ts], res[:ts])
+        times.append(time.perf_counter() - t0)
+    ms = statistics.mean(times) * 1e3
+    value = ts / (ms * 1e-3)
+    sample = f"{ts} of the {T} tokens per step, CPU restatement of the reference MoE path"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (same seeded layer as the GPU arm)",
+        "config": {"workload": f"{CONFIG}: Qwen3-30B-A3B-shaped W4A8 MoE layer, {T}-token prefill",
+                   "hidden": spec.hidden, "experts": spec.experts, "top_k": spec.top,
+                   "intermediate": spec.inter, "tokens_per_gpu": T, "seq_len": T,
+                   "global_batch": T},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": O.threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--no-extra", dest="extra", action="store_false")
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()
