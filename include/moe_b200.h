@@ -38,6 +38,7 @@ extern "C" {
 #define MOE_B200_ERR_NONFINITE (-8)     /* non-finite router logit / activation */
 #define MOE_B200_ERR_BAD_ROUTE (-9)     /* negative or NaN routing weight */
 #define MOE_B200_ERR_NO_DEVICE (-10)    /* no sm_100 device / library built without it */
+#define MOE_B200_ERR_NOALLOC_LIMIT (-11) /* request larger than the fixed no-allocation scratch */
 
 /* Routed-expert weight formats. */
 #define MOE_B200_W4_PER_CHANNEL 0 /* reference native format: int4 codes, f32 scale per n */
@@ -209,6 +210,29 @@ int moe_b200_workspace_profile_read(moe_b200_workspace *ws, int32_t call, moe_b2
 
 /* Number of kernels this workspace has launched since creation. */
 int64_t moe_b200_workspace_launches(const moe_b200_workspace *ws);
+
+/* Router + top-k that allocates nothing (no counterpart in the reference; an
+ * addition for callers that cannot call cudaMalloc, such as an engine whose
+ * own pool owns all device memory, or a hot path that must not risk an
+ * allocation or its device synchronisation). Same results as
+ * moe_b200_route_device, but without a workspace or router object: the
+ * caller passes device input [rows][hidden] f32, router weights
+ * [experts][hidden] f32, optional bias [experts] (or NULL), and the device
+ * outputs ids / routes [rows][top]. Scratch (logits and tile counters) lives
+ * in one fixed device array of the library, about 4.3 MiB on every GPU that
+ * loads it, kept until exit; rows * experts must not exceed
+ * MOE_B200_NOALLOC_MAX_LOGITS, else MOE_B200_ERR_NOALLOC_LIMIT. Runs on the
+ * calling thread's current device (the stream must belong to it). The first
+ * call on a device looks up the scratch array's device address, so make that
+ * first call before any stream capture. All calls on a device share the
+ * scratch: calls that overlap on the GPU (other streams or host threads) race
+ * and must be serialised by the caller. Asynchronous; non-finite logits are
+ * not reported by this entry point. */
+#define MOE_B200_NOALLOC_MAX_LOGITS (1 << 20)
+int moe_b200_route_noalloc(const float *d_input, const float *d_router, const float *d_bias,
+                           int32_t rows, int32_t hidden, int32_t experts, int32_t top,
+                           int32_t order, float min_weight, int32_t *d_ids, float *d_routes,
+                           void *stream);
 
 /* Replaces rk_npu_strerror (src/npu.rs:187-193). */
 const char *moe_b200_strerror(int code);

@@ -22,6 +22,8 @@ ERR_BAD_EXPERT = -7
 ERR_NONFINITE = -8
 ERR_BAD_ROUTE = -9
 ERR_NO_DEVICE = -10
+ERR_NOALLOC_LIMIT = -11
+NOALLOC_MAX_LOGITS = 1 << 20
 
 W4_PER_CHANNEL = 0
 W4_G32_FP16 = 1
@@ -103,6 +105,9 @@ SIGNATURES = [
     ("moe_b200_workspace_profile", C.c_int, [C.c_void_p, C.c_int32]),
     ("moe_b200_workspace_profile_read", C.c_int, [C.c_void_p, C.c_int32, C.POINTER(Timings)]),
     ("moe_b200_workspace_launches", C.c_int64, [C.c_void_p]),
+    ("moe_b200_route_noalloc", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+      C.c_float, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("moe_b200_strerror", C.c_char_p, [C.c_int]),
     ("moe_b200_version", C.c_char_p, []),
 ]

@@ -981,6 +981,8 @@ const char* moe_b200_strerror(int code) {
         case MOE_B200_ERR_NONFINITE: return "non-finite router logit or activation";
         case MOE_B200_ERR_BAD_ROUTE: return "negative or NaN routing weight";
         case MOE_B200_ERR_NO_DEVICE: return "no sm_100 CUDA device available";
+        case MOE_B200_ERR_NOALLOC_LIMIT:
+            return "rows * experts exceed the fixed scratch of the no-allocation router";
         default: return "unknown error";
     }
 }
