@@ -248,13 +248,11 @@ struct moe_b200_workspace {
     float* s_perm = nullptr;
     // routed experts
     float* middle = nullptr;
-    uint32_t* rowmax = nullptr;
     int8_t* q_m = nullptr;
     float *s_m = nullptr, *y = nullptr;
     // shared expert
     int8_t *q_xd = nullptr, *sq_m = nullptr;
     float *s_xd = nullptr, *s_middle = nullptr, *ss_m = nullptr, *s_y = nullptr;
-    uint32_t* s_rowmax = nullptr;
     float* logits = nullptr;
     uint32_t* err = nullptr;
     CUtensorMap map_a[3], map_qm[3], map_qx[3], map_qxd[3], map_sqm[3];
@@ -296,8 +294,7 @@ int map_err_bits(uint32_t bits) {
 }
 
 GemmArgs gemm_args(moe_b200_workspace* ws, const PackedMat& m, const float* act_scale,
-                   const int32_t* offsets, int experts, long max_rows, float* out, int ldo,
-                   uint32_t* rowmax) {
+                   const int32_t* offsets, int experts, long max_rows, float* out, int ldo) {
     GemmArgs a{};
     a.act_scale = act_scale;
     a.offsets = offsets;
@@ -314,7 +311,6 @@ GemmArgs gemm_args(moe_b200_workspace* ws, const PackedMat& m, const float* act_
     a.out = out;
     a.ldo = ldo;
     a.n_valid = m.n;
-    a.rowmax = rowmax;
     a.swiglu_layout = m.swiglu ? 1 : 0;
     a.err = ws->err;
     return a;
@@ -333,18 +329,18 @@ int run_shared(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, cons
         amap = &ws->map_qxd[nt_index(nt)];
         ascale = ws->s_xd;
     }
-    cudaMemsetAsync(ws->s_rowmax, 0, sizeof(uint32_t) * rows, s);
-    GemmArgs g = gemm_args(ws, w->sgu, ascale, ws->shared_offsets, 1, rows, ws->s_middle, w->Is,
-                           ws->s_rowmax);
+    GemmArgs g = gemm_args(ws, w->sgu, ascale, ws->shared_offsets, 1, rows, ws->s_middle, w->Is);
     if (launch_gemm(*amap, g, w->sgu.fmt, kEpiSwiGLU, nt, ws->num_sms, s)) return MOE_B200_ERR_UNSUPPORTED;
-    launch_requant(ws->s_middle, ws->s_rowmax, ws->shared_offsets + 1, rows, w->Is, ws->Kis, rule,
-                   ws->sq_m, ws->ss_m, s);
-    GemmArgs d = gemm_args(ws, w->sdn, ws->ss_m, ws->shared_offsets, 1, rows, ws->s_y, ws->H,
-                           nullptr);
+    launch_requant(ws->s_middle, ws->shared_offsets + 1, rows, w->Is, ws->Kis, rule, ws->sq_m,
+                   ws->ss_m, s);
+    GemmArgs d = gemm_args(ws, w->sdn, ws->ss_m, ws->shared_offsets, 1, rows, ws->s_y, ws->H);
     if (launch_gemm(ws->map_sqm[nt_index(nt)], d, w->sdn.fmt, kEpiStore, nt, ws->num_sms, s))
         return MOE_B200_ERR_UNSUPPORTED;
     return MOE_B200_OK;
 }
+
+// Activation / output rows are moved as 16-byte vectors.
+bool aligned16(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int compatible(const moe_b200_workspace* ws, const moe_b200_weights* w) {
     if (!ws || !w) return MOE_B200_ERR_INVALID;
@@ -384,16 +380,14 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
     launch_quant_gather(d_x, rows, H, ws->Kh, kQuantMoe, k, ws->pos, ws->q_x, ws->s_x, ws->a_perm,
                         ws->s_perm, ws->err, s);
     mark(3);
-    cudaMemsetAsync(ws->rowmax, 0, sizeof(uint32_t) * n, s);
     const int nt = choose_nt(n, E);
-    GemmArgs g = gemm_args(ws, w->gu, ws->s_perm, ws->offsets, E, n, ws->middle, I, ws->rowmax);
+    GemmArgs g = gemm_args(ws, w->gu, ws->s_perm, ws->offsets, E, n, ws->middle, I);
     if (launch_gemm(ws->map_a[nt_index(nt)], g, w->gu.fmt, kEpiSwiGLU, nt, ws->num_sms, s))
         return MOE_B200_ERR_UNSUPPORTED;
     mark(4);
-    launch_requant(ws->middle, ws->rowmax, ws->offsets + E, (int)n, I, ws->Ki, kQuantMoe, ws->q_m,
-                   ws->s_m, s);
+    launch_requant(ws->middle, ws->offsets + E, (int)n, I, ws->Ki, kQuantMoe, ws->q_m, ws->s_m, s);
     mark(5);
-    GemmArgs d = gemm_args(ws, w->dn, ws->s_m, ws->offsets, E, n, ws->y, H, nullptr);
+    GemmArgs d = gemm_args(ws, w->dn, ws->s_m, ws->offsets, E, n, ws->y, H);
     if (launch_gemm(ws->map_qm[nt_index(nt)], d, w->dn.fmt, kEpiStore, nt, ws->num_sms, s))
         return MOE_B200_ERR_UNSUPPORTED;
     mark(6);
@@ -624,7 +618,6 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     rc |= ws_alloc(ws, &ws->a_perm, (n + pad_rows) * ws->Kh);
     rc |= ws_alloc(ws, &ws->s_perm, n);
     rc |= ws_alloc(ws, &ws->middle, n * ws->I);
-    rc |= ws_alloc(ws, &ws->rowmax, n);
     rc |= ws_alloc(ws, &ws->q_m, (n + pad_rows) * ws->Ki);
     rc |= ws_alloc(ws, &ws->s_m, n);
     rc |= ws_alloc(ws, &ws->y, n * ws->H);
@@ -634,7 +627,6 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
         rc |= ws_alloc(ws, &ws->q_xd, (T + pad_rows) * ws->Kh);
         rc |= ws_alloc(ws, &ws->s_xd, T);
         rc |= ws_alloc(ws, &ws->s_middle, T * ws->Is);
-        rc |= ws_alloc(ws, &ws->s_rowmax, T);
         rc |= ws_alloc(ws, &ws->sq_m, (T + pad_rows) * ws->Kis);
         rc |= ws_alloc(ws, &ws->ss_m, T);
         rc |= ws_alloc(ws, &ws->s_y, T * ws->H);
@@ -694,6 +686,7 @@ int moe_b200_run_device(moe_b200_workspace* ws, const moe_b200_weights* w, int32
     if (rows > ws->max_rows) return MOE_B200_ERR_CAPACITY;
     if (rows == 0) return MOE_B200_OK;
     if (!d_input || !d_ids || !d_routes || !d_output) return MOE_B200_ERR_INVALID;
+    if (!aligned16(d_input) || !aligned16(d_output)) return MOE_B200_ERR_INVALID;
     DeviceGuard guard(ws->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaEvent_t* evs = prof_slot(ws, w->shared ? 2 : 0);
@@ -820,6 +813,9 @@ int moe_b200_forward_device(moe_b200_workspace* ws, const moe_b200_weights* w,
     if (rows < 0) return MOE_B200_ERR_INVALID;
     if (rows > ws->max_rows) return MOE_B200_ERR_CAPACITY;
     if (rows == 0) return MOE_B200_OK;
+    if (!d_input || !d_output || !aligned16(d_input) || !aligned16(d_residual) ||
+        !aligned16(d_output))
+        return MOE_B200_ERR_INVALID;
     DeviceGuard guard(ws->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaEvent_t* evs = prof_slot(ws, 1 | (w->shared ? 2 : 0));
@@ -893,7 +889,6 @@ int moe_b200_workspace_buffer(moe_b200_workspace* ws, const char* name, void** d
         {"a_perm", ws->a_perm, (uint64_t)n * ws->Kh},
         {"s_perm", ws->s_perm, sizeof(float) * (uint64_t)n},
         {"middle", ws->middle, sizeof(float) * (uint64_t)n * ws->I},
-        {"rowmax", ws->rowmax, sizeof(uint32_t) * (uint64_t)n},
         {"q_m", ws->q_m, (uint64_t)n * ws->Ki},
         {"s_m", ws->s_m, sizeof(float) * (uint64_t)n},
         {"y", ws->y, sizeof(float) * (uint64_t)n * ws->H},
@@ -927,8 +922,8 @@ int moe_b200_debug_accumulators(moe_b200_workspace* ws, const moe_b200_weights* 
     if ((uint64_t)n * G * ld > capacity_elems) return MOE_B200_ERR_CAPACITY;
     cudaMemsetAsync(d_acc, 0, sizeof(int32_t) * (size_t)n * G * ld, s);
     const int nt = which == 0 ? ws->last_nt_gu : ws->last_nt_dn;
-    GemmArgs a = which == 0 ? gemm_args(ws, m, ws->s_perm, ws->offsets, ws->E, n, nullptr, 0, nullptr)
-                            : gemm_args(ws, m, ws->s_m, ws->offsets, ws->E, n, nullptr, 0, nullptr);
+    GemmArgs a = which == 0 ? gemm_args(ws, m, ws->s_perm, ws->offsets, ws->E, n, nullptr, 0)
+                            : gemm_args(ws, m, ws->s_m, ws->offsets, ws->E, n, nullptr, 0);
     a.acc_out = d_acc;
     a.acc_ld = ld;
     a.n_valid = which == 0 ? w->I : w->H;

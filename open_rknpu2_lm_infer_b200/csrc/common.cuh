@@ -184,6 +184,60 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+}
+
+// N consecutive 32-bit columns of this thread's lane (N = 8, 16 or 32).
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
+    if constexpr (N == 8) {
+        tmem_ld8(taddr, r);
+    } else if constexpr (N == 16) {
+        tmem_ld16(taddr, r);
+    } else {
+        static_assert(N == 32, "tmem_ld width");
+        tmem_ld32(taddr, r);
+    }
+}
+
+// Fill N consecutive 32-bit columns of this thread's lane with one value.
+template <int N>
+__device__ __forceinline__ void tmem_fill(uint32_t taddr, uint32_t v) {
+    if constexpr (N == 8) {
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+            "r"(v)
+            : "memory");
+    } else if constexpr (N == 16) {
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+            "%1,%1,%1};" ::"r"(taddr),
+            "r"(v)
+            : "memory");
+    } else {
+        static_assert(N == 32, "tmem_fill width");
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+            "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+            "r"(v)
+            : "memory");
+    }
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major operand stored in the
 // 128-byte swizzle layout: rows of 128 bytes, 8-row atoms of 1024 bytes.
 __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t smem_addr) {

@@ -147,14 +147,25 @@ __device__ __forceinline__ int quant_one(float x, float s, float inv, int rule) 
     return q > 127 ? 127 : (q < -127 ? -127 : q);
 }
 
-__device__ __forceinline__ float block_max_256(float v, float* red) {
+__device__ __forceinline__ uint32_t quant4(float4 v, float s, float inv, int rule) {
+    return (uint32_t)(quant_one(v.x, s, inv, rule) & 0xFF) |
+           ((uint32_t)(quant_one(v.y, s, inv, rule) & 0xFF) << 8) |
+           ((uint32_t)(quant_one(v.z, s, inv, rule) & 0xFF) << 16) |
+           ((uint32_t)(quant_one(v.w, s, inv, rule) & 0xFF) << 24);
+}
+
+__device__ __forceinline__ float amax4(float4 v) {
+    return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+}
+
+// Block-wide max of non-negative values (blockDim.x a multiple of 32, <= 1024).
+__device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
     float m = red[0];
     for (int i = 1; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
-    __syncthreads();
     return m;
 }
 
@@ -165,26 +176,29 @@ __device__ __forceinline__ float row_scale(float m, int rule) {
     return s;
 }
 
-// One CTA per token: quantise the row once, write it to q_rows[t] (if given)
-// and to every kept permuted slot pos[t*k + r] (if pos given).
+// One CTA (256 threads) per token: the row is read once into registers
+// (V float4 per thread), quantised, and written to q_rows[t] (if given) and
+// to every kept permuted slot pos[t*k + r] (if pos given). The padding
+// columns of the destinations stay as created (zero). Needs H % 4 == 0.
+template <int V>
 __global__ void __launch_bounds__(256)
 quant_gather_kernel(const float* __restrict__ x, int H, int ld_q, int rule, int k,
                     const int32_t* __restrict__ pos, int8_t* q_rows, float* s_rows,
                     int8_t* q_perm, float* s_perm, uint32_t* err) {
     __shared__ float red[8];
     __shared__ int slots[32];
-    const int t = blockIdx.x;
-    const float* xr = x + (size_t)t * H;
-    float m = 0.0f;
-    for (int c = threadIdx.x; c < H; c += blockDim.x) {
-        const float a = fabsf(xr[c]);
-        if (a > m) m = a;
-    }
-    m = block_max_256(m, red);
-    const float s = row_scale(m, rule);
-    const float inv = __fdiv_rn(1.0f, s);
-    if (!isfinite(s) && threadIdx.x == 0) atomicOr(err, kErrNonFinite);
     __shared__ int nslot_s;
+    const int t = blockIdx.x;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * H);
+    const int n4 = H / 4;
+    float4 v[V];
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int c = threadIdx.x + 256 * i;
+        v[i] = c < n4 ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        m = fmaxf(m, amax4(v[i]));
+    }
     if (threadIdx.x == 0) {
         int ns = 0;
         if (pos)
@@ -193,66 +207,102 @@ quant_gather_kernel(const float* __restrict__ x, int H, int ld_q, int rule, int 
                 if (p >= 0) slots[ns++] = p;
             }
         nslot_s = ns;
-        if (s_rows) s_rows[t] = s;
-        for (int i = 0; i < ns; ++i) s_perm[slots[i]] = s;
     }
-    __syncthreads();
+    m = block_max(m, red);  // includes a __syncthreads: slots are visible after it
+    const float s = row_scale(m, rule);
+    const float inv = __fdiv_rn(1.0f, s);
     const int nslot = nslot_s;
-    // 4 columns per step -> one 32-bit store per destination
-    for (int c4 = threadIdx.x * 4; c4 < ld_q; c4 += blockDim.x * 4) {
-        uint32_t packed = 0;
+    if (threadIdx.x == 0) {
+        if (!isfinite(s)) atomicOr(err, kErrNonFinite);
+        if (s_rows) s_rows[t] = s;
+        for (int i = 0; i < nslot; ++i) s_perm[slots[i]] = s;
+    }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int c = c4 + i;
-            const int q = c < H ? quant_one(xr[c], s, inv, rule) : 0;
-            packed |= (uint32_t)(q & 0xFF) << (8 * i);
+    for (int i = 0; i < V; ++i) {
+        const int c = threadIdx.x + 256 * i;
+        if (c < n4) {
+            const uint32_t packed = quant4(v[i], s, inv, rule);
+            if (q_rows) reinterpret_cast<uint32_t*>(q_rows + (size_t)t * ld_q)[c] = packed;
+            for (int j = 0; j < nslot; ++j)
+                reinterpret_cast<uint32_t*>(q_perm + (size_t)slots[j] * ld_q)[c] = packed;
         }
-        if (q_rows) *reinterpret_cast<uint32_t*>(q_rows + (size_t)t * ld_q + c4) = packed;
-        for (int i = 0; i < nslot; ++i)
-            *reinterpret_cast<uint32_t*>(q_perm + (size_t)slots[i] * ld_q + c4) = packed;
     }
 }
 
-// One CTA per permuted row; rows >= *count exit. Scale from the row max that
-// the gate/up epilogue accumulated.
+// One CTA (128 threads) per permuted row; rows >= *count exit. Reads the
+// SwiGLU row once (V float4 per thread), takes its max |m|, quantises.
+template <int V>
 __global__ void __launch_bounds__(128)
-requant_kernel(const float* __restrict__ mid, const uint32_t* __restrict__ rowmax,
-               const int32_t* __restrict__ count, int I, int ld_q, int rule, int8_t* q,
-               float* sc) {
+requant_kernel(const float* __restrict__ mid, const int32_t* __restrict__ count, int I, int ld_q,
+               int rule, int8_t* q, float* sc) {
+    __shared__ float red[4];
     const int row = blockIdx.x;
     if (row >= *count) return;
-    const float m = __uint_as_float(rowmax[row]);
+    const float4* mr = reinterpret_cast<const float4*>(mid + (size_t)row * I);
+    const int n4 = I / 4;
+    float4 v[V];
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int c = threadIdx.x + 128 * i;
+        v[i] = c < n4 ? mr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        m = fmaxf(m, amax4(v[i]));
+    }
+    m = block_max(m, red);
     const float s = row_scale(m, rule);
     const float inv = __fdiv_rn(1.0f, s);
     if (threadIdx.x == 0) sc[row] = s;
-    const float* mr = mid + (size_t)row * I;
-    for (int c4 = threadIdx.x * 4; c4 < ld_q; c4 += blockDim.x * 4) {
-        uint32_t packed = 0;
+    uint32_t* qr = reinterpret_cast<uint32_t*>(q + (size_t)row * ld_q);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int c = c4 + i;
-            const int qv = c < I ? quant_one(mr[c], s, inv, rule) : 0;
-            packed |= (uint32_t)(qv & 0xFF) << (8 * i);
-        }
-        *reinterpret_cast<uint32_t*>(q + (size_t)row * ld_q + c4) = packed;
+    for (int i = 0; i < V; ++i) {
+        const int c = threadIdx.x + 128 * i;
+        if (c < n4) qr[c] = quant4(v[i], s, inv, rule);
     }
 }
 
+// One CTA (256 threads) per token, float4 columns (H % 4 == 0).
 __global__ void __launch_bounds__(256)
 combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ pos,
                const float* __restrict__ routes, const float* __restrict__ shared,
                const float* __restrict__ residual, int H, int k, float* out) {
+    __shared__ int ps[32];
+    __shared__ float ws[32];
     const int t = blockIdx.x;
-    for (int c = threadIdx.x; c < H; c += blockDim.x) {
-        float acc = 0.0f;
+    if (threadIdx.x < k) {
+        const size_t a = (size_t)t * k + threadIdx.x;
+        const float w = routes[a];
+        ws[threadIdx.x] = route_kept(w) ? w : 0.0f;
+        ps[threadIdx.x] = route_kept(w) ? pos[a] : -1;
+    }
+    __syncthreads();
+    const int n4 = H / 4;
+    for (int c = threadIdx.x; c < n4; c += blockDim.x) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int r = 0; r < k; ++r) {
-            const size_t a = (size_t)t * k + r;
-            const float w = routes[a];
-            if (route_kept(w)) acc = __fmaf_rn(y[(size_t)pos[a] * H + c], w, acc);
+            const int p = ps[r];
+            if (p < 0) continue;
+            const float w = ws[r];
+            const float4 yv = reinterpret_cast<const float4*>(y + (size_t)p * H)[c];
+            acc.x = __fmaf_rn(yv.x, w, acc.x);
+            acc.y = __fmaf_rn(yv.y, w, acc.y);
+            acc.z = __fmaf_rn(yv.z, w, acc.z);
+            acc.w = __fmaf_rn(yv.w, w, acc.w);
         }
-        if (shared) acc = __fadd_rn(acc, shared[(size_t)t * H + c]);
-        if (residual) acc = __fadd_rn(residual[(size_t)t * H + c], acc);
-        out[(size_t)t * H + c] = acc;
+        if (shared) {
+            const float4 sv = reinterpret_cast<const float4*>(shared + (size_t)t * H)[c];
+            acc.x = __fadd_rn(acc.x, sv.x);
+            acc.y = __fadd_rn(acc.y, sv.y);
+            acc.z = __fadd_rn(acc.z, sv.z);
+            acc.w = __fadd_rn(acc.w, sv.w);
+        }
+        if (residual) {
+            const float4 rv = reinterpret_cast<const float4*>(residual + (size_t)t * H)[c];
+            acc.x = __fadd_rn(rv.x, acc.x);
+            acc.y = __fadd_rn(rv.y, acc.y);
+            acc.z = __fadd_rn(rv.z, acc.z);
+            acc.w = __fadd_rn(rv.w, acc.w);
+        }
+        reinterpret_cast<float4*>(out + (size_t)t * H)[c] = acc;
     }
 }
 
@@ -279,15 +329,26 @@ void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k
                          const int32_t* pos, int8_t* q_rows, float* s_rows, int8_t* q_perm,
                          float* s_perm, uint32_t* err, cudaStream_t s) {
     if (T == 0) return;
-    quant_gather_kernel<<<T, 256, 0, s>>>(x, H, ld_q, rule, k, pos, q_rows, s_rows, q_perm,
-                                          s_perm, err);
+    const int v = (H / 4 + 255) / 256;
+#define QG(V) quant_gather_kernel<V><<<T, 256, 0, s>>>(x, H, ld_q, rule, k, pos, q_rows, s_rows, q_perm, s_perm, err)
+    if (v <= 1) QG(1);
+    else if (v <= 2) QG(2);
+    else if (v <= 4) QG(4);
+    else QG(8);
+#undef QG
 }
 
-void launch_requant(const float* mid, const uint32_t* rowmax, const int32_t* count,
-                    int max_rows, int I, int ld_q, int rule, int8_t* q, float* sc,
-                    cudaStream_t s) {
+void launch_requant(const float* mid, const int32_t* count, int max_rows, int I, int ld_q,
+                    int rule, int8_t* q, float* sc, cudaStream_t s) {
     if (max_rows == 0) return;
-    requant_kernel<<<max_rows, 128, 0, s>>>(mid, rowmax, count, I, ld_q, rule, q, sc);
+    const int v = (I / 4 + 127) / 128;
+#define RQ(V) requant_kernel<V><<<max_rows, 128, 0, s>>>(mid, count, I, ld_q, rule, q, sc)
+    if (v <= 1) RQ(1);
+    else if (v <= 2) RQ(2);
+    else if (v <= 4) RQ(4);
+    else if (v <= 8) RQ(8);
+    else RQ(16);
+#undef RQ
 }
 
 void launch_combine(const float* y, const int32_t* pos, const float* routes, const float* shared,

@@ -8,45 +8,64 @@
 //
 // Layout ("swap-AB"): the weight tile is the MMA's M=128 operand and the
 // tokens of one expert are the N operand, so one TMEM lane = one output
-// channel and TMEM columns = tokens. Small token counts (decode) then cost
-// N=16 columns instead of a 128-row M tile, and each epilogue thread owns a
-// channel whose per-group scale it loads once per group.
+// channel and TMEM columns = tokens. Small token counts (decode) cost N=16
+// columns instead of a 128-row M tile, and each epilogue thread owns a
+// channel whose per-group scale it reads once per group.
 //
-// Warp roles (320 threads):
-//   warp 0      producer: bulk copies of pre-swizzled weight tiles + scales,
-//               TMA tensor loads of the permuted activation rows
-//   warp 1      TMEM allocator + single-thread MMA issuer
-//   warps 2..5  int4 -> int8 unpack into the 128B-swizzled operand buffer
-//   warps 6..9  epilogue: tcgen05.ld, scale, SwiGLU / store
+// Warp roles (384 threads):
+//   warp 0       producer: bulk copies of pre-swizzled weight blocks and
+//                scales, TMA tensor loads of the permuted activation rows,
+//                into a deep load ring (~100 KB in flight per SM)
+//   warp 1       TMEM allocator + single-thread MMA issuer
+//   warps 2..3   int4 -> int8 unpack from the load ring into a 3-deep
+//                operand ring (W4 formats)
+//   warps 4..11  epilogue, two warps per TMEM lane quadrant, each owning half
+//                of the token columns
 //
-// Group-32 formats: one MMA (K = 32 = one group) per TMEM buffer, exact INT32
-// per group, accumulated in fp32 by the epilogue as fma(acc_g, s_g, f).
+// Group-32 formats: one MMA (K = 32 = one group) per TMEM buffer of a ring.
+// Every buffer is pre-filled with the bits of 12582912.0f (0x4B400000) and
+// the MMA accumulates into it, so the int32 result read back as a float is
+// exactly 12582912 + 16*acc (|16*acc| < 2^22). The epilogue then computes
+// f = fma(D - 12582912, s/16, f): an exact subtraction and one FMA, equal to
+// fma((float)acc, s, f) bit for bit, without an int->float conversion.
 // Per-channel formats: all of K accumulates in TMEM, one dequant per tile.
 #include "kernels.cuh"
 
 namespace moe {
 
-constexpr int kGemmThreads = 320;
-constexpr int kStages = 4;          // smem ring depth (k-blocks)
-constexpr int kScaleStages = 8;     // group-scale ring depth (k-blocks)
-constexpr int kTileRows = 128;      // weight rows per tile (MMA M)
-constexpr int kKBlock = 128;        // K bytes per stage (one 128B swizzle row)
+constexpr int kGemmThreads = 384;
+constexpr int kEpiWarp0 = 4;          // first epilogue warp
+constexpr int kEpiWarps = 8;
+constexpr int kConvWarps = 2;
+constexpr int kScaleStages = 8;       // group-scale ring depth (k-blocks)
+constexpr int kTileRows = 128;        // weight rows per tile (MMA M)
+constexpr int kKBlock = 128;          // K bytes per stage (one 128B swizzle row)
+constexpr uint32_t kMagicBits = 0x4B400000u;  // 12582912.0f
+constexpr float kMagic = 12582912.0f;
 
 template <int FMT, int NT>
 struct GemmCfg {
     static constexpr bool kW4 = (FMT == kFmtW4G32 || FMT == kFmtW4PC);
     static constexpr bool kGroup = (FMT == kFmtW4G32);
-    static constexpr int kPackedBytes = kW4 ? kTileRows * kKBlock / 2 : 0;  // 8 KB
-    static constexpr int kOperandBytes = kTileRows * kKBlock;               // 16 KB
+    static constexpr int kWBytes = kW4 ? kTileRows * kKBlock / 2 : kTileRows * kKBlock;
     static constexpr int kActBytes = NT * kKBlock;
-    static constexpr int kStageBytes = kOperandBytes + kActBytes + kPackedBytes;
-    static constexpr int kScaleBytes = kGroup ? 4 * kTileRows * 2 : 0;     // 1 KB
-    // TMEM buffers: groups in flight (group formats) or tile accumulators.
-    static constexpr int kNBuf = kGroup ? ((512 / NT) < 16 ? (512 / NT) : 16) : 2;
-    static constexpr int kCols = kNBuf * NT;
+    static constexpr int kOpBytes = kTileRows * kKBlock;     // MMA weight operand (16 KB)
+    // load stage: [activation rows][weight operand][packed int4 (W4)]
+    static constexpr int kLoadBytes = kActBytes + kOpBytes + (kW4 ? kWBytes : 0);
+    static constexpr int kBudget = 196 * 1024;
+    static constexpr int kFit = kBudget / kLoadBytes;
+    static constexpr int kLoadStages = kFit >= 8 ? 8 : kFit;
+    static constexpr int kScaleBytes = kGroup ? 4 * kTileRows * 2 : 0;  // 1 KB
+    // TMEM: group formats use slots of one k-block (4 group buffers of NT
+    // columns); per-channel formats use two tile accumulators.
+    static constexpr int kSlotCols = kGroup ? 4 * NT : NT;
+    static constexpr int kNSlot = kGroup ? ((512 / kSlotCols) < 4 ? (512 / kSlotCols) : 4) : 2;
+    static constexpr int kCols = kNSlot * kSlotCols;
     static constexpr int kAllocCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
                                     : kCols <= 256 ? 256 : 512;
+    static constexpr int kHalf = NT / 2;                      // columns per epilogue warp
     static constexpr int kXchgStride = NT + 1;
+    static_assert(kLoadStages >= 4, "smem budget");
 };
 
 struct TileCoord {
@@ -55,14 +74,12 @@ struct TileCoord {
 
 // Tile t -> (expert, weight row tile, token tile); token tile fastest so the
 // CTAs sharing a weight tile run together and reuse it from L2.
-__device__ __forceinline__ TileCoord decode_tile(int t, const int* tb, const int* tcnt, int E,
-                                                 int row_tiles) {
-    int lo = 0, hi = E - 1;  // last e with tb[e] <= t and a non-empty range
+__device__ __forceinline__ TileCoord decode_tile(int t, const int* tb, const int* tcnt, int E) {
+    int lo = 0, hi = E - 1;  // last e with tb[e] <= t (that expert is non-empty)
     while (lo < hi) {
         int mid = (lo + hi + 1) >> 1;
         if (tb[mid] <= t) lo = mid; else hi = mid - 1;
     }
-    // skip back over experts with no tiles that share the same start
     while (lo > 0 && tcnt[lo] == 0) --lo;
     TileCoord c;
     c.e = lo;
@@ -76,26 +93,24 @@ template <int FMT, int EPI, int NT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs a) {
     using C = GemmCfg<FMT, NT>;
+    constexpr int SL = C::kLoadStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    // 1024-byte alignment for the swizzled operand buffers
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
-    uint8_t* op_w = smem;                                   // [S][16 KB]
-    uint8_t* op_a = op_w + kStages * C::kOperandBytes;      // [S][NT*128]
-    uint8_t* packed = op_a + kStages * C::kActBytes;        // [S][8 KB] (W4)
-    uint8_t* scales = packed + kStages * C::kPackedBytes;   // [SS][1 KB] (group)
+    uint8_t* load = smem;
+    uint8_t* scales = load + SL * C::kLoadBytes;              // [SS][1 KB] (group)
     float* xchg = reinterpret_cast<float*>(scales + kScaleStages * C::kScaleBytes);
     uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + 64 * C::kXchgStride + 2);
-    uint64_t* full = bars;
-    uint64_t* conv = full + kStages;
-    uint64_t* empty = conv + kStages;
-    uint64_t* sfull = empty + kStages;
+    uint64_t* lfull = bars;           // TMA bytes of stage s landed
+    uint64_t* lempty = lfull + SL;    // MMAs that read stage s completed
+    uint64_t* ofull = lempty + SL;    // int4 operand of stage s unpacked (W4)
+    uint64_t* sfull = ofull + SL;
     uint64_t* sempty = sfull + kScaleStages;
     uint64_t* tfull = sempty + kScaleStages;
-    uint64_t* tempty = tfull + C::kNBuf;
-    uint64_t* done = tempty + C::kNBuf;
-    uint64_t* xfull = done + 1;   // up values written (2 warps)
-    uint64_t* xempty = xfull + 1; // gate warps done reading (2 warps)
+    uint64_t* tempty = tfull + C::kNSlot;
+    uint64_t* done = tempty + C::kNSlot;
+    uint64_t* xfull = done + 1;    // up halves written (4 warps)
+    uint64_t* xempty = xfull + 1;  // gate halves read (4 warps)
     int* tcnt = reinterpret_cast<int*>(xempty + 1);
     int* tb = tcnt + a.num_experts + 1;
     __shared__ uint32_t tmem_base_s;
@@ -104,28 +119,31 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int E = a.num_experts;
+    auto act_at = [&](int s) { return load + s * C::kLoadBytes; };
+    auto op_at = [&](int s) { return load + s * C::kLoadBytes + C::kActBytes; };
+    auto packed_at = [&](int s) { return load + s * C::kLoadBytes + C::kActBytes + C::kOpBytes; };
 
     if (threadIdx.x == 0) {
         abort_s = 0;
-        for (int i = 0; i < kStages; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&conv[i], 4);
-            mbar_init(&empty[i], 1);
+        for (int i = 0; i < SL; ++i) {
+            mbar_init(&lfull[i], 1);
+            mbar_init(&lempty[i], 1);
+            mbar_init(&ofull[i], kConvWarps);
         }
         for (int i = 0; i < kScaleStages; ++i) {
             mbar_init(&sfull[i], 1);
-            mbar_init(&sempty[i], 4);
+            mbar_init(&sempty[i], kEpiWarps);
         }
-        for (int i = 0; i < C::kNBuf; ++i) {
+        for (int i = 0; i < C::kNSlot; ++i) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], 4);
+            mbar_init(&tempty[i], kEpiWarps);
         }
         mbar_init(done, 1);
-        mbar_init(xfull, 2);
-        mbar_init(xempty, 2);
+        mbar_init(xfull, 4);
+        mbar_init(xempty, 4);
         fence_barrier_init();
     }
-    // tile table: tcnt[e] = token tiles of expert e, tb[e] = first tile index
+    // tile table: tcnt[e] = token tiles of expert e, tb[e] = its first tile index
     if (warp == 2) {
         const int per = (E + 31) / 32;
         int local = 0;
@@ -166,51 +184,70 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     const int total = total_tiles_s;
     volatile int* abort_flag = &abort_s;
 
+    // epilogue geometry: quadrant = TMEM lanes, half = token columns
+    const int ew = warp - kEpiWarp0;
+    const int quad = warp & 3;
+    const int half = ew >= 4 ? 1 : 0;
+    const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+    if (C::kGroup && warp >= kEpiWarp0) {
+        // every group buffer starts as the float 12582912.0
+        for (int b = 0; b < C::kNSlot * 4; ++b)
+            tmem_fill<C::kHalf>(tmem_base + lane_addr + b * NT + half * C::kHalf, kMagicBits);
+        tmem_wait_st();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                const TileCoord c = decode_tile(t, tb, tcnt, E, a.row_tiles);
+                const TileCoord c = decode_tile(t, tb, tcnt, E);
                 const int row0 = a.offsets[c.e] + c.mt * NT;
                 const uint8_t* wtile = a.w + (size_t)c.e * a.w_expert_stride +
                                        (size_t)c.rt * a.w_tile_stride;
-                for (int kb = 0; kb < a.kblocks && ok; ++kb, ++it) {
-                    const int s = it % kStages;
-                    const uint32_t ph = (it / kStages) & 1u;
-                    if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err)) { ok = false; break; }
-                    constexpr uint32_t wbytes = C::kW4 ? C::kPackedBytes : C::kOperandBytes;
-                    mbar_arrive_expect_tx(&full[s], wbytes + C::kActBytes);
-                    const uint8_t* wsrc = wtile + (size_t)kb * wbytes;
-                    uint8_t* wdst = C::kW4 ? packed + s * C::kPackedBytes : op_w + s * C::kOperandBytes;
-                    bulk_g2s(wdst, wsrc, wbytes, &full[s]);
-                    tma_load_2d(op_a + s * C::kActBytes, &act_map, kb * kKBlock, row0, &full[s]);
+                const uint8_t* stile = reinterpret_cast<const uint8_t*>(a.wscale) +
+                                       (size_t)c.e * a.ws_expert_stride +
+                                       (size_t)c.rt * a.ws_tile_stride;
+                for (int kb = 0; kb < a.kblocks; ++kb, ++it) {
+                    const int s = it % SL;
+                    if (!mbar_wait(&lempty[s], ((it / SL) & 1u) ^ 1u, abort_flag, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&lfull[s], C::kWBytes + C::kActBytes);
+                    bulk_g2s(C::kW4 ? packed_at(s) : op_at(s), wtile + (size_t)kb * C::kWBytes,
+                             C::kWBytes, &lfull[s]);
+                    tma_load_2d(act_at(s), &act_map, kb * kKBlock, row0, &lfull[s]);
                     if (C::kGroup) {
                         const int ss = it % kScaleStages;
-                        const uint32_t sph = (it / kScaleStages) & 1u;
-                        if (!mbar_wait(&sempty[ss], sph ^ 1u, abort_flag, a.err)) { ok = false; break; }
+                        if (!mbar_wait(&sempty[ss], ((it / kScaleStages) & 1u) ^ 1u, abort_flag,
+                                       a.err)) {
+                            ++it;  // the load stage above was issued
+                            ok = false;
+                            break;
+                        }
                         mbar_arrive_expect_tx(&sfull[ss], C::kScaleBytes);
-                        const uint8_t* ssrc = reinterpret_cast<const uint8_t*>(a.wscale) +
-                                              (size_t)c.e * a.ws_expert_stride +
-                                              (size_t)c.rt * a.ws_tile_stride +
-                                              (size_t)kb * C::kScaleBytes;
-                        bulk_g2s(scales + ss * C::kScaleBytes, ssrc, C::kScaleBytes, &sfull[ss]);
+                        bulk_g2s(scales + ss * C::kScaleBytes, stile + (size_t)kb * C::kScaleBytes,
+                                 C::kScaleBytes, &sfull[ss]);
                     }
                 }
             }
-            // drain: every issued fill must land before the CTA exits
-            const uint32_t first = it > (uint32_t)kStages ? it - kStages : 0u;
-            for (uint32_t d = first; d < it; ++d) {
-                int dummy = 0;
-                mbar_wait(&full[d % kStages], (d / kStages) & 1u, &dummy, a.err);
-            }
+            // drain: every issued copy lands before the CTA can exit
+            int never = 0;
+            for (uint32_t d = it > (uint32_t)SL ? it - SL : 0u; d < it; ++d)
+                mbar_wait(&lfull[d % SL], (d / SL) & 1u, &never, a.err);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
+        // Two tcgen05.commit per k-block at most (slot full, stage empty): the
+        // commit is the costly part of issuing, so groups share one.
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_i8(kTileRows, NT);
-            uint32_t it = 0, gi = 0, ti = 0;
+            uint32_t it = 0, ti = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++ti) {
                 uint32_t dcol = 0;
@@ -221,89 +258,98 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                     dcol = buf * NT;
                 }
                 for (int kb = 0; kb < a.kblocks && ok; ++kb, ++it) {
-                    const int s = it % kStages;
-                    const uint32_t ph = (it / kStages) & 1u;
-                    uint64_t* ready = C::kW4 ? &conv[s] : &full[s];
-                    if (!mbar_wait(ready, ph, abort_flag, a.err)) { ok = false; break; }
+                    const int s = it % SL;
+                    if (!mbar_wait(&lfull[s], (it / SL) & 1u, abort_flag, a.err) ||
+                        (C::kW4 && !mbar_wait(&ofull[s], (it / SL) & 1u, abort_flag, a.err))) {
+                        ok = false;
+                        break;
+                    }
+                    uint32_t slot = 0;
+                    if (C::kGroup) {
+                        slot = it % C::kNSlot;
+                        if (!mbar_wait(&tempty[slot], ((it / C::kNSlot) & 1u) ^ 1u, abort_flag,
+                                       a.err)) {
+                            ok = false;
+                            break;
+                        }
+                    }
                     tc_fence_after();
-                    const uint32_t wa = smem_u32(op_w + s * C::kOperandBytes);
-                    const uint32_t ab = smem_u32(op_a + s * C::kActBytes);
+                    const uint32_t wa = smem_u32(op_at(s));
+                    const uint32_t ab = smem_u32(act_at(s));
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const uint64_t da = smem_desc_k_sw128(wa + 32 * j);
                         const uint64_t db = smem_desc_k_sw128(ab + 32 * j);
-                        if (C::kGroup) {
-                            const uint32_t buf = gi % C::kNBuf;
-                            if (!mbar_wait(&tempty[buf], ((gi / C::kNBuf) & 1u) ^ 1u, abort_flag,
-                                           a.err)) { ok = false; break; }
-                            tc_fence_after();
-                            mma_i8(tmem_base + buf * NT, da, db, idesc, 0u);
-                            mma_commit(&tfull[buf]);
-                            ++gi;
-                        } else {
+                        if (C::kGroup)
+                            mma_i8(tmem_base + slot * C::kSlotCols + j * NT, da, db, idesc, 1u);
+                        else
                             mma_i8(tmem_base + dcol, da, db, idesc, (kb > 0 || j > 0) ? 1u : 0u);
-                        }
                     }
-                    if (!ok) break;
-                    mma_commit(&empty[s]);
+                    if (C::kGroup) mma_commit(&tfull[slot]);
+                    mma_commit(&lempty[s]);
                 }
                 if (!C::kGroup && ok) mma_commit(&tfull[ti % 2u]);
             }
             // all issued MMAs complete before TMEM can be released
             mma_commit(done);
-            int dummy = 0;
-            mbar_wait(done, 0, &dummy, a.err);
+            int never = 0;
+            mbar_wait(done, 0, &never, a.err);
         }
-    } else if (warp < 6) {
+    } else if (warp < kEpiWarp0) {
         // ------------------------------------------------------------ int4 unpack
         if (C::kW4) {
-            const int ct = threadIdx.x - 64;  // 0..127
+            const int ct = threadIdx.x - 64;  // 0 .. 32*kConvWarps-1
             uint32_t it = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
                 for (int kb = 0; kb < a.kblocks; ++kb, ++it) {
-                    const int s = it % kStages;
-                    const uint32_t ph = (it / kStages) & 1u;
-                    if (!mbar_wait(&full[s], ph, abort_flag, a.err)) { ok = false; break; }
-                    const uint2* src = reinterpret_cast<const uint2*>(packed + s * C::kPackedBytes);
-                    uint4* dst = reinterpret_cast<uint4*>(op_w + s * C::kOperandBytes);
+                    // the producer refilled stage s only after the MMAs that read its
+                    // previous operand completed, so the operand slot is free here
+                    const int s = it % SL;
+                    if (!mbar_wait(&lfull[s], (it / SL) & 1u, abort_flag, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint2* src = reinterpret_cast<const uint2*>(packed_at(s));
+                    uint4* dst = reinterpret_cast<uint4*>(op_at(s));
+                    constexpr int kPer = C::kWBytes / 8 / (32 * kConvWarps);
+                    // all loads first: the compiler cannot prove src and dst apart,
+                    // so interleaving would serialise every load behind a store
+                    uint2 p[kPer];
 #pragma unroll
-                    for (int i = 0; i < C::kPackedBytes / 8 / 128; ++i) {
-                        const int idx = ct + 128 * i;
-                        const uint2 p = src[idx];
+                    for (int i = 0; i < kPer; ++i) p[i] = src[ct + 32 * kConvWarps * i];
+#pragma unroll
+                    for (int i = 0; i < kPer; ++i) {
                         // packed byte b holds element b (low nibble) and b+4 (high
                         // nibble) of an 8-element run; each lands as 16 * value.
-                        uint4 o;
-                        o.x = (p.x << 4) & 0xF0F0F0F0u;
-                        o.y = p.x & 0xF0F0F0F0u;
-                        o.z = (p.y << 4) & 0xF0F0F0F0u;
-                        o.w = p.y & 0xF0F0F0F0u;
-                        dst[idx] = o;
+                        uint4 v;
+                        v.x = (p[i].x << 4) & 0xF0F0F0F0u;
+                        v.y = p[i].x & 0xF0F0F0F0u;
+                        v.z = (p[i].y << 4) & 0xF0F0F0F0u;
+                        v.w = p[i].y & 0xF0F0F0F0u;
+                        dst[ct + 32 * kConvWarps * i] = v;
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&conv[s]);
+                    if (lane == 0) mbar_arrive(&ofull[s]);
                 }
             }
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        const int quad = warp & 3;                 // TMEM lanes 32*quad ...
-        const int r = quad * 32 + lane;            // weight row within the tile
-        const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-        uint32_t gi = 0, ti = 0, it = 0;
+        const int r = quad * 32 + lane;  // weight row within the tile = TMEM lane
+        const int c0 = half * C::kHalf;  // first token column of this warp
+        uint32_t ti = 0, it = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++ti) {
-            const TileCoord c = decode_tile(t, tb, tcnt, E, a.row_tiles);
+            const TileCoord c = decode_tile(t, tb, tcnt, E);
             const int m_e = a.offsets[c.e + 1] - a.offsets[c.e];
             const int row0 = a.offsets[c.e] + c.mt * NT;
             const int nvalid = min(NT, m_e - c.mt * NT);
-            const int nchunks = (nvalid + 7) / 8;
-            // output channel of this lane
+            // output channel of this lane (gate/up tiles: 64 gate rows then 64 up rows)
+            const bool swiglu_tile = (EPI == kEpiSwiGLU) || (EPI == kEpiAcc && a.swiglu_layout);
             int col;
             bool is_up = false;
-            // gate/up tiles hold 64 gate rows then 64 up rows of the same channels
-            const bool swiglu_tile = (EPI == kEpiSwiGLU) || (EPI == kEpiAcc && a.swiglu_layout);
             if (swiglu_tile) {
                 is_up = r >= 64;
                 col = c.rt * 64 + (r & 63);
@@ -311,9 +357,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                 col = c.rt * kTileRows + r;
             }
             const bool col_ok = col < a.n_valid;
-            float facc[NT];
+            float sx[C::kHalf];
 #pragma unroll
-            for (int j = 0; j < NT; ++j) facc[j] = 0.0f;
+            for (int q = 0; q < C::kHalf; ++q)
+                sx[q] = (c0 + q < nvalid) ? a.act_scale[row0 + c0 + q] : 0.0f;
             float wscale_pc = 0.0f;
             if (!C::kGroup) {
                 const float* sp = reinterpret_cast<const float*>(
@@ -321,6 +368,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                     (size_t)c.rt * a.ws_tile_stride);
                 wscale_pc = sp[r];
             }
+            float facc[C::kHalf];
+#pragma unroll
+            for (int q = 0; q < C::kHalf; ++q) facc[q] = 0.0f;
+
             if (C::kGroup) {
                 for (int kb = 0; kb < a.kblocks && ok; ++kb, ++it) {
                     const int ss = it % kScaleStages;
@@ -334,56 +385,55 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                     for (int j = 0; j < 4; ++j) sg[j] = __half2float(sc[j * kTileRows + r]);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&sempty[ss]);
+                    // one TMEM slot per k-block: wait once, then GB groups per round
+                    // trip (loads, one wait, re-arm, one wait)
+                    constexpr int GB = C::kHalf <= 16 ? 4 : 2;
+                    const uint32_t slot = it % C::kNSlot;
+                    if (!mbar_wait(&tfull[slot], (it / C::kNSlot) & 1u, abort_flag, a.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sbase = tmem_base + lane_addr + slot * C::kSlotCols + c0;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint32_t buf = gi % C::kNBuf;
-                        if (!mbar_wait(&tfull[buf], (gi / C::kNBuf) & 1u, abort_flag, a.err)) {
-                            ok = false;
-                            break;
+                    for (int j0 = 0; j0 < 4; j0 += GB) {
+                        uint32_t v[GB][C::kHalf];
+#pragma unroll
+                        for (int jj = 0; jj < GB; ++jj) tmem_ld<C::kHalf>(sbase + (j0 + jj) * NT, v[jj]);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int jj = 0; jj < GB; ++jj)  // re-arm for the next MMAs
+                            tmem_fill<C::kHalf>(sbase + (j0 + jj) * NT, kMagicBits);
+                        if (j0 + GB == 4) {
+                            tmem_wait_st();
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&tempty[slot]);
                         }
-                        tc_fence_after();
-                        const uint32_t taddr = tmem_base + lane_addr + buf * NT;
-                        // W4 codes enter the MMA as 16*w: fold 1/16 into the scale (exact)
-                        const float s_eff = C::kW4 ? sg[j] * 0.0625f : sg[j];
-                        if (EPI == kEpiAcc) {
 #pragma unroll
-                            for (int ch = 0; ch < NT / 8; ++ch) {
-                                if (ch < nchunks) {
-                                    uint32_t v[8];
-                                    tmem_ld8(taddr + ch * 8, v);
-                                    tmem_wait_ld();
+                        for (int jj = 0; jj < GB; ++jj) {
+                            const int j = j0 + jj;
+                            if (EPI == kEpiAcc) {
+                                const int g = kb * 4 + j;
+                                const int ncol = is_up ? a.n_valid + col : col;
 #pragma unroll
-                                    for (int q = 0; q < 8; ++q) {
-                                        const int jj = ch * 8 + q;
-                                        if (jj < nvalid && col_ok) {
-                                            int acc = (int)v[q];
-                                            if (C::kW4) acc >>= 4;
-                                            const int g = kb * 4 + j;
-                                            const int ncol = is_up ? a.n_valid + col : col;
-                                            a.acc_out[((size_t)(row0 + jj) * (a.kblocks * 4) + g) *
-                                                          a.acc_ld + ncol] = acc;
-                                        }
+                                for (int q = 0; q < C::kHalf; ++q) {
+                                    if (c0 + q < nvalid && col_ok) {
+                                        int acc = (int)(v[jj][q] - kMagicBits);
+                                        if (C::kW4) acc >>= 4;
+                                        a.acc_out[((size_t)(row0 + c0 + q) * (a.kblocks * 4) + g) *
+                                                      a.acc_ld + ncol] = acc;
                                     }
                                 }
-                            }
-                        } else {
+                            } else {
+                                // W4 codes enter the MMA as 16*w: fold 1/16 into the scale (exact)
+                                const float s_eff = C::kW4 ? sg[j] * 0.0625f : sg[j];
 #pragma unroll
-                            for (int ch = 0; ch < NT / 8; ++ch) {
-                                if (ch < nchunks) {
-                                    uint32_t v[8];
-                                    tmem_ld8(taddr + ch * 8, v);
-                                    tmem_wait_ld();
-#pragma unroll
-                                    for (int q = 0; q < 8; ++q)
-                                        facc[ch * 8 + q] = __fmaf_rn(
-                                            __int2float_rn((int)v[q]), s_eff, facc[ch * 8 + q]);
-                                }
+                                for (int q = 0; q < C::kHalf; ++q)
+                                    facc[q] = __fmaf_rn(__fsub_rn(__uint_as_float(v[jj][q]), kMagic),
+                                                        s_eff, facc[q]);
                             }
                         }
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&tempty[buf]);
-                        ++gi;
                     }
                 }
                 if (!ok) break;
@@ -391,84 +441,66 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                 const uint32_t buf = ti % 2u;
                 if (!mbar_wait(&tfull[buf], (ti / 2u) & 1u, abort_flag, a.err)) break;
                 tc_fence_after();
-                const uint32_t taddr = tmem_base + lane_addr + buf * NT;
-#pragma unroll
-                for (int ch = 0; ch < NT / 8; ++ch) {
-                    if (ch < nchunks) {
-                        uint32_t v[8];
-                        tmem_ld8(taddr + ch * 8, v);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            int acc = (int)v[q];
-                            if (C::kW4) acc >>= 4;
-                            if (EPI == kEpiAcc) {
-                                const int jj = ch * 8 + q;
-                                if (jj < nvalid && col_ok) {
-                                    const int ncol = is_up ? a.n_valid + col : col;
-                                    a.acc_out[(size_t)(row0 + jj) * a.acc_ld + ncol] = acc;
-                                }
-                            } else {
-                                facc[ch * 8 + q] = __int2float_rn(acc);
-                            }
-                        }
-                    }
-                }
+                uint32_t v[C::kHalf];
+                tmem_ld<C::kHalf>(tmem_base + lane_addr + buf * NT + c0, v);
+                tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
+#pragma unroll
+                for (int q = 0; q < C::kHalf; ++q) {
+                    int acc = (int)v[q];
+                    if (C::kW4) acc >>= 4;
+                    if (EPI == kEpiAcc) {
+                        if (c0 + q < nvalid && col_ok) {
+                            const int ncol = is_up ? a.n_valid + col : col;
+                            a.acc_out[(size_t)(row0 + c0 + q) * a.acc_ld + ncol] = acc;
+                        }
+                    } else {
+                        facc[q] = __int2float_rn(acc);
+                    }
+                }
             }
             if (EPI == kEpiAcc) continue;
 
             // dequantise with the per-token activation scale
-            float val[NT];
+            float val[C::kHalf];
 #pragma unroll
-            for (int j = 0; j < NT; ++j) {
-                if (j < nvalid) {
-                    const float sx = a.act_scale[row0 + j];
-                    if (C::kGroup)
-                        val[j] = __fmul_rn(facc[j], sx);
-                    else
-                        val[j] = __fmul_rn(__fmul_rn(facc[j], sx), wscale_pc);
-                } else {
-                    val[j] = 0.0f;
-                }
+            for (int q = 0; q < C::kHalf; ++q) {
+                if (C::kGroup)
+                    val[q] = __fmul_rn(facc[q], sx[q]);
+                else
+                    val[q] = __fmul_rn(__fmul_rn(facc[q], sx[q]), wscale_pc);
             }
             if (EPI == kEpiSwiGLU) {
-                // exchange: up lanes (64..127) hand their values to gate lanes
+                // up lanes (64..127) hand their values to the gate lanes of the same channel
                 const uint32_t xph = ti & 1u;
                 if (is_up) {
                     if (!mbar_wait(xempty, xph ^ 1u, abort_flag, a.err)) { ok = false; break; }
 #pragma unroll
-                    for (int j = 0; j < NT; ++j) xchg[(r - 64) * C::kXchgStride + j] = val[j];
+                    for (int q = 0; q < C::kHalf; ++q) xchg[(r - 64) * C::kXchgStride + c0 + q] = val[q];
                     __syncwarp();
                     if (lane == 0) mbar_arrive(xfull);
                 } else {
                     if (!mbar_wait(xfull, xph, abort_flag, a.err)) { ok = false; break; }
 #pragma unroll
-                    for (int j = 0; j < NT; ++j) {
+                    for (int q = 0; q < C::kHalf; ++q) {
+                        const int j = c0 + q;
                         if (j < nvalid) {
-                            const float gv = val[j];
+                            const float gv = val[q];
                             const float uv = xchg[r * C::kXchgStride + j];
                             const float d = __fadd_rn(1.0f, expf(-gv));
                             const float m = __fmul_rn(__fdiv_rn(gv, d), uv);
-                            float amax = col_ok ? fabsf(m) : 0.0f;
                             if (col_ok) a.out[(size_t)(row0 + j) * a.ldo + col] = m;
-#pragma unroll
-                            for (int off = 16; off > 0; off >>= 1)
-                                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-                            if (lane == 0) atomicMax(&a.rowmax[row0 + j], __float_as_uint(amax));
                         }
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(xempty);
                 }
-            } else {
-                if (col_ok) {
+            } else if (col_ok) {
 #pragma unroll
-                    for (int j = 0; j < NT; ++j)
-                        if (j < nvalid) a.out[(size_t)(row0 + j) * a.ldo + col] = val[j];
-                }
+                for (int q = 0; q < C::kHalf; ++q)
+                    if (c0 + q < nvalid) a.out[(size_t)(row0 + c0 + q) * a.ldo + col] = val[q];
             }
         }
         if (!ok) *abort_flag = 1;
@@ -486,12 +518,12 @@ template <int FMT, int EPI, int NT>
 static size_t gemm_smem_bytes(int E) {
     using C = GemmCfg<FMT, NT>;
     size_t b = 1024;  // alignment slack
-    b += (size_t)kStages * (C::kOperandBytes + C::kActBytes + C::kPackedBytes);
+    b += (size_t)C::kLoadStages * C::kLoadBytes;
     b += (size_t)kScaleStages * C::kScaleBytes;
     b += sizeof(float) * (64 * C::kXchgStride + 2);
-    b += sizeof(uint64_t) * (3 * kStages + 2 * kScaleStages + 2 * C::kNBuf + 3);
+    b += sizeof(uint64_t) * (3 * C::kLoadStages + 2 * kScaleStages + 2 * C::kNSlot + 3);
     b += sizeof(int) * (2 * (size_t)E + 2);
-    // one CTA per SM: the kernel allocates TMEM up to 512 columns
+    // one CTA per SM: the kernel allocates up to 512 TMEM columns
     return b < 120 * 1024 ? 120 * 1024 : b;
 }
 

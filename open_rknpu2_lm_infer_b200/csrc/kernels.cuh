@@ -43,7 +43,6 @@ struct GemmArgs {
     float* out;               // SwiGLU: middle [rows][ldo]; store: y [rows][ldo]
     int ldo;
     int n_valid;              // valid output channels (I or H)
-    uint32_t* rowmax;         // SwiGLU: per-row max |middle| as float bits
     int32_t* acc_out;         // accumulator dump
     int acc_ld;               // row length of the dump (n or 2I)
     int swiglu_layout;        // dump channel mapping of the gate/up tiles
@@ -66,12 +65,11 @@ void launch_route_scatter(const int32_t* ids, const float* routes, int n, int E,
 void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k,
                          const int32_t* pos, int8_t* q_rows, float* s_rows, int8_t* q_perm,
                          float* s_perm, uint32_t* err, cudaStream_t s);
-void launch_requant(const float* mid, const uint32_t* rowmax, const int32_t* count,
-                    int max_rows, int I, int ld_q, int rule, int8_t* q, float* sc,
-                    cudaStream_t s);
+void launch_requant(const float* mid, const int32_t* count, int max_rows, int I, int ld_q,
+                    int rule, int8_t* q, float* sc, cudaStream_t s);
 void launch_combine(const float* y, const int32_t* pos, const float* routes, const float* shared,
                     const float* residual, int T, int H, int k, float* out, cudaStream_t s);
 
-constexpr int kRouteChunk = 2048;  // assignments per route_count / route_scatter CTA
+constexpr int kRouteChunk = 512;  // assignments per route_count / route_scatter CTA
 
 }  // namespace moe

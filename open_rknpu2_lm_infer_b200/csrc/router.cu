@@ -16,34 +16,136 @@
 namespace moe {
 
 constexpr int kRouterThreads = 256;
-constexpr int kRouterEB = 128;          // experts per block pass
-constexpr int kRouterChunk = 64;        // hidden elements per smem stage
-constexpr int kRouterWStride = kRouterChunk + 16;  // padded row: conflict-free
 
-// grid: (ceil(T/TT), ceil(E/EB)). Each CTA computes logits for TT tokens x EB
-// experts into `logits`; the last CTA of a token tile to finish runs top-k.
-template <int TT>
-__global__ void __launch_bounds__(kRouterThreads)
-router_neon16_kernel(const float* __restrict__ x, const float* __restrict__ wr,
+// The 16 lanes of one (token, expert) dot live in 16 consecutive threads
+// (j = tid & 15); reduce them with the fixed tree of vaddq/vaddvq:
+// (l[j]+l[j+4]) + (l[j+8]+l[j+12]), then (v0+v1)+(v2+v3). Result in lane j=0.
+__device__ __forceinline__ float neon16_tree(float v) {
+    float s1 = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4, 16));   // a+b / c+d
+    float s2 = __fadd_rn(s1, __shfl_down_sync(0xffffffffu, s1, 8, 16)); // (a+b)+(c+d)
+    float p = __fadd_rn(s2, __shfl_down_sync(0xffffffffu, s2, 1, 16));  // v0+v1, v2+v3
+    return __fadd_rn(p, __shfl_down_sync(0xffffffffu, p, 2, 16));       // total
+}
+
+// Scalar tail (H % 16 elements, separately rounded products) and the bias.
+__device__ __forceinline__ float neon16_finish(float q, const float* wrow, const float* xrow,
+                                               int H16, int H, const float* bias, int e) {
+    for (int h = H16; h < H; ++h) q = __fadd_rn(q, __fmul_rn(wrow[h], xrow[h]));
+    if (bias) q = __fadd_rn(q, bias[e]);
+    return q;
+}
+
+// Last CTA of a token tile (all expert blocks done) runs top-k for its tokens.
+__device__ __forceinline__ void finish_tile(int* tile_counter, int tile, int t0, int nt, int E,
+                                            const float* logits, int k, float min_weight,
+                                            int32_t* ids, float* weights, uint32_t* err) {
+    __shared__ int is_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int prev = atomicAdd(&tile_counter[tile], 1);
+        is_last = (prev == (int)gridDim.y - 1);
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int t = warp; t < nt; t += blockDim.x / 32)
+        topk_row(logits + (size_t)(t0 + t) * E, E, k, min_weight, ids + (size_t)(t0 + t) * k,
+                 weights + (size_t)(t0 + t) * k, lane, err);
+    if (threadIdx.x == 0) tile_counter[tile] = 0;
+}
+
+// Decode-sized router: one token, 8 experts per CTA (grid (T, ceil(E/8))),
+// 128 threads = 8 experts x 16 lanes. The CTA's router rows and the token
+// row are staged in shared memory with one batch of 16-byte copies, then each
+// thread runs its lane's sequential FMA chain.
+constexpr int kDecEB = 8;
+__global__ void __launch_bounds__(128)
+router_decode_kernel(const float* __restrict__ x, const float* __restrict__ wr,
                      const float* __restrict__ bias, int T, int H, int E, float* logits,
                      int* tile_counter, int k, float min_weight, int32_t* ids, float* weights,
                      uint32_t* err) {
-    constexpr int EPG = kRouterEB / 16;  // experts per 16-thread group
-    extern __shared__ __align__(16) float router_smem[];
-    float* w_s[2] = {router_smem, router_smem + kRouterEB * kRouterWStride};
-    float* x_s[2] = {router_smem + 2 * kRouterEB * kRouterWStride,
-                     router_smem + 2 * kRouterEB * kRouterWStride + TT * kRouterChunk};
-    __shared__ int is_last;
-
-    const int tid = threadIdx.x;
-    const int j = tid & 15;
-    const int g = tid >> 4;
-    const int t0 = blockIdx.x * TT;
-    const int e0 = blockIdx.y * kRouterEB;
-    const int ne = min(kRouterEB, E - e0);
-    const int nt = min(TT, T - t0);
+    extern __shared__ __align__(16) float rsm[];
+    const int stride = H + 16;  // padded rows: the two experts of a warp use different banks
+    float* w_s = rsm;                     // [8][stride]
+    float* x_s = rsm + kDecEB * stride;   // [H]
+    const int t = blockIdx.x, e0 = blockIdx.y * kDecEB;
+    const int ne = min(kDecEB, E - e0);
     const int H16 = (H / 16) * 16;
-    const int nchunks = (H16 + kRouterChunk - 1) / kRouterChunk;
+    const bool vec = (H & 3) == 0;
+    if (vec) {
+        const int q4 = H / 4;
+        for (int idx = threadIdx.x; idx < (ne + 1) * q4; idx += blockDim.x) {
+            const int r = idx / q4, q = idx % q4;
+            const float* src = r < ne ? wr + (size_t)(e0 + r) * H + 4 * q : x + (size_t)t * H + 4 * q;
+            float* dst = r < ne ? w_s + r * stride + 4 * q : x_s + 4 * q;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src));
+        }
+        asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+    } else {
+        for (int idx = threadIdx.x; idx < (ne + 1) * H; idx += blockDim.x) {
+            const int r = idx / H, h = idx % H;
+            if (r < ne) w_s[r * stride + h] = wr[(size_t)(e0 + r) * H + h];
+            else x_s[h] = x[(size_t)t * H + h];
+        }
+    }
+    __syncthreads();
+    const int j = threadIdx.x & 15, el = threadIdx.x >> 4;
+    float acc = 0.0f;
+    if (el < ne) {
+        const float* wrow = w_s + el * stride;
+#pragma unroll 8
+        for (int i = 0; i < H16; i += 16) acc = __fmaf_rn(wrow[i + j], x_s[i + j], acc);
+    }
+    const float q = neon16_tree(acc);
+    if (j == 0 && el < ne)
+        logits[(size_t)t * E + e0 + el] =
+            neon16_finish(q, w_s + el * stride, x_s, H16, H, bias, e0 + el);
+    finish_tile(tile_counter, t, t, 1, E, logits, k, min_weight, ids, weights, err);
+}
+
+// Prefill-sized router: TT tokens x EB experts per CTA (grid (ceil(T/TT),
+// ceil(E/EB))), 256 threads = 16 lanes x 16 groups; a group owns EB/16 experts
+// for all TT tokens. Hidden dimension streamed in chunks of kCh through a
+// kStg-deep cp.async ring.
+template <int TT, int EB>
+__global__ void __launch_bounds__(kRouterThreads)
+router_tile_kernel(const float* __restrict__ x, const float* __restrict__ wr,
+                   const float* __restrict__ bias, int T, int H, int E, float* logits,
+                   int* tile_counter, int k, float min_weight, int32_t* ids, float* weights,
+                   uint32_t* err) {
+    constexpr int EPG = EB / 16;
+    constexpr int kCh = 128, kStg = 4, kWS = kCh + 16;
+    constexpr int kStageF = EB * kWS + TT * kCh;
+    extern __shared__ __align__(16) float rsm[];
+    const int tid = threadIdx.x, j = tid & 15, g = tid >> 4;
+    const int t0 = blockIdx.x * TT, e0 = blockIdx.y * EB;
+    const int ne = min(EB, E - e0), nt = min(TT, T - t0);
+    const int H16 = (H / 16) * 16;
+    const int nchunks = (H16 + kCh - 1) / kCh;
+    const bool vec = (H & 3) == 0;
+
+    auto load_chunk = [&](int c) {
+        float* w_s = rsm + (c % kStg) * kStageF;
+        float* x_s = w_s + EB * kWS;
+        const int h0 = c * kCh;
+        const int q4 = min(kCh, H16 - h0) / 4;
+        for (int idx = tid; idx < (EB + TT) * (kCh / 4); idx += kRouterThreads) {
+            const int r = idx / (kCh / 4), q = idx % (kCh / 4);
+            if (q >= q4) continue;
+            const bool isw = r < EB;
+            if (isw ? r >= ne : (r - EB) >= nt) continue;
+            const float* src = isw ? wr + (size_t)(e0 + r) * H + h0 + 4 * q
+                                   : x + (size_t)(t0 + r - EB) * H + h0 + 4 * q;
+            float* dst = isw ? w_s + r * kWS + 4 * q : x_s + (r - EB) * kCh + 4 * q;
+            if (vec) {
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src));
+            } else {
+                for (int c2 = 0; c2 < 4; ++c2) dst[c2] = src[c2];
+            }
+        }
+    };
 
     float acc[TT][EPG];
 #pragma unroll
@@ -51,101 +153,45 @@ router_neon16_kernel(const float* __restrict__ x, const float* __restrict__ wr,
 #pragma unroll
         for (int m = 0; m < EPG; ++m) acc[t][m] = 0.0f;
 
-    // stage loader: cp.async 16-byte pieces of the w rows and x rows of one chunk
-    auto load_chunk = [&](int c, int buf) {
-        const int h0 = c * kRouterChunk;
-        const int len = min(kRouterChunk, H16 - h0);  // multiple of 16
-        const int q4 = len / 4;
-        for (int idx = tid; idx < kRouterEB * (kRouterChunk / 4); idx += kRouterThreads) {
-            int e = idx / (kRouterChunk / 4), q = idx % (kRouterChunk / 4);
-            float* dst = &w_s[buf][e * kRouterWStride + 4 * q];
-            if (e < ne && q < q4 && (((H & 3) == 0))) {
-                const float* src = wr + (size_t)(e0 + e) * H + h0 + 4 * q;
-                asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)),
-                             "l"(src));
-            } else if (e < ne && q < q4) {
-                for (int c2 = 0; c2 < 4; ++c2) dst[c2] = wr[(size_t)(e0 + e) * H + h0 + 4 * q + c2];
-            }
-        }
-        for (int idx = tid; idx < TT * (kRouterChunk / 4); idx += kRouterThreads) {
-            int t = idx / (kRouterChunk / 4), q = idx % (kRouterChunk / 4);
-            float* dst = &x_s[buf][t * kRouterChunk + 4 * q];
-            if (t < nt && q < q4 && ((H & 3) == 0)) {
-                const float* src = x + (size_t)(t0 + t) * H + h0 + 4 * q;
-                asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)),
-                             "l"(src));
-            } else if (t < nt && q < q4) {
-                for (int c2 = 0; c2 < 4; ++c2) dst[c2] = x[(size_t)(t0 + t) * H + h0 + 4 * q + c2];
-            }
-        }
+    for (int c = 0; c < kStg - 1; ++c) {
+        if (c < nchunks) load_chunk(c);
         asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-
-    if (nchunks > 0) load_chunk(0, 0);
+    }
     for (int c = 0; c < nchunks; ++c) {
-        const int buf = c & 1;
-        if (c + 1 < nchunks) {
-            load_chunk(c + 1, buf ^ 1);
-            asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
-        }
+        asm volatile("cp.async.wait_group %0;" ::"n"(kStg - 2) : "memory");
         __syncthreads();
-        const int steps = min(kRouterChunk, H16 - c * kRouterChunk) / 16;
+        if (c + kStg - 1 < nchunks) load_chunk(c + kStg - 1);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        const float* w_s = rsm + (c % kStg) * kStageF;
+        const float* x_s = w_s + EB * kWS;
+        const int steps = min(kCh, H16 - c * kCh) / 16;
+#pragma unroll 2
+        for (int i = 0; i < steps; ++i) {
+            float wv[EPG];
 #pragma unroll
-        for (int i = 0; i < kRouterChunk / 16; ++i) {
-            if (i < steps) {
-                float wv[EPG];
+            for (int m = 0; m < EPG; ++m) wv[m] = w_s[(g + 16 * m) * kWS + 16 * i + j];
 #pragma unroll
-                for (int m = 0; m < EPG; ++m)
-                    wv[m] = w_s[buf][(g + 16 * m) * kRouterWStride + 16 * i + j];
+            for (int t = 0; t < TT; ++t) {
+                const float xv = x_s[t * kCh + 16 * i + j];
 #pragma unroll
-                for (int t = 0; t < TT; ++t) {
-                    const float xv = x_s[buf][t * kRouterChunk + 16 * i + j];
-#pragma unroll
-                    for (int m = 0; m < EPG; ++m) acc[t][m] = __fmaf_rn(wv[m], xv, acc[t][m]);
-                }
+                for (int m = 0; m < EPG; ++m) acc[t][m] = __fmaf_rn(wv[m], xv, acc[t][m]);
             }
         }
-        __syncthreads();
     }
-
-    // fixed reduction tree over the 16 lanes of each (t, e) dot
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
 #pragma unroll
         for (int m = 0; m < EPG; ++m) {
-            float v = acc[t][m];
-            float s1 = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 4, 16));     // a+b / c+d
-            float s2 = __fadd_rn(s1, __shfl_down_sync(0xffffffffu, s1, 8, 16));   // (a+b)+(c+d)
-            float p = __fadd_rn(s2, __shfl_down_sync(0xffffffffu, s2, 1, 16));    // v0+v1, v2+v3
-            float q = __fadd_rn(p, __shfl_down_sync(0xffffffffu, p, 2, 16));      // total
+            const float q = neon16_tree(acc[t][m]);
             const int e = g + 16 * m;
-            if (j == 0 && t < nt && e < ne) {
-                const float* wrow = wr + (size_t)(e0 + e) * H;
-                const float* xrow = x + (size_t)(t0 + t) * H;
-                for (int h = H16; h < H; ++h) q = __fadd_rn(q, __fmul_rn(wrow[h], xrow[h]));
-                if (bias) q = __fadd_rn(q, bias[e0 + e]);
-                logits[(size_t)(t0 + t) * E + e0 + e] = q;
-            }
+            if (j == 0 && t < nt && e < ne)
+                logits[(size_t)(t0 + t) * E + e0 + e] =
+                    neon16_finish(q, wr + (size_t)(e0 + e) * H, x + (size_t)(t0 + t) * H, H16, H,
+                                  bias, e0 + e);
         }
     }
-
-    // last CTA of this token tile runs top-k over all E logits
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        int prev = atomicAdd(&tile_counter[blockIdx.x], 1);
-        is_last = (prev == (int)gridDim.y - 1);
-    }
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int t = warp; t < nt; t += kRouterThreads / 32)
-        topk_row(logits + (size_t)(t0 + t) * E, E, k, min_weight, ids + (size_t)(t0 + t) * k,
-                 weights + (size_t)(t0 + t) * k, lane, err);
-    if (tid == 0) tile_counter[blockIdx.x] = 0;
+    finish_tile(tile_counter, blockIdx.x, t0, nt, E, logits, k, min_weight, ids, weights, err);
 }
 
 // x86 order: one thread per (token, expert), sequential sum += w*x with a
@@ -182,7 +228,7 @@ __device__ void topk_row(const float* row, int E, int k, float min_weight, int32
     bool finite = true;
     for (int i = 0; i < per_lane; ++i) {
         int e = lane + 32 * i;
-        if (e < E && !isfinite(row[e])) finite = false;
+        if (e < E && !isfinite(__ldcg(row + e))) finite = false;
     }
     if (__any_sync(0xffffffffu, !finite) && lane == 0) atomicOr(err, kErrNonFinite);
     for (int r = 0; r < k; ++r) {
@@ -190,7 +236,7 @@ __device__ void topk_row(const float* row, int E, int k, float min_weight, int32
         for (int i = 0; i < per_lane; ++i) {
             int e = lane + 32 * i;
             if (e >= E || (taken >> i) & 1u) continue;
-            uint32_t key = (uint32_t)total_key(row[e]) ^ 0x80000000u;
+            uint32_t key = (uint32_t)total_key(__ldcg(row + e)) ^ 0x80000000u;
             unsigned long long v = ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)e);
             if (v > best) best = v;
         }
@@ -205,9 +251,9 @@ __device__ void topk_row(const float* row, int E, int k, float min_weight, int32
     }
     // softmax over the selected, in rank order (src/model/qwen35/moe.rs:60-65)
     const int id0 = __shfl_sync(0xffffffffu, my_id, 0);
-    const float mx = row[id0];
+    const float mx = __ldcg(row + id0);
     float w = 0.0f;
-    if (lane < k) w = expf(__fsub_rn(row[my_id], mx));
+    if (lane < k) w = expf(__fsub_rn(__ldcg(row + my_id), mx));
     float sum = -0.0f;
     for (int r = 0; r < k; ++r) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, w, r));
     if (lane < k) {
@@ -216,21 +262,6 @@ __device__ void topk_row(const float* row, int E, int k, float min_weight, int32
         ids[lane] = my_id;
         weights[lane] = w;
     }
-}
-
-template <int TT>
-static void launch_neon16(const RouterArgs& a, cudaStream_t s) {
-    const size_t smem = sizeof(float) * (2 * kRouterEB * kRouterWStride + 2 * TT * kRouterChunk);
-    static bool configured = false;  // attribute is per function, set once per process
-    if (!configured) {
-        cudaFuncSetAttribute(router_neon16_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-        configured = true;
-    }
-    dim3 grid((a.T + TT - 1) / TT, (a.E + kRouterEB - 1) / kRouterEB);
-    router_neon16_kernel<TT><<<grid, kRouterThreads, smem, s>>>(
-        a.x, a.w, a.bias, a.T, a.H, a.E, a.logits, a.counters, a.k, a.min_weight, a.ids,
-        a.weights, a.err);
 }
 
 int launch_router(const RouterArgs& a, cudaStream_t s) {
@@ -242,12 +273,25 @@ int launch_router(const RouterArgs& a, cudaStream_t s) {
                                                            a.min_weight, a.ids, a.weights, a.err);
         return 0;
     }
-    if (a.T >= 2048)
-        launch_neon16<16>(a, s);
-    else if (a.T >= 64)
-        launch_neon16<4>(a, s);
-    else
-        launch_neon16<1>(a, s);
+    if (a.T < 16) {
+        const size_t smem = sizeof(float) * ((size_t)kDecEB * (a.H + 16) + a.H);
+        if (smem > 200 * 1024) return -1;
+        cudaFuncSetAttribute(router_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+        dim3 grid(a.T, (a.E + kDecEB - 1) / kDecEB);
+        router_decode_kernel<<<grid, 128, smem, s>>>(a.x, a.w, a.bias, a.T, a.H, a.E, a.logits,
+                                                     a.counters, a.k, a.min_weight, a.ids,
+                                                     a.weights, a.err);
+        return 0;
+    }
+    constexpr int TT = 16, EB = 32;
+    const size_t smem = sizeof(float) * 4 * (EB * (128 + 16) + TT * 128);
+    cudaFuncSetAttribute(router_tile_kernel<TT, EB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem);
+    dim3 grid((a.T + TT - 1) / TT, (a.E + EB - 1) / EB);
+    router_tile_kernel<TT, EB><<<grid, kRouterThreads, smem, s>>>(
+        a.x, a.w, a.bias, a.T, a.H, a.E, a.logits, a.counters, a.k, a.min_weight, a.ids,
+        a.weights, a.err);
     return 0;
 }
 
