@@ -92,16 +92,18 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     return fn;
 }
 
-// 2-D map over an int8 row-major [rows][cols] buffer, box = 128 bytes x nt rows,
-// 128-byte swizzle (matches the MMA operand layout).
+// Tensor map over an int8 row-major [rows][cols] buffer viewed in 3-D as
+// (byte within a 128-byte k-block, row, k-block), box = 128 B x nt rows x kKPS
+// k-blocks, 128-byte swizzle: one copy lands the MMA operand tiles of all
+// k-blocks of a stage, each nt x 128 B and 1024-byte aligned.
 int make_act_map(CUtensorMap* map, const void* base, int rows, int cols, int nt) {
     auto enc = get_encode();
-    if (!enc) return MOE_B200_ERR_CUDA;
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)cols};
-    cuuint32_t box[2] = {128, (cuuint32_t)nt};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+    if (!enc || cols % kKAlign) return MOE_B200_ERR_CUDA;
+    cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)(cols / 128)};
+    cuuint64_t strides[2] = {(cuuint64_t)cols, 128};
+    cuuint32_t box[3] = {128, (cuuint32_t)nt, (cuuint32_t)kKPS};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides,
                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? MOE_B200_OK : MOE_B200_ERR_CUDA;
@@ -109,11 +111,13 @@ int make_act_map(CUtensorMap* map, const void* base, int rows, int cols, int nt)
 
 constexpr int kNTs[3] = {16, 32, 64};
 int nt_index(int nt) { return nt == 16 ? 0 : nt == 32 ? 1 : 2; }
-// Token tile (MMA N) from the expected rows per expert.
-int choose_nt(long rows, int experts) {
+// Token tile (MMA N) from the expected rows per expert; group-32 weights keep
+// four K=32 buffers per k-block in TMEM next to the unpacked weights, which
+// caps their tile at 32 tokens.
+int choose_nt(long rows, int experts, int fmt) {
     const long avg = experts > 0 ? (rows + experts - 1) / experts : rows;
     if (avg <= 16) return 16;
-    if (avg <= 32) return 32;
+    if (avg <= 32 || fmt == kFmtW4G32) return 32;
     return 64;
 }
 
@@ -149,43 +153,53 @@ inline int tile_channel(const PackedMat& m, int rt, int lr) {
 }
 
 // Packs one reference-layout matrix (codes [K][N], N = 2n for SwiGLU) into
-// tile-major device order. host_w / host_s point at this expert's slot.
+// tile-major device order. For each 128-row tile: stages of kKPS k-blocks,
+// each stage = the k-blocks' weight blocks followed (group-32) by their fp16
+// scales [4 groups][128 rows], so one bulk copy moves a whole stage.
+// host_w / host_s point at this expert's slot.
 void pack_expert(const PackedMat& m, const int8_t* codes, const float* scales,
                  const uint16_t* gscales, uint8_t* host_w, uint8_t* host_s) {
     const int K = m.k;
     const int N = m.swiglu ? 2 * m.n : m.n;
     const bool w4 = m.fmt != kFmtW8PC;
     const size_t tile_bytes = w4 ? 8192 : 16384;
+    const size_t stage_bytes = m.w_tile_stride / (m.kblocks / kKPS);
     for (int rt = 0; rt < m.row_tiles; ++rt) {
         for (int lr = 0; lr < 128; ++lr) {
             const int ch = tile_channel(m, rt, lr);
             for (int kb = 0; kb < m.kblocks; ++kb) {
-                uint8_t* tile = host_w + (size_t)rt * m.w_tile_stride + (size_t)kb * tile_bytes;
+                uint8_t* stage = host_w + (size_t)rt * m.w_tile_stride + (kb / kKPS) * stage_bytes;
+                uint8_t* tile = stage + (size_t)(kb % kKPS) * tile_bytes;
                 for (int kbyte = 0; kbyte < 128; ++kbyte) {
                     const int k = kb * 128 + kbyte;
                     const int8_t code = (ch >= 0 && k < K) ? codes[(size_t)k * N + ch] : 0;
-                    const size_t o = sw128(lr, kbyte);
                     if (!w4) {
-                        tile[o] = (uint8_t)code;
+                        // W8: the tensor core's 128-byte-swizzle K-major operand layout
+                        tile[sw128(lr, kbyte)] = (uint8_t)code;
                     } else {
-                        // int8 offset o comes from 32-bit packed word o/8: low nibbles
-                        // give bytes 0..3 of the 8, high nibbles bytes 4..7
-                        const size_t word = o / 8, within = o % 8;
-                        const size_t pb = word * 4 + (within & 3);
+                        // W4: row lr owns 64 bytes; 16-byte chunk c (k 32c..32c+31) sits
+                        // at chunk c ^ ((lr >> 1) & 3); byte b of word w holds k =
+                        // 32c+8w+b in its low nibble and k+4 in its high nibble
+                        const int c = kbyte / 32, w = (kbyte % 32) / 8, e = kbyte % 8;
+                        const size_t pb = (size_t)lr * 64 + ((c ^ ((lr >> 1) & 3)) * 16) + w * 4 + (e & 3);
                         const uint8_t nib = (uint8_t)code & 0xF;
-                        if (within < 4)
+                        if (e < 4)
                             tile[pb] = (uint8_t)((tile[pb] & 0xF0) | nib);
                         else
                             tile[pb] = (uint8_t)((tile[pb] & 0x0F) | (nib << 4));
                     }
                 }
+                if (m.fmt == kFmtW4G32) {
+                    uint16_t* st = reinterpret_cast<uint16_t*>(stage + kKPS * tile_bytes) +
+                                   (size_t)(kb % kKPS) * 4 * 128;
+                    for (int j = 0; j < 4; ++j) {
+                        const int g = kb * 4 + j;
+                        st[(size_t)j * 128 + lr] =
+                            (ch >= 0 && g * 32 < K) ? gscales[(size_t)g * N + ch] : (uint16_t)0;
+                    }
+                }
             }
-            if (m.fmt == kFmtW4G32) {
-                uint16_t* st = reinterpret_cast<uint16_t*>(host_s + (size_t)rt * m.s_tile_stride);
-                for (int g = 0; g < m.kblocks * 4; ++g)
-                    st[(size_t)g * 128 + lr] =
-                        (ch >= 0 && g * 32 < K) ? gscales[(size_t)g * N + ch] : (uint16_t)0;
-            } else {
+            if (m.fmt != kFmtW4G32) {
                 float* st = reinterpret_cast<float*>(host_s + (size_t)rt * m.s_tile_stride);
                 st[lr] = ch >= 0 ? scales[ch] : 0.0f;
             }
@@ -199,12 +213,13 @@ int setup_mat(PackedMat& m, int fmt, int experts, int K, int n, bool swiglu) {
     m.k = K;
     m.n = n;
     m.swiglu = swiglu;
-    m.kblocks = pad_to(K, 128) / 128;
+    m.kblocks = pad_to(K, kKAlign) / 128;
     m.row_tiles = swiglu ? (n + 63) / 64 : (n + 127) / 128;
     const size_t tile_bytes = fmt == kFmtW8PC ? 16384 : 8192;
-    m.w_tile_stride = (size_t)m.kblocks * tile_bytes;
+    const size_t stage_bytes = kKPS * (tile_bytes + (fmt == kFmtW4G32 ? 1024 : 0));
+    m.w_tile_stride = (size_t)(m.kblocks / kKPS) * stage_bytes;
     m.w_expert_stride = (size_t)m.row_tiles * m.w_tile_stride;
-    m.s_tile_stride = fmt == kFmtW4G32 ? (size_t)m.kblocks * 1024 : 512;
+    m.s_tile_stride = 512;  // per-channel f32 scales of one tile (group scales live in w)
     m.s_expert_stride = (size_t)m.row_tiles * m.s_tile_stride;
     return MOE_B200_OK;
 }
@@ -320,7 +335,7 @@ GemmArgs gemm_args(moe_b200_workspace* ws, const PackedMat& m, const float* act_
 int run_shared(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
                cudaStream_t s) {
     const int rule = w->shared_mode == MOE_B200_SHARED_JOINT ? kQuantMoe : kQuantDense;
-    const int nt = choose_nt(rows, 1);
+    const int nt = choose_nt(rows, 1, w->sgu.fmt);
     const CUtensorMap* amap = &ws->map_qx[nt_index(nt)];
     const float* ascale = ws->s_x;
     if (w->shared_mode != MOE_B200_SHARED_JOINT) {
@@ -380,7 +395,7 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
     launch_quant_gather(d_x, rows, H, ws->Kh, kQuantMoe, k, ws->pos, ws->q_x, ws->s_x, ws->a_perm,
                         ws->s_perm, ws->err, s);
     mark(3);
-    const int nt = choose_nt(n, E);
+    const int nt = choose_nt(n, E, w->gu.fmt);
     GemmArgs g = gemm_args(ws, w->gu, ws->s_perm, ws->offsets, E, n, ws->middle, I);
     if (launch_gemm(ws->map_a[nt_index(nt)], g, w->gu.fmt, kEpiSwiGLU, nt, ws->num_sms, s))
         return MOE_B200_ERR_UNSUPPORTED;
@@ -594,9 +609,9 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
                  ? (cfg->weights.shared_intermediate > 0 ? cfg->weights.shared_intermediate : ws->I)
                  : 0;
     ws->num_sms = sms;
-    ws->Kh = pad_to(ws->H, 128);
-    ws->Ki = pad_to(ws->I, 128);
-    ws->Kis = pad_to(ws->Is > 0 ? ws->Is : 32, 128);
+    ws->Kh = pad_to(ws->H, kKAlign);
+    ws->Ki = pad_to(ws->I, kKAlign);
+    ws->Kis = pad_to(ws->Is > 0 ? ws->Is : 32, kKAlign);
     const long T = ws->max_rows, n = T * ws->k;
     ws->n_max = n;
     const long nb = (n + kRouteChunk - 1) / kRouteChunk;

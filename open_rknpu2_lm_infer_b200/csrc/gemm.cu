@@ -12,34 +12,40 @@
 // columns instead of a 128-row M tile, and each epilogue thread owns a
 // channel whose per-group scale it reads once per group.
 //
-// Warp roles (384 threads):
-//   warp 0       producer: bulk copies of pre-swizzled weight blocks and
-//                scales, TMA tensor loads of the permuted activation rows,
-//                into a deep load ring (~100 KB in flight per SM)
+// Warp roles (704 threads):
+//   warp 0       producer: per load stage (kKPS k-blocks) one bulk copy of the
+//                weight blocks (+ group scales) and one 3-D TMA copy of the
+//                permuted activation rows. A copy request costs ~0.2 us per SM
+//                whatever its size, so a stage moves >= 16 KB per request.
 //   warp 1       TMEM allocator + single-thread MMA issuer
-//   warps 2..3   int4 -> int8 unpack from the load ring into a 3-deep
-//                operand ring (W4 formats)
-//   warps 4..11  epilogue, two warps per TMEM lane quadrant, each owning half
-//                of the token columns
+//   warps 2..5   W4 formats: unpack int4 -> int8 straight into tensor memory,
+//                one warp per TMEM lane quadrant, one weight row per thread;
+//                the MMA then reads its weight operand from TMEM (no shared
+//                memory operand, no proxy fence). W8: idle.
+//   warps 6..21  epilogue, four warps per TMEM lane quadrant, each owning a
+//                quarter of the token columns (the epilogue is latency-bound,
+//                so it gets the most warps)
 //
-// Group-32 formats: one MMA (K = 32 = one group) per TMEM buffer of a ring.
-// Every buffer is pre-filled with the bits of 12582912.0f (0x4B400000) and
-// the MMA accumulates into it, so the int32 result read back as a float is
-// exactly 12582912 + 16*acc (|16*acc| < 2^22). The epilogue then computes
-// f = fma(D - 12582912, s/16, f): an exact subtraction and one FMA, equal to
-// fma((float)acc, s, f) bit for bit, without an int->float conversion.
-// Per-channel formats: all of K accumulates in TMEM, one dequant per tile.
+// Group-32 formats: one MMA (K = 32 = one group) per TMEM buffer; the four
+// buffers of a k-block form a slot. Every buffer is pre-filled with the bits
+// of 12582912.0f (0x4B400000) and the MMA accumulates into it, so the int32
+// result read back as a float is exactly 12582912 + 16*acc (|16*acc| < 2^22).
+// The epilogue computes f = fma(D - 12582912, s/16, f): an exact subtraction
+// and one FMA, equal to fma((float)acc, s, f) bit for bit, without an
+// int->float conversion. Per-channel formats: all of K accumulates in TMEM,
+// one dequant per tile.
 #include "kernels.cuh"
 
 namespace moe {
 
-constexpr int kGemmThreads = 384;
-constexpr int kEpiWarp0 = 4;          // first epilogue warp
-constexpr int kEpiWarps = 8;
-constexpr int kConvWarps = 2;
+constexpr int kGemmThreads = 704;
+constexpr int kConvWarp0 = 2;         // first unpack warp
+constexpr int kConvWarps = 4;
+constexpr int kEpiWarp0 = 6;          // first epilogue warp
+constexpr int kEpiWarps = 16;
 constexpr int kScaleStages = 8;       // group-scale ring depth (k-blocks)
 constexpr int kTileRows = 128;        // weight rows per tile (MMA M)
-constexpr int kKBlock = 128;          // K bytes per stage (one 128B swizzle row)
+constexpr int kKBlock = 128;          // K bytes per k-block (one 128B swizzle row)
 constexpr uint32_t kMagicBits = 0x4B400000u;  // 12582912.0f
 constexpr float kMagic = 12582912.0f;
 
@@ -48,24 +54,30 @@ struct GemmCfg {
     static constexpr bool kW4 = (FMT == kFmtW4G32 || FMT == kFmtW4PC);
     static constexpr bool kGroup = (FMT == kFmtW4G32);
     static constexpr int kWBytes = kW4 ? kTileRows * kKBlock / 2 : kTileRows * kKBlock;
-    static constexpr int kActBytes = NT * kKBlock;
-    static constexpr int kOpBytes = kTileRows * kKBlock;     // MMA weight operand (16 KB)
-    // load stage: [activation rows][weight operand][packed int4 (W4)]
-    static constexpr int kLoadBytes = kActBytes + kOpBytes + (kW4 ? kWBytes : 0);
-    static constexpr int kBudget = 196 * 1024;
-    static constexpr int kFit = kBudget / kLoadBytes;
-    static constexpr int kLoadStages = kFit >= 8 ? 8 : kFit;
-    static constexpr int kScaleBytes = kGroup ? 4 * kTileRows * 2 : 0;  // 1 KB
-    // TMEM: group formats use slots of one k-block (4 group buffers of NT
-    // columns); per-channel formats use two tile accumulators.
+    static constexpr int kScaleBytes = kGroup ? 4 * kTileRows * 2 : 0;  // 1 KB per k-block
+    static constexpr int kActBytes = NT * kKBlock;           // per k-block
+    // weight request of one stage (HBM layout: kKPS weight blocks, then their scales)
+    static constexpr int kStageW = kKPS * (kWBytes + kScaleBytes);
+    // load stage: [activations kKPS x NT x 128][weights (+ scales)]; W8 weights
+    // are the MMA operand tiles, W4 weights are unpacked into TMEM.
+    static constexpr int kLoadBytes = kKPS * kActBytes + kStageW;
+    // TMEM: [W4 weight operand ring: kLoadStages x kKPS x 32 columns][accumulators]
+    static constexpr int kACols = 32;                        // one k-block of int8 weights
+    static constexpr int kLoadStages = kW4 ? 4 : ((200 * 1024) / kLoadBytes >= 6 ? 6
+                                                  : (200 * 1024) / kLoadBytes);
+    static constexpr int kARegion = kW4 ? kLoadStages * kKPS * kACols : 0;
+    // group formats: slots of one k-block (4 group buffers of NT columns);
+    // per-channel formats: two tile accumulators.
     static constexpr int kSlotCols = kGroup ? 4 * NT : NT;
-    static constexpr int kNSlot = kGroup ? ((512 / kSlotCols) < 4 ? (512 / kSlotCols) : 4) : 2;
-    static constexpr int kCols = kNSlot * kSlotCols;
-    static constexpr int kAllocCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128
-                                    : kCols <= 256 ? 256 : 512;
-    static constexpr int kHalf = NT / 2;                      // columns per epilogue warp
+    static constexpr int kAccFree = 512 - kARegion;
+    static constexpr int kNSlot = kGroup ? ((kAccFree / kSlotCols) < 4 ? (kAccFree / kSlotCols) : 4)
+                                         : 2;
+    static constexpr int kAllocCols = 512;
+    static constexpr int kHalf = NT / 4;                      // columns per epilogue warp
     static constexpr int kXchgStride = NT + 1;
-    static_assert(kLoadStages >= 4, "smem budget");
+    static_assert(kLoadStages >= 2, "smem budget");
+    static_assert(kNSlot >= 2, "TMEM budget: group formats need NT <= 32");
+    static_assert(kARegion + kNSlot * kSlotCols <= 512, "TMEM budget");
 };
 
 struct TileCoord {
@@ -103,14 +115,14 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + 64 * C::kXchgStride + 2);
     uint64_t* lfull = bars;           // TMA bytes of stage s landed
     uint64_t* lempty = lfull + SL;    // MMAs that read stage s completed
-    uint64_t* ofull = lempty + SL;    // int4 operand of stage s unpacked (W4)
+    uint64_t* ofull = lempty + SL;    // W4 operand of stage s unpacked into TMEM
     uint64_t* sfull = ofull + SL;
     uint64_t* sempty = sfull + kScaleStages;
     uint64_t* tfull = sempty + kScaleStages;
     uint64_t* tempty = tfull + C::kNSlot;
     uint64_t* done = tempty + C::kNSlot;
-    uint64_t* xfull = done + 1;    // up halves written (4 warps)
-    uint64_t* xempty = xfull + 1;  // gate halves read (4 warps)
+    uint64_t* xfull = done + 1;    // up values written (8 warps)
+    uint64_t* xempty = xfull + 1;  // gate warps done reading (8 warps)
     int* tcnt = reinterpret_cast<int*>(xempty + 1);
     int* tb = tcnt + a.num_experts + 1;
     __shared__ uint32_t tmem_base_s;
@@ -119,9 +131,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int E = a.num_experts;
-    auto act_at = [&](int s) { return load + s * C::kLoadBytes; };
-    auto op_at = [&](int s) { return load + s * C::kLoadBytes + C::kActBytes; };
-    auto packed_at = [&](int s) { return load + s * C::kLoadBytes + C::kActBytes + C::kOpBytes; };
+    // k-block j (< kKPS) of stage s
+    auto act_at = [&](int s, int j) { return load + s * C::kLoadBytes + j * C::kActBytes; };
+    auto w_at = [&](int s) { return load + s * C::kLoadBytes + kKPS * C::kActBytes; };
 
     if (threadIdx.x == 0) {
         abort_s = 0;
@@ -131,7 +143,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             mbar_init(&ofull[i], kConvWarps);
         }
         for (int i = 0; i < kScaleStages; ++i) {
-            mbar_init(&sfull[i], 1);
+            mbar_init(&sfull[i], kConvWarps);
             mbar_init(&sempty[i], kEpiWarps);
         }
         for (int i = 0; i < C::kNSlot; ++i) {
@@ -139,8 +151,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             mbar_init(&tempty[i], kEpiWarps);
         }
         mbar_init(done, 1);
-        mbar_init(xfull, 4);
-        mbar_init(xempty, 4);
+        mbar_init(xfull, kEpiWarps / 2);
+        mbar_init(xempty, kEpiWarps / 2);
         fence_barrier_init();
     }
     // tile table: tcnt[e] = token tiles of expert e, tb[e] = its first tile index
@@ -181,18 +193,18 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = tmem_base_s;
+    const uint32_t acc_base = tmem_base + C::kARegion;  // accumulator columns
     const int total = total_tiles_s;
     volatile int* abort_flag = &abort_s;
 
-    // epilogue geometry: quadrant = TMEM lanes, half = token columns
-    const int ew = warp - kEpiWarp0;
+    // lane quadrant of this warp's TMEM accesses
     const int quad = warp & 3;
-    const int half = ew >= 4 ? 1 : 0;
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+    const int half = (warp - kEpiWarp0) >> 2;  // epilogue column quarter (0..3)
     if (C::kGroup && warp >= kEpiWarp0) {
         // every group buffer starts as the float 12582912.0
         for (int b = 0; b < C::kNSlot * 4; ++b)
-            tmem_fill<C::kHalf>(tmem_base + lane_addr + b * NT + half * C::kHalf, kMagicBits);
+            tmem_fill<C::kHalf>(acc_base + lane_addr + b * NT + half * C::kHalf, kMagicBits);
         tmem_wait_st();
     }
     tc_fence_before();
@@ -202,38 +214,23 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            uint32_t it = 0;
+            const int kstages = a.kblocks / kKPS;
+            uint32_t it = 0;  // stage counter
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
                 const TileCoord c = decode_tile(t, tb, tcnt, E);
                 const int row0 = a.offsets[c.e] + c.mt * NT;
                 const uint8_t* wtile = a.w + (size_t)c.e * a.w_expert_stride +
                                        (size_t)c.rt * a.w_tile_stride;
-                const uint8_t* stile = reinterpret_cast<const uint8_t*>(a.wscale) +
-                                       (size_t)c.e * a.ws_expert_stride +
-                                       (size_t)c.rt * a.ws_tile_stride;
-                for (int kb = 0; kb < a.kblocks; ++kb, ++it) {
+                for (int st = 0; st < kstages; ++st, ++it) {
                     const int s = it % SL;
                     if (!mbar_wait(&lempty[s], ((it / SL) & 1u) ^ 1u, abort_flag, a.err)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&lfull[s], C::kWBytes + C::kActBytes);
-                    bulk_g2s(C::kW4 ? packed_at(s) : op_at(s), wtile + (size_t)kb * C::kWBytes,
-                             C::kWBytes, &lfull[s]);
-                    tma_load_2d(act_at(s), &act_map, kb * kKBlock, row0, &lfull[s]);
-                    if (C::kGroup) {
-                        const int ss = it % kScaleStages;
-                        if (!mbar_wait(&sempty[ss], ((it / kScaleStages) & 1u) ^ 1u, abort_flag,
-                                       a.err)) {
-                            ++it;  // the load stage above was issued
-                            ok = false;
-                            break;
-                        }
-                        mbar_arrive_expect_tx(&sfull[ss], C::kScaleBytes);
-                        bulk_g2s(scales + ss * C::kScaleBytes, stile + (size_t)kb * C::kScaleBytes,
-                                 C::kScaleBytes, &sfull[ss]);
-                    }
+                    mbar_arrive_expect_tx(&lfull[s], C::kStageW + kKPS * C::kActBytes);
+                    bulk_g2s(w_at(s), wtile + (size_t)st * C::kStageW, C::kStageW, &lfull[s]);
+                    tma_load_3d(act_at(s, 0), &act_map, 0, row0, st * kKPS, &lfull[s]);
                 }
             }
             // drain: every issued copy lands before the CTA can exit
@@ -243,11 +240,12 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        // Two tcgen05.commit per k-block at most (slot full, stage empty): the
-        // commit is the costly part of issuing, so groups share one.
+        // At most one tcgen05.commit per k-block (TMEM slot full) plus one per
+        // stage (stage empty): the commit is the costly part of issuing.
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_i8(kTileRows, NT);
-            uint32_t it = 0, ti = 0;
+            const int kstages = a.kblocks / kKPS;
+            uint32_t it = 0, kbc = 0, ti = 0;  // stage, k-block and tile counters
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++ti) {
                 uint32_t dcol = 0;
@@ -257,35 +255,42 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                     tc_fence_after();
                     dcol = buf * NT;
                 }
-                for (int kb = 0; kb < a.kblocks && ok; ++kb, ++it) {
+                for (int st = 0; st < kstages && ok; ++st, ++it) {
                     const int s = it % SL;
                     if (!mbar_wait(&lfull[s], (it / SL) & 1u, abort_flag, a.err) ||
                         (C::kW4 && !mbar_wait(&ofull[s], (it / SL) & 1u, abort_flag, a.err))) {
                         ok = false;
                         break;
                     }
-                    uint32_t slot = 0;
-                    if (C::kGroup) {
-                        slot = it % C::kNSlot;
-                        if (!mbar_wait(&tempty[slot], ((it / C::kNSlot) & 1u) ^ 1u, abort_flag,
-                                       a.err)) {
-                            ok = false;
-                            break;
-                        }
-                    }
-                    tc_fence_after();
-                    const uint32_t wa = smem_u32(op_at(s));
-                    const uint32_t ab = smem_u32(act_at(s));
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint64_t da = smem_desc_k_sw128(wa + 32 * j);
-                        const uint64_t db = smem_desc_k_sw128(ab + 32 * j);
-                        if (C::kGroup)
-                            mma_i8(tmem_base + slot * C::kSlotCols + j * NT, da, db, idesc, 1u);
-                        else
-                            mma_i8(tmem_base + dcol, da, db, idesc, (kb > 0 || j > 0) ? 1u : 0u);
+                    for (int jk = 0; jk < kKPS; ++jk, ++kbc) {
+                        uint32_t slot = 0;
+                        if (C::kGroup) {
+                            slot = kbc % C::kNSlot;
+                            if (!mbar_wait(&tempty[slot], ((kbc / C::kNSlot) & 1u) ^ 1u, abort_flag,
+                                           a.err)) {
+                                ok = false;
+                                break;
+                            }
+                        }
+                        tc_fence_after();
+                        const uint32_t ab = smem_u32(act_at(s, jk));
+                        const uint32_t a_tmem = tmem_base + (s * kKPS + jk) * C::kACols;
+                        const uint32_t wa = smem_u32(w_at(s) + jk * C::kWBytes);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const uint64_t db = smem_desc_k_sw128(ab + 32 * j);
+                            const uint32_t d = C::kGroup ? acc_base + slot * C::kSlotCols + j * NT
+                                                         : acc_base + dcol;
+                            const uint32_t acc = C::kGroup ? 1u : ((st > 0 || jk > 0 || j > 0) ? 1u : 0u);
+                            if (C::kW4)
+                                mma_i8_ts(d, a_tmem + 8 * j, db, idesc, acc);
+                            else
+                                mma_i8(d, smem_desc_k_sw128(wa + 32 * j), db, idesc, acc);
+                        }
+                        if (C::kGroup) mma_commit(&tfull[slot]);
                     }
-                    if (C::kGroup) mma_commit(&tfull[slot]);
+                    if (!ok) break;
                     mma_commit(&lempty[s]);
                 }
                 if (!C::kGroup && ok) mma_commit(&tfull[ti % 2u]);
@@ -298,40 +303,66 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     } else if (warp < kEpiWarp0) {
         // ------------------------------------------------------------ int4 unpack
         if (C::kW4) {
-            const int ct = threadIdx.x - 64;  // 0 .. 32*kConvWarps-1
-            uint32_t it = 0;
+            const int r = quad * 32 + lane;  // weight row = TMEM lane
+            const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..127
+            const int kstages = a.kblocks / kKPS;
+            uint32_t it = 0, kbc = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                for (int kb = 0; kb < a.kblocks; ++kb, ++it) {
+                for (int st = 0; st < kstages && ok; ++st, ++it) {
                     // the producer refilled stage s only after the MMAs that read its
-                    // previous operand completed, so the operand slot is free here
+                    // previous operands completed, so the TMEM operand slot is free
                     const int s = it % SL;
                     if (!mbar_wait(&lfull[s], (it / SL) & 1u, abort_flag, a.err)) {
                         ok = false;
                         break;
                     }
-                    const uint2* src = reinterpret_cast<const uint2*>(packed_at(s));
-                    uint4* dst = reinterpret_cast<uint4*>(op_at(s));
-                    constexpr int kPer = C::kWBytes / 8 / (32 * kConvWarps);
-                    // all loads first: the compiler cannot prove src and dst apart,
-                    // so interleaving would serialise every load behind a store
-                    uint2 p[kPer];
 #pragma unroll
-                    for (int i = 0; i < kPer; ++i) p[i] = src[ct + 32 * kConvWarps * i];
+                    for (int jk = 0; jk < kKPS; ++jk) {
+                        // row r of the k-block: 64 bytes in four 16-byte chunks,
+                        // chunk c stored at position c ^ ((r >> 1) & 3) (conflict-free)
+                        const uint8_t* rowp = w_at(s) + jk * C::kWBytes + r * 64;
+                        uint32_t o[32];
 #pragma unroll
-                    for (int i = 0; i < kPer; ++i) {
-                        // packed byte b holds element b (low nibble) and b+4 (high
-                        // nibble) of an 8-element run; each lands as 16 * value.
-                        uint4 v;
-                        v.x = (p[i].x << 4) & 0xF0F0F0F0u;
-                        v.y = p[i].x & 0xF0F0F0F0u;
-                        v.z = (p[i].y << 4) & 0xF0F0F0F0u;
-                        v.w = p[i].y & 0xF0F0F0F0u;
-                        dst[ct + 32 * kConvWarps * i] = v;
+                        for (int c = 0; c < 4; ++c) {
+                            const uint4 p =
+                                *reinterpret_cast<const uint4*>(rowp + ((c ^ ((r >> 1) & 3)) << 4));
+                            // packed byte b of word w holds k = 32c+8w+b (low nibble) and
+                            // k + 4 (high nibble); each lands as 16 * value.
+                            o[8 * c + 0] = (p.x << 4) & 0xF0F0F0F0u;
+                            o[8 * c + 1] = p.x & 0xF0F0F0F0u;
+                            o[8 * c + 2] = (p.y << 4) & 0xF0F0F0F0u;
+                            o[8 * c + 3] = p.y & 0xF0F0F0F0u;
+                            o[8 * c + 4] = (p.z << 4) & 0xF0F0F0F0u;
+                            o[8 * c + 5] = p.z & 0xF0F0F0F0u;
+                            o[8 * c + 6] = (p.w << 4) & 0xF0F0F0F0u;
+                            o[8 * c + 7] = p.w & 0xF0F0F0F0u;
+                        }
+                        tmem_st32(tmem_base + lane_addr + (s * kKPS + jk) * C::kACols, o);
                     }
-                    fence_proxy_async_smem();
+                    tmem_wait_st();
+                    tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&ofull[s]);
+                    if (C::kGroup) {
+                        // hand the stage's group scales to the epilogue (1 KB per k-block)
+                        const uint2* ssrc = reinterpret_cast<const uint2*>(w_at(s) + kKPS * C::kWBytes);
+#pragma unroll
+                        for (int jk = 0; jk < kKPS; ++jk, ++kbc) {
+                            const int ss = kbc % kScaleStages;
+                            if (!mbar_wait(&sempty[ss], ((kbc / kScaleStages) & 1u) ^ 1u, abort_flag,
+                                           a.err)) {
+                                ok = false;
+                                break;
+                            }
+                            static_assert(C::kScaleBytes == 8 * 32 * kConvWarps || !C::kGroup,
+                                          "one 8-byte piece of the scales per unpack thread");
+                            reinterpret_cast<uint2*>(scales + ss * C::kScaleBytes)[ct] =
+                                ssrc[jk * (C::kScaleBytes / 8) + ct];
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&sfull[ss]);
+                        }
+                    }
                 }
             }
         }
@@ -357,10 +388,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                 col = c.rt * kTileRows + r;
             }
             const bool col_ok = col < a.n_valid;
-            float sx[C::kHalf];
-#pragma unroll
-            for (int q = 0; q < C::kHalf; ++q)
-                sx[q] = (c0 + q < nvalid) ? a.act_scale[row0 + c0 + q] : 0.0f;
+            // lane q prefetches the scale of token column c0 + q (one register across
+            // the K loop); the values are broadcast by shuffles at the tile end
+            const float my_sx = (lane < C::kHalf && c0 + lane < nvalid) ? a.act_scale[row0 + c0 + lane]
+                                                                        : 0.0f;
             float wscale_pc = 0.0f;
             if (!C::kGroup) {
                 const float* sp = reinterpret_cast<const float*>(
@@ -385,33 +416,27 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                     for (int j = 0; j < 4; ++j) sg[j] = __half2float(sc[j * kTileRows + r]);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&sempty[ss]);
-                    // one TMEM slot per k-block: wait once, then GB groups per round
-                    // trip (loads, one wait, re-arm, one wait)
-                    constexpr int GB = C::kHalf <= 16 ? 4 : 2;
+                    // one TMEM slot per k-block: wait once, load its four group
+                    // buffers, start re-arming them, do the math while the stores
+                    // drain, then release the slot
                     const uint32_t slot = it % C::kNSlot;
                     if (!mbar_wait(&tfull[slot], (it / C::kNSlot) & 1u, abort_flag, a.err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t sbase = tmem_base + lane_addr + slot * C::kSlotCols + c0;
+                    const uint32_t sbase = acc_base + lane_addr + slot * C::kSlotCols + c0;
+                    // two rounds of two groups: load, re-arm (stores drain meanwhile), math
 #pragma unroll
-                    for (int j0 = 0; j0 < 4; j0 += GB) {
-                        uint32_t v[GB][C::kHalf];
+                    for (int j0 = 0; j0 < 4; j0 += 2) {
+                        uint32_t v[2][C::kHalf];
 #pragma unroll
-                        for (int jj = 0; jj < GB; ++jj) tmem_ld<C::kHalf>(sbase + (j0 + jj) * NT, v[jj]);
+                        for (int jj = 0; jj < 2; ++jj) tmem_ld<C::kHalf>(sbase + (j0 + jj) * NT, v[jj]);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int jj = 0; jj < GB; ++jj)  // re-arm for the next MMAs
-                            tmem_fill<C::kHalf>(sbase + (j0 + jj) * NT, kMagicBits);
-                        if (j0 + GB == 4) {
-                            tmem_wait_st();
-                            tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&tempty[slot]);
-                        }
+                        for (int jj = 0; jj < 2; ++jj) tmem_fill<C::kHalf>(sbase + (j0 + jj) * NT, kMagicBits);
 #pragma unroll
-                        for (int jj = 0; jj < GB; ++jj) {
+                        for (int jj = 0; jj < 2; ++jj) {
                             const int j = j0 + jj;
                             if (EPI == kEpiAcc) {
                                 const int g = kb * 4 + j;
@@ -435,6 +460,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                             }
                         }
                     }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[slot]);
                 }
                 if (!ok) break;
             } else {
@@ -442,7 +471,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                 if (!mbar_wait(&tfull[buf], (ti / 2u) & 1u, abort_flag, a.err)) break;
                 tc_fence_after();
                 uint32_t v[C::kHalf];
-                tmem_ld<C::kHalf>(tmem_base + lane_addr + buf * NT + c0, v);
+                tmem_ld<C::kHalf>(acc_base + lane_addr + buf * NT + c0, v);
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
@@ -467,10 +496,11 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             float val[C::kHalf];
 #pragma unroll
             for (int q = 0; q < C::kHalf; ++q) {
+                const float sxq = __shfl_sync(0xffffffffu, my_sx, q);
                 if (C::kGroup)
-                    val[q] = __fmul_rn(facc[q], sx[q]);
+                    val[q] = __fmul_rn(facc[q], sxq);
                 else
-                    val[q] = __fmul_rn(__fmul_rn(facc[q], sx[q]), wscale_pc);
+                    val[q] = __fmul_rn(__fmul_rn(facc[q], sxq), wscale_pc);
             }
             if (EPI == kEpiSwiGLU) {
                 // up lanes (64..127) hand their values to the gate lanes of the same channel
@@ -486,12 +516,11 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
 #pragma unroll
                     for (int q = 0; q < C::kHalf; ++q) {
                         const int j = c0 + q;
-                        if (j < nvalid) {
+                        if (j < nvalid && col_ok) {
                             const float gv = val[q];
                             const float uv = xchg[r * C::kXchgStride + j];
                             const float d = __fadd_rn(1.0f, expf(-gv));
-                            const float m = __fmul_rn(__fdiv_rn(gv, d), uv);
-                            if (col_ok) a.out[(size_t)(row0 + j) * a.ldo + col] = m;
+                            a.out[(size_t)(row0 + j) * a.ldo + col] = __fmul_rn(__fdiv_rn(gv, d), uv);
                         }
                     }
                     __syncwarp();
@@ -523,7 +552,7 @@ static size_t gemm_smem_bytes(int E) {
     b += sizeof(float) * (64 * C::kXchgStride + 2);
     b += sizeof(uint64_t) * (3 * C::kLoadStages + 2 * kScaleStages + 2 * C::kNSlot + 3);
     b += sizeof(int) * (2 * (size_t)E + 2);
-    // one CTA per SM: the kernel allocates up to 512 TMEM columns
+    // one CTA per SM: the kernel allocates all 512 TMEM columns
     return b < 120 * 1024 ? 120 * 1024 : b;
 }
 
@@ -546,7 +575,9 @@ static int launch_gemm_nt(const CUtensorMap& map, const GemmArgs& a, int nt, int
     switch (nt) {
         case 16: return launch_gemm_t<FMT, EPI, 16>(map, a, num_sms, s);
         case 32: return launch_gemm_t<FMT, EPI, 32>(map, a, num_sms, s);
-        case 64: return launch_gemm_t<FMT, EPI, 64>(map, a, num_sms, s);
+        case 64:
+            if constexpr (FMT != kFmtW4G32) return launch_gemm_t<FMT, EPI, 64>(map, a, num_sms, s);
+            return -1;
         default: return -1;
     }
 }

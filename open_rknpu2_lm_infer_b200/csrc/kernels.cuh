@@ -72,4 +72,10 @@ void launch_combine(const float* y, const int32_t* pos, const float* routes, con
 
 constexpr int kRouteChunk = 512;  // assignments per route_count / route_scatter CTA
 
+// K-blocks (128 bytes of K each) per GEMM load stage: one bulk copy brings the
+// stage's weights (and group scales), one 3-D tensor copy its activations.
+// A copy request costs a fixed ~0.2 us per SM, so stages move >= 16 KB.
+constexpr int kKPS = 2;
+constexpr int kKAlign = 128 * kKPS;  // K padding of weights and activation rows
+
 }  // namespace moe
