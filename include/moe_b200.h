@@ -99,7 +99,7 @@ typedef struct {
 /* Replaces rk_npu_moe_w8_timings (fields read at src/npu/moe.rs:342-351).
  * Filled from CUDA events: input_us = activation quantisation, schedule_us =
  * route histogram + permutation, gather_us = row gather, gate_us = gate/up
- * GEMM + SwiGLU, middle_cpu_us = middle requantisation, down_us = down GEMM,
+ * GEMM, middle_cpu_us = SwiGLU + middle requantisation, down_us = down GEMM,
  * combine_us = weighted combine (+ shared + residual), build_us = shared
  * expert, total_us = whole call. Counters are work items of the launch. */
 typedef struct {
@@ -187,8 +187,9 @@ int moe_b200_route_device(moe_b200_workspace *ws, const moe_b200_router *r, int3
 int moe_b200_workspace_status(moe_b200_workspace *ws);
 
 /* Device address and size of a workspace buffer, for inspection by tests:
- * "q_x","s_x","perm","pos","offsets","a_perm","s_perm","middle","rowmax",
- * "q_m","s_m","y","shared_y","logits". Valid until the next call. */
+ * "q_x","s_x","perm","pos","offsets","a_perm","s_perm","gate_up" (f32
+ * [rows][2I]: dequantised gate then up, before SwiGLU),"q_m","s_m","y",
+ * "shared_y","logits","ids","routes". Valid until the next call. */
 int moe_b200_workspace_buffer(moe_b200_workspace *ws, const char *name, void **d_ptr,
                               uint64_t *bytes);
 

@@ -153,17 +153,18 @@ inline int tile_channel(const PackedMat& m, int rt, int lr) {
 }
 
 // Packs one reference-layout matrix (codes [K][N], N = 2n for SwiGLU) into
-// tile-major device order. For each 128-row tile: stages of kKPS k-blocks,
-// each stage = the k-blocks' weight blocks followed (group-32) by their fp16
-// scales [4 groups][128 rows], so one bulk copy moves a whole stage.
-// host_w / host_s point at this expert's slot.
+// tile-major device order. For each 128-row tile: stages of kKPS k-blocks of
+// weights, so one bulk copy moves a whole stage. Scales: per-channel formats
+// f32 [128] per tile; group-32 fp16 [stage][row][kKPS k-blocks][4 groups],
+// 16 bytes per row and stage (one vector load for the epilogue thread of
+// that row). host_w / host_s point at this expert's slot.
 void pack_expert(const PackedMat& m, const int8_t* codes, const float* scales,
                  const uint16_t* gscales, uint8_t* host_w, uint8_t* host_s) {
     const int K = m.k;
     const int N = m.swiglu ? 2 * m.n : m.n;
     const bool w4 = m.fmt != kFmtW8PC;
     const size_t tile_bytes = w4 ? 8192 : 16384;
-    const size_t stage_bytes = m.w_tile_stride / (m.kblocks / kKPS);
+    const size_t stage_bytes = kKPS * tile_bytes;
     for (int rt = 0; rt < m.row_tiles; ++rt) {
         for (int lr = 0; lr < 128; ++lr) {
             const int ch = tile_channel(m, rt, lr);
@@ -190,12 +191,12 @@ void pack_expert(const PackedMat& m, const int8_t* codes, const float* scales,
                     }
                 }
                 if (m.fmt == kFmtW4G32) {
-                    uint16_t* st = reinterpret_cast<uint16_t*>(stage + kKPS * tile_bytes) +
-                                   (size_t)(kb % kKPS) * 4 * 128;
+                    uint16_t* st = reinterpret_cast<uint16_t*>(host_s + (size_t)rt * m.s_tile_stride +
+                                                               (size_t)(kb / kKPS) * 128 * kKPS * 8) +
+                                   (size_t)lr * kKPS * 4 + (kb % kKPS) * 4;
                     for (int j = 0; j < 4; ++j) {
                         const int g = kb * 4 + j;
-                        st[(size_t)j * 128 + lr] =
-                            (ch >= 0 && g * 32 < K) ? gscales[(size_t)g * N + ch] : (uint16_t)0;
+                        st[j] = (ch >= 0 && g * 32 < K) ? gscales[(size_t)g * N + ch] : (uint16_t)0;
                     }
                 }
             }
@@ -216,10 +217,11 @@ int setup_mat(PackedMat& m, int fmt, int experts, int K, int n, bool swiglu) {
     m.kblocks = pad_to(K, kKAlign) / 128;
     m.row_tiles = swiglu ? (n + 63) / 64 : (n + 127) / 128;
     const size_t tile_bytes = fmt == kFmtW8PC ? 16384 : 8192;
-    const size_t stage_bytes = kKPS * (tile_bytes + (fmt == kFmtW4G32 ? 1024 : 0));
-    m.w_tile_stride = (size_t)(m.kblocks / kKPS) * stage_bytes;
+    const size_t stages = (size_t)(m.kblocks / kKPS);
+    m.w_tile_stride = stages * kKPS * tile_bytes;
     m.w_expert_stride = (size_t)m.row_tiles * m.w_tile_stride;
-    m.s_tile_stride = 512;  // per-channel f32 scales of one tile (group scales live in w)
+    // group-32: fp16 [stage][128 rows][kKPS][4]; per-channel: f32 [128]
+    m.s_tile_stride = fmt == kFmtW4G32 ? stages * 128 * kKPS * 8 : 512;
     m.s_expert_stride = (size_t)m.row_tiles * m.s_tile_stride;
     return MOE_B200_OK;
 }
@@ -262,7 +264,7 @@ struct moe_b200_workspace {
     int8_t* a_perm = nullptr;
     float* s_perm = nullptr;
     // routed experts
-    float* middle = nullptr;
+    float* gate_up = nullptr;  // dequantised gate | up rows [n][2I]
     int8_t* q_m = nullptr;
     float *s_m = nullptr, *y = nullptr;
     // shared expert
@@ -344,8 +346,8 @@ int run_shared(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, cons
         amap = &ws->map_qxd[nt_index(nt)];
         ascale = ws->s_xd;
     }
-    GemmArgs g = gemm_args(ws, w->sgu, ascale, ws->shared_offsets, 1, rows, ws->s_middle, w->Is);
-    if (launch_gemm(*amap, g, w->sgu.fmt, kEpiSwiGLU, nt, ws->num_sms, s)) return MOE_B200_ERR_UNSUPPORTED;
+    GemmArgs g = gemm_args(ws, w->sgu, ascale, ws->shared_offsets, 1, rows, ws->s_middle, 2 * w->Is);
+    if (launch_gemm(*amap, g, w->sgu.fmt, kEpiGateUp, nt, ws->num_sms, s)) return MOE_B200_ERR_UNSUPPORTED;
     launch_requant(ws->s_middle, ws->shared_offsets + 1, rows, w->Is, ws->Kis, rule, ws->sq_m,
                    ws->ss_m, s);
     GemmArgs d = gemm_args(ws, w->sdn, ws->ss_m, ws->shared_offsets, 1, rows, ws->s_y, ws->H);
@@ -396,11 +398,11 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
                         ws->s_perm, ws->err, s);
     mark(3);
     const int nt = choose_nt(n, E, w->gu.fmt);
-    GemmArgs g = gemm_args(ws, w->gu, ws->s_perm, ws->offsets, E, n, ws->middle, I);
-    if (launch_gemm(ws->map_a[nt_index(nt)], g, w->gu.fmt, kEpiSwiGLU, nt, ws->num_sms, s))
+    GemmArgs g = gemm_args(ws, w->gu, ws->s_perm, ws->offsets, E, n, ws->gate_up, 2 * I);
+    if (launch_gemm(ws->map_a[nt_index(nt)], g, w->gu.fmt, kEpiGateUp, nt, ws->num_sms, s))
         return MOE_B200_ERR_UNSUPPORTED;
     mark(4);
-    launch_requant(ws->middle, ws->offsets + E, (int)n, I, ws->Ki, kQuantMoe, ws->q_m, ws->s_m, s);
+    launch_requant(ws->gate_up, ws->offsets + E, (int)n, I, ws->Ki, kQuantMoe, ws->q_m, ws->s_m, s);
     mark(5);
     GemmArgs d = gemm_args(ws, w->dn, ws->s_m, ws->offsets, E, n, ws->y, H);
     if (launch_gemm(ws->map_qm[nt_index(nt)], d, w->dn.fmt, kEpiStore, nt, ws->num_sms, s))
@@ -632,7 +634,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     rc |= ws_alloc(ws, &ws->counters, T);
     rc |= ws_alloc(ws, &ws->a_perm, (n + pad_rows) * ws->Kh);
     rc |= ws_alloc(ws, &ws->s_perm, n);
-    rc |= ws_alloc(ws, &ws->middle, n * ws->I);
+    rc |= ws_alloc(ws, &ws->gate_up, n * 2 * ws->I);
     rc |= ws_alloc(ws, &ws->q_m, (n + pad_rows) * ws->Ki);
     rc |= ws_alloc(ws, &ws->s_m, n);
     rc |= ws_alloc(ws, &ws->y, n * ws->H);
@@ -641,7 +643,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     if (ws->Is > 0 && rc == MOE_B200_OK) {
         rc |= ws_alloc(ws, &ws->q_xd, (T + pad_rows) * ws->Kh);
         rc |= ws_alloc(ws, &ws->s_xd, T);
-        rc |= ws_alloc(ws, &ws->s_middle, T * ws->Is);
+        rc |= ws_alloc(ws, &ws->s_middle, T * 2 * ws->Is);
         rc |= ws_alloc(ws, &ws->sq_m, (T + pad_rows) * ws->Kis);
         rc |= ws_alloc(ws, &ws->ss_m, T);
         rc |= ws_alloc(ws, &ws->s_y, T * ws->H);
@@ -903,7 +905,7 @@ int moe_b200_workspace_buffer(moe_b200_workspace* ws, const char* name, void** d
         {"offsets", ws->offsets, sizeof(int32_t) * (uint64_t)(ws->E + 1)},
         {"a_perm", ws->a_perm, (uint64_t)n * ws->Kh},
         {"s_perm", ws->s_perm, sizeof(float) * (uint64_t)n},
-        {"middle", ws->middle, sizeof(float) * (uint64_t)n * ws->I},
+        {"gate_up", ws->gate_up, sizeof(float) * (uint64_t)n * 2 * ws->I},
         {"q_m", ws->q_m, (uint64_t)n * ws->Ki},
         {"s_m", ws->s_m, sizeof(float) * (uint64_t)n},
         {"y", ws->y, sizeof(float) * (uint64_t)n * ws->H},

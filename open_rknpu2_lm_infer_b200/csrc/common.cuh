@@ -204,6 +204,16 @@ __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// The registers a tcgen05.ld writes hold their values only after
+// tcgen05.wait::ld, but the compiler sees them as outputs of the load itself
+// and may schedule arithmetic on them before the wait. Passing each register
+// through an empty volatile asm after the wait pins every use behind it.
+template <int N>
+__device__ __forceinline__ void tmem_ld_pin(uint32_t (&r)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 // 32 lanes x 8 columns of 32-bit: thread i gets lane (base+i), 8 columns.
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
     asm volatile(

@@ -2,7 +2,7 @@
 //   route_count / route_scatter : stable grouping of assignments by expert
 //   quant_gather                : dynamic per-token int8 quantisation, written
 //                                 straight into the permuted GEMM operand
-//   requant                     : SwiGLU middle -> int8 for the down GEMM
+//   requant                     : gate | up -> SwiGLU middle -> int8 for the down GEMM
 //   combine                     : routing-weighted sum (+ shared, + residual)
 //
 // Reference semantics (happyme531/open_rknpu2_lm_infer):
@@ -229,23 +229,39 @@ quant_gather_kernel(const float* __restrict__ x, int H, int ld_q, int rule, int 
     }
 }
 
-// One CTA (128 threads) per permuted row; rows >= *count exit. Reads the
-// SwiGLU row once (V float4 per thread), takes its max |m|, quantises.
+// SwiGLU of x86 native/cpu_kernels/swiglu.cpp:23-25 with the gate/up split of
+// Cpu::swiglu (src/model/cpu.rs:269-294): h = (g / (1 + exp(-g))) * u, IEEE
+// division and multiply (no contraction).
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    const float d = __fadd_rn(1.0f, expf(-g));
+    return __fmul_rn(__fdiv_rn(g, d), u);
+}
+
+// One CTA (128 threads) per permuted row; rows >= *count exit. Reads the row's
+// gate | up halves once (V float4 of each per thread), applies SwiGLU, takes
+// the max |h|, quantises.
 template <int V>
 __global__ void __launch_bounds__(128)
-requant_kernel(const float* __restrict__ mid, const int32_t* __restrict__ count, int I, int ld_q,
-               int rule, int8_t* q, float* sc) {
+requant_kernel(const float* __restrict__ gate_up, const int32_t* __restrict__ count, int I,
+               int ld_q, int rule, int8_t* q, float* sc) {
     __shared__ float red[4];
     const int row = blockIdx.x;
     if (row >= *count) return;
-    const float4* mr = reinterpret_cast<const float4*>(mid + (size_t)row * I);
+    const float4* gr = reinterpret_cast<const float4*>(gate_up + (size_t)row * 2 * I);
+    const float4* ur = reinterpret_cast<const float4*>(gate_up + (size_t)row * 2 * I + I);
     const int n4 = I / 4;
     float4 v[V];
     float m = 0.0f;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
         const int c = threadIdx.x + 128 * i;
-        v[i] = c < n4 ? mr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c < n4) {
+            const float4 g = gr[c], u = ur[c];
+            v[i] = make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z),
+                               silu_mul(g.w, u.w));
+        } else {
+            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         m = fmaxf(m, amax4(v[i]));
     }
     m = block_max(m, red);
@@ -338,11 +354,11 @@ void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k
 #undef QG
 }
 
-void launch_requant(const float* mid, const int32_t* count, int max_rows, int I, int ld_q,
+void launch_requant(const float* gate_up, const int32_t* count, int max_rows, int I, int ld_q,
                     int rule, int8_t* q, float* sc, cudaStream_t s) {
     if (max_rows == 0) return;
     const int v = (I / 4 + 127) / 128;
-#define RQ(V) requant_kernel<V><<<max_rows, 128, 0, s>>>(mid, count, I, ld_q, rule, q, sc)
+#define RQ(V) requant_kernel<V><<<max_rows, 128, 0, s>>>(gate_up, count, I, ld_q, rule, q, sc)
     if (v <= 1) RQ(1);
     else if (v <= 2) RQ(2);
     else if (v <= 4) RQ(4);

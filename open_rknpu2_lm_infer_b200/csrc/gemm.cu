@@ -22,30 +22,34 @@
 //                one warp per TMEM lane quadrant, one weight row per thread;
 //                the MMA then reads its weight operand from TMEM (no shared
 //                memory operand, no proxy fence). W8: idle.
-//   warps 6..21  epilogue, four warps per TMEM lane quadrant, each owning a
-//                quarter of the token columns (the epilogue is latency-bound,
-//                so it gets the most warps)
+//   warps 6..13  epilogue, two warps per TMEM lane quadrant, each owning half
+//                of the token columns. The epilogue shares each SM sub-partition
+//                with an unpack warp, so it is kept to few instructions per value.
 //
 // Group-32 formats: one MMA (K = 32 = one group) per TMEM buffer; the four
-// buffers of a k-block form a slot. Every buffer is pre-filled with the bits
-// of 12582912.0f (0x4B400000) and the MMA accumulates into it, so the int32
-// result read back as a float is exactly 12582912 + 16*acc (|16*acc| < 2^22).
-// The epilogue computes f = fma(D - 12582912, s/16, f): an exact subtraction
-// and one FMA, equal to fma((float)acc, s, f) bit for bit, without an
-// int->float conversion. Per-channel formats: all of K accumulates in TMEM,
+// buffers of a k-block form a slot. Every buffer holds the bits of 12582912.0f
+// (0x4B400000) before its MMA, which adds the int32 sum to them, so the result
+// read back as a float is exactly 12582912 + 16*acc (|16*acc| < 2^22). The
+// epilogue re-arms the buffers right after loading them and computes
+// f = fma(D - 12582912, s/16, f) two values per instruction (f32x2): an exact
+// subtraction and one FMA, equal to fma((float)acc, s, f) bit for bit. Per-channel formats: all of K accumulates in TMEM,
 // one dequant per tile.
 #include "kernels.cuh"
 
 namespace moe {
 
-constexpr int kGemmThreads = 704;
+constexpr int kGemmThreads = 448;
 constexpr int kConvWarp0 = 2;         // first unpack warp
 constexpr int kConvWarps = 4;
 constexpr int kEpiWarp0 = 6;          // first epilogue warp
-constexpr int kEpiWarps = 16;
-constexpr int kScaleStages = 8;       // group-scale ring depth (k-blocks)
+constexpr int kEpiWarps = 8;
 constexpr int kTileRows = 128;        // weight rows per tile (MMA M)
 constexpr int kKBlock = 128;          // K bytes per k-block (one 128B swizzle row)
+// Shared memory: the load ring gets what is left of 227 KB after the tile
+// tables (up to 1024 experts), barriers and the 1 KB alignment slack.
+constexpr int kSmemTotal = 227 * 1024;
+constexpr int kSmemFixed = 10 * 1024;
+constexpr int kMaxLoadStages = 8;
 constexpr uint32_t kMagicBits = 0x4B400000u;  // 12582912.0f
 constexpr float kMagic = 12582912.0f;
 
@@ -54,18 +58,20 @@ struct GemmCfg {
     static constexpr bool kW4 = (FMT == kFmtW4G32 || FMT == kFmtW4PC);
     static constexpr bool kGroup = (FMT == kFmtW4G32);
     static constexpr int kWBytes = kW4 ? kTileRows * kKBlock / 2 : kTileRows * kKBlock;
-    static constexpr int kScaleBytes = kGroup ? 4 * kTileRows * 2 : 0;  // 1 KB per k-block
     static constexpr int kActBytes = NT * kKBlock;           // per k-block
-    // weight request of one stage (HBM layout: kKPS weight blocks, then their scales)
-    static constexpr int kStageW = kKPS * (kWBytes + kScaleBytes);
-    // load stage: [activations kKPS x NT x 128][weights (+ scales)]; W8 weights
-    // are the MMA operand tiles, W4 weights are unpacked into TMEM.
+    static constexpr int kStageW = kKPS * kWBytes;           // weight request of one stage
+    // load stage: [activations kKPS x NT x 128][weights]; W8 weights are the MMA
+    // operand tiles, W4 weights are unpacked into TMEM.
     static constexpr int kLoadBytes = kKPS * kActBytes + kStageW;
-    // TMEM: [W4 weight operand ring: kLoadStages x kKPS x 32 columns][accumulators]
+    static constexpr int kLoadBudget = kSmemTotal - kSmemFixed;
+    static constexpr int kLoadStages = kLoadBudget / kLoadBytes > kMaxLoadStages
+                                           ? kMaxLoadStages : kLoadBudget / kLoadBytes;
+    // TMEM: [W4 weight operand ring: kAStages x kKPS x 32 columns][accumulators].
+    // The operand ring is shallower than the load ring: unpacking is quick,
+    // while HBM latency needs many stages of loads in flight.
     static constexpr int kACols = 32;                        // one k-block of int8 weights
-    static constexpr int kLoadStages = kW4 ? 4 : ((200 * 1024) / kLoadBytes >= 6 ? 6
-                                                  : (200 * 1024) / kLoadBytes);
-    static constexpr int kARegion = kW4 ? kLoadStages * kKPS * kACols : 0;
+    static constexpr int kAStages = kW4 ? (kGroup ? 2 : 4) : 0;
+    static constexpr int kARegion = kAStages * kKPS * kACols;
     // group formats: slots of one k-block (4 group buffers of NT columns);
     // per-channel formats: two tile accumulators.
     static constexpr int kSlotCols = kGroup ? 4 * NT : NT;
@@ -73,11 +79,12 @@ struct GemmCfg {
     static constexpr int kNSlot = kGroup ? ((kAccFree / kSlotCols) < 4 ? (kAccFree / kSlotCols) : 4)
                                          : 2;
     static constexpr int kAllocCols = 512;
-    static constexpr int kHalf = NT / 4;                      // columns per epilogue warp
-    static constexpr int kXchgStride = NT + 1;
+    static constexpr int kHalf = NT / 2;                      // columns per epilogue warp
     static_assert(kLoadStages >= 2, "smem budget");
+    static_assert(kLoadStages >= kAStages, "operand ring reuse is ordered by the load ring");
     static_assert(kNSlot >= 2, "TMEM budget: group formats need NT <= 32");
     static_assert(kARegion + kNSlot * kSlotCols <= 512, "TMEM budget");
+    static_assert(kHalf % 2 == 0, "paired f32x2 epilogue math");
 };
 
 struct TileCoord {
@@ -101,29 +108,32 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const int* tb, const int
     return c;
 }
 
+// Group scales of (tile, stage) for one weight row: 16 bytes, kKPS k-blocks x 4
+// groups of fp16, read through the read-only path two stages ahead of use.
+struct ScaleCursor {
+    int t, st;
+    const uint8_t* base;  // scales of the current tile
+};
+
 template <int FMT, int EPI, int NT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs a) {
     using C = GemmCfg<FMT, NT>;
     constexpr int SL = C::kLoadStages;
+    constexpr int AS = C::kAStages;
+    constexpr int AS1 = AS > 0 ? AS : 1;  // ring arithmetic of formats without one
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
     uint8_t* load = smem;
-    uint8_t* scales = load + SL * C::kLoadBytes;              // [SS][1 KB] (group)
-    float* xchg = reinterpret_cast<float*>(scales + kScaleStages * C::kScaleBytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + 64 * C::kXchgStride + 2);
-    uint64_t* lfull = bars;           // TMA bytes of stage s landed
-    uint64_t* lempty = lfull + SL;    // MMAs that read stage s completed
-    uint64_t* ofull = lempty + SL;    // W4 operand of stage s unpacked into TMEM
-    uint64_t* sfull = ofull + SL;
-    uint64_t* sempty = sfull + kScaleStages;
-    uint64_t* tfull = sempty + kScaleStages;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(load + SL * C::kLoadBytes);
+    uint64_t* lfull = bars;             // TMA bytes of stage s landed
+    uint64_t* lempty = lfull + SL;      // MMAs that read stage s completed
+    uint64_t* ofull = lempty + SL;      // W4 operand slot a unpacked into TMEM
+    uint64_t* tfull = ofull + (AS > 0 ? AS : 1);
     uint64_t* tempty = tfull + C::kNSlot;
     uint64_t* done = tempty + C::kNSlot;
-    uint64_t* xfull = done + 1;    // up values written (8 warps)
-    uint64_t* xempty = xfull + 1;  // gate warps done reading (8 warps)
-    int* tcnt = reinterpret_cast<int*>(xempty + 1);
+    int* tcnt = reinterpret_cast<int*>(done + 1);
     int* tb = tcnt + a.num_experts + 1;
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_s;
@@ -140,19 +150,13 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
         for (int i = 0; i < SL; ++i) {
             mbar_init(&lfull[i], 1);
             mbar_init(&lempty[i], 1);
-            mbar_init(&ofull[i], kConvWarps);
         }
-        for (int i = 0; i < kScaleStages; ++i) {
-            mbar_init(&sfull[i], kConvWarps);
-            mbar_init(&sempty[i], kEpiWarps);
-        }
+        for (int i = 0; i < AS; ++i) mbar_init(&ofull[i], kConvWarps);
         for (int i = 0; i < C::kNSlot; ++i) {
             mbar_init(&tfull[i], 1);
             mbar_init(&tempty[i], kEpiWarps);
         }
         mbar_init(done, 1);
-        mbar_init(xfull, kEpiWarps / 2);
-        mbar_init(xempty, kEpiWarps / 2);
         fence_barrier_init();
     }
     // tile table: tcnt[e] = token tiles of expert e, tb[e] = its first tile index
@@ -195,12 +199,13 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     const uint32_t tmem_base = tmem_base_s;
     const uint32_t acc_base = tmem_base + C::kARegion;  // accumulator columns
     const int total = total_tiles_s;
+    const int kstages = a.kblocks / kKPS;
     volatile int* abort_flag = &abort_s;
 
     // lane quadrant of this warp's TMEM accesses
     const int quad = warp & 3;
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-    const int half = (warp - kEpiWarp0) >> 2;  // epilogue column quarter (0..3)
+    const int half = (warp - kEpiWarp0) >> 2;  // epilogue column half (0..1)
     if (C::kGroup && warp >= kEpiWarp0) {
         // every group buffer starts as the float 12582912.0
         for (int b = 0; b < C::kNSlot * 4; ++b)
@@ -214,7 +219,6 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
-            const int kstages = a.kblocks / kKPS;
             uint32_t it = 0;  // stage counter
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
@@ -241,10 +245,12 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         // At most one tcgen05.commit per k-block (TMEM slot full) plus one per
-        // stage (stage empty): the commit is the costly part of issuing.
+        // stage (stage empty). Each mbarrier wait on this thread stalls the MMA
+        // issue (~150 cycles even when the phase is complete), so it waits on as
+        // few as possible: W4 stages only on the unpack warps' barrier (they
+        // waited for the stage's copies first), W8 stages on the copies.
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_i8(kTileRows, NT);
-            const int kstages = a.kblocks / kKPS;
             uint32_t it = 0, kbc = 0, ti = 0;  // stage, k-block and tile counters
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++ti) {
@@ -257,8 +263,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                 }
                 for (int st = 0; st < kstages && ok; ++st, ++it) {
                     const int s = it % SL;
-                    if (!mbar_wait(&lfull[s], (it / SL) & 1u, abort_flag, a.err) ||
-                        (C::kW4 && !mbar_wait(&ofull[s], (it / SL) & 1u, abort_flag, a.err))) {
+                    const int ao = it % AS1;
+                    if (C::kW4 ? !mbar_wait(&ofull[ao], (it / AS1) & 1u, abort_flag, a.err)
+                               : !mbar_wait(&lfull[s], (it / SL) & 1u, abort_flag, a.err)) {
                         ok = false;
                         break;
                     }
@@ -275,13 +282,15 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                         }
                         tc_fence_after();
                         const uint32_t ab = smem_u32(act_at(s, jk));
-                        const uint32_t a_tmem = tmem_base + (s * kKPS + jk) * C::kACols;
+                        const uint32_t a_tmem = tmem_base + (ao * kKPS + jk) * C::kACols;
                         const uint32_t wa = smem_u32(w_at(s) + jk * C::kWBytes);
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
                             const uint64_t db = smem_desc_k_sw128(ab + 32 * j);
                             const uint32_t d = C::kGroup ? acc_base + slot * C::kSlotCols + j * NT
                                                          : acc_base + dcol;
+                            // group formats: each buffer adds one group's sum to the
+                            // magic float; per-channel formats: accumulate over K
                             const uint32_t acc = C::kGroup ? 1u : ((st > 0 || jk > 0 || j > 0) ? 1u : 0u);
                             if (C::kW4)
                                 mma_i8_ts(d, a_tmem + 8 * j, db, idesc, acc);
@@ -291,6 +300,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                         if (C::kGroup) mma_commit(&tfull[slot]);
                     }
                     if (!ok) break;
+                    // also frees the stage's W4 operand slot for the unpack warps
                     mma_commit(&lempty[s]);
                 }
                 if (!C::kGroup && ok) mma_commit(&tfull[ti % 2u]);
@@ -304,19 +314,27 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
         // ------------------------------------------------------------ int4 unpack
         if (C::kW4) {
             const int r = quad * 32 + lane;  // weight row = TMEM lane
-            const int ct = threadIdx.x - kConvWarp0 * 32;  // 0..127
-            const int kstages = a.kblocks / kKPS;
-            uint32_t it = 0, kbc = 0;
+            uint32_t it = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                for (int st = 0; st < kstages && ok; ++st, ++it) {
-                    // the producer refilled stage s only after the MMAs that read its
-                    // previous operands completed, so the TMEM operand slot is free
+                for (int st = 0; st < kstages; ++st, ++it) {
                     const int s = it % SL;
+                    const int ao = it % AS1;
+                    // operand slot ao was last read by the MMAs of stage it - AS; their
+                    // commit completed phase (it - AS) / SL of that stage's lempty (it
+                    // cannot have moved further: its next phase needs this stage)
+                    if (it >= (uint32_t)AS1) {
+                        const uint32_t prev = it - AS1;
+                        if (!mbar_wait(&lempty[prev % SL], (prev / SL) & 1u, abort_flag, a.err)) {
+                            ok = false;
+                            break;
+                        }
+                    }
                     if (!mbar_wait(&lfull[s], (it / SL) & 1u, abort_flag, a.err)) {
                         ok = false;
                         break;
                     }
+                    tc_fence_after();
 #pragma unroll
                     for (int jk = 0; jk < kKPS; ++jk) {
                         // row r of the k-block: 64 bytes in four 16-byte chunks,
@@ -338,31 +356,14 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                             o[8 * c + 6] = (p.w << 4) & 0xF0F0F0F0u;
                             o[8 * c + 7] = p.w & 0xF0F0F0F0u;
                         }
-                        tmem_st32(tmem_base + lane_addr + (s * kKPS + jk) * C::kACols, o);
+                        tmem_st32(tmem_base + lane_addr + (ao * kKPS + jk) * C::kACols, o);
                     }
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&ofull[s]);
-                    if (C::kGroup) {
-                        // hand the stage's group scales to the epilogue (1 KB per k-block)
-                        const uint2* ssrc = reinterpret_cast<const uint2*>(w_at(s) + kKPS * C::kWBytes);
-#pragma unroll
-                        for (int jk = 0; jk < kKPS; ++jk, ++kbc) {
-                            const int ss = kbc % kScaleStages;
-                            if (!mbar_wait(&sempty[ss], ((kbc / kScaleStages) & 1u) ^ 1u, abort_flag,
-                                           a.err)) {
-                                ok = false;
-                                break;
-                            }
-                            static_assert(C::kScaleBytes == 8 * 32 * kConvWarps || !C::kGroup,
-                                          "one 8-byte piece of the scales per unpack thread");
-                            reinterpret_cast<uint2*>(scales + ss * C::kScaleBytes)[ct] =
-                                ssrc[jk * (C::kScaleBytes / 8) + ct];
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&sfull[ss]);
-                        }
-                    }
+                    // the MMA issuer waits on this barrier alone: these warps have
+                    // observed the stage's copies (lfull) before arriving
+                    if (lane == 0) mbar_arrive(&ofull[ao]);
                 }
             }
         }
@@ -370,6 +371,34 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
         // ------------------------------------------------------------ epilogue
         const int r = quad * 32 + lane;  // weight row within the tile = TMEM lane
         const int c0 = half * C::kHalf;  // first token column of this warp
+        // group scales: a cursor two stages ahead of use over the same tile order
+        ScaleCursor cur{(int)blockIdx.x, 0, nullptr};
+        auto cursor_tile = [&](ScaleCursor& k) {
+            k.base = nullptr;
+            if (k.t < total) {
+                const TileCoord c = decode_tile(k.t, tb, tcnt, E);
+                k.base = reinterpret_cast<const uint8_t*>(a.wscale) + (size_t)c.e * a.ws_expert_stride +
+                         (size_t)c.rt * a.ws_tile_stride;
+            }
+        };
+        auto cursor_load = [&](ScaleCursor& k) -> uint4 {
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (k.base)
+                v = __ldg(reinterpret_cast<const uint4*>(k.base + ((size_t)k.st * kTileRows + r) * 16));
+            if (++k.st == kstages) {
+                k.st = 0;
+                k.t += gridDim.x;
+                cursor_tile(k);
+            }
+            return v;
+        };
+        uint4 pf0 = make_uint4(0u, 0u, 0u, 0u), pf1 = pf0;
+        if (C::kGroup) {
+            static_assert(kKPS == 2 || !C::kGroup, "16 bytes of group scales per row and stage");
+            cursor_tile(cur);
+            pf0 = cursor_load(cur);
+            pf1 = cursor_load(cur);
+        }
         uint32_t ti = 0, it = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++ti) {
@@ -378,7 +407,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             const int row0 = a.offsets[c.e] + c.mt * NT;
             const int nvalid = min(NT, m_e - c.mt * NT);
             // output channel of this lane (gate/up tiles: 64 gate rows then 64 up rows)
-            const bool swiglu_tile = (EPI == kEpiSwiGLU) || (EPI == kEpiAcc && a.swiglu_layout);
+            const bool swiglu_tile = (EPI == kEpiGateUp) || (EPI == kEpiAcc && a.swiglu_layout);
             int col;
             bool is_up = false;
             if (swiglu_tile) {
@@ -399,71 +428,97 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                     (size_t)c.rt * a.ws_tile_stride);
                 wscale_pc = sp[r];
             }
-            float facc[C::kHalf];
+            // this warp's token columns hold no token at all (the expert's last tile):
+            // it still takes part in every slot handshake but skips the loads and math
+            const bool active = c0 < nvalid;
+            float2 facc[C::kHalf / 2];
 #pragma unroll
-            for (int q = 0; q < C::kHalf; ++q) facc[q] = 0.0f;
+            for (int q = 0; q < C::kHalf / 2; ++q) facc[q] = make_float2(0.0f, 0.0f);
 
             if (C::kGroup) {
-                for (int kb = 0; kb < a.kblocks && ok; ++kb, ++it) {
-                    const int ss = it % kScaleStages;
-                    if (!mbar_wait(&sfull[ss], (it / kScaleStages) & 1u, abort_flag, a.err)) {
-                        ok = false;
-                        break;
+                for (int st = 0; st < kstages && ok; ++st) {
+                    const uint4 sc = pf0;
+                    pf0 = pf1;
+                    pf1 = cursor_load(cur);
+                    // the stage's 8 group scales (k-block jk, group j at 4*jk + j), with
+                    // the 1/16 of the W4 codes folded in (exact)
+                    float2 sg[4];
+                    {
+                        const uint32_t w[4] = {sc.x, sc.y, sc.z, sc.w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            sg[i] = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+                            if (C::kW4) sg[i] = __fmul2_rn(sg[i], make_float2(0.0625f, 0.0625f));
+                        }
                     }
-                    const __half* sc = reinterpret_cast<const __half*>(scales + ss * C::kScaleBytes);
-                    float sg[4];
+#pragma unroll 1
+                    for (int jk = 0; jk < kKPS; ++jk, ++it) {
+                        const int kb = st * kKPS + jk;
+                        const float2 sga = jk ? sg[2] : sg[0];  // groups 0, 1 of this k-block
+                        const float2 sgb = jk ? sg[3] : sg[1];  // groups 2, 3
+                        // one TMEM slot per k-block: wait once, load its four group
+                        // buffers, re-arm them, release the slot, then do the math
+                        const uint32_t slot = it % C::kNSlot;
+                        if (!mbar_wait(&tfull[slot], (it / C::kNSlot) & 1u, abort_flag, a.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t sbase = acc_base + lane_addr + slot * C::kSlotCols + c0;
+                        // rounds of 8 token columns x 4 groups bound the registers; each
+                        // round is loaded, re-armed and folded into its columns' sums
+                        // (the group order per column stays 0..3)
+                        constexpr int kRound = C::kHalf < 8 ? C::kHalf : 8;
+                        const int ncol = is_up ? a.n_valid + col : col;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) sg[j] = __half2float(sc[j * kTileRows + r]);
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&sempty[ss]);
-                    // one TMEM slot per k-block: wait once, load its four group
-                    // buffers, start re-arming them, do the math while the stores
-                    // drain, then release the slot
-                    const uint32_t slot = it % C::kNSlot;
-                    if (!mbar_wait(&tfull[slot], (it / C::kNSlot) & 1u, abort_flag, a.err)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t sbase = acc_base + lane_addr + slot * C::kSlotCols + c0;
-                    // two rounds of two groups: load, re-arm (stores drain meanwhile), math
+                        for (int r0 = 0; r0 < C::kHalf; r0 += kRound) {
+                            uint32_t v[4][kRound];
+                            if (active) {
 #pragma unroll
-                    for (int j0 = 0; j0 < 4; j0 += 2) {
-                        uint32_t v[2][C::kHalf];
+                                for (int j = 0; j < 4; ++j) tmem_ld<kRound>(sbase + j * NT + r0, v[j]);
+                                tmem_wait_ld();
 #pragma unroll
-                        for (int jj = 0; jj < 2; ++jj) tmem_ld<C::kHalf>(sbase + (j0 + jj) * NT, v[jj]);
-                        tmem_wait_ld();
+                                for (int j = 0; j < 4; ++j) tmem_ld_pin(v[j]);
+                            }
+                            // columns of an idle warp are re-armed too: the MMA adds to them
 #pragma unroll
-                        for (int jj = 0; jj < 2; ++jj) tmem_fill<C::kHalf>(sbase + (j0 + jj) * NT, kMagicBits);
-#pragma unroll
-                        for (int jj = 0; jj < 2; ++jj) {
-                            const int j = j0 + jj;
+                            for (int j = 0; j < 4; ++j) tmem_fill<kRound>(sbase + j * NT + r0, kMagicBits);
+                            if (!active) continue;
                             if (EPI == kEpiAcc) {
-                                const int g = kb * 4 + j;
-                                const int ncol = is_up ? a.n_valid + col : col;
 #pragma unroll
-                                for (int q = 0; q < C::kHalf; ++q) {
-                                    if (c0 + q < nvalid && col_ok) {
-                                        int acc = (int)(v[jj][q] - kMagicBits);
-                                        if (C::kW4) acc >>= 4;
-                                        a.acc_out[((size_t)(row0 + c0 + q) * (a.kblocks * 4) + g) *
-                                                      a.acc_ld + ncol] = acc;
+                                for (int j = 0; j < 4; ++j) {
+#pragma unroll
+                                    for (int q = 0; q < kRound; ++q) {
+                                        if (c0 + r0 + q < nvalid && col_ok) {
+                                            int acc = (int)(v[j][q] - kMagicBits);
+                                            if (C::kW4) acc >>= 4;
+                                            a.acc_out[((size_t)(row0 + c0 + r0 + q) * (a.kblocks * 4) + kb * 4 +
+                                                       j) * a.acc_ld + ncol] = acc;
+                                        }
                                     }
                                 }
                             } else {
-                                // W4 codes enter the MMA as 16*w: fold 1/16 into the scale (exact)
-                                const float s_eff = C::kW4 ? sg[j] * 0.0625f : sg[j];
+                                const float2 nm = make_float2(-kMagic, -kMagic);
 #pragma unroll
-                                for (int q = 0; q < C::kHalf; ++q)
-                                    facc[q] = __fmaf_rn(__fsub_rn(__uint_as_float(v[jj][q]), kMagic),
-                                                        s_eff, facc[q]);
+                                for (int j = 0; j < 4; ++j) {
+                                    const float2 sp = (j >> 1) ? sgb : sga;
+                                    const float sj = (j & 1) ? sp.y : sp.x;
+                                    const float2 s2 = make_float2(sj, sj);
+#pragma unroll
+                                    for (int q = 0; q < kRound / 2; ++q) {
+                                        const float2 d = __fadd2_rn(
+                                            make_float2(__uint_as_float(v[j][2 * q]), __uint_as_float(v[j][2 * q + 1])),
+                                            nm);
+                                        facc[r0 / 2 + q] = __ffma2_rn(d, s2, facc[r0 / 2 + q]);
+                                    }
+                                }
                             }
                         }
+                        tmem_wait_st();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[slot]);
                     }
-                    tmem_wait_st();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tempty[slot]);
                 }
                 if (!ok) break;
             } else {
@@ -473,6 +528,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                 uint32_t v[C::kHalf];
                 tmem_ld<C::kHalf>(acc_base + lane_addr + buf * NT + c0, v);
                 tmem_wait_ld();
+                tmem_ld_pin(v);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -486,7 +542,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                             a.acc_out[(size_t)(row0 + c0 + q) * a.acc_ld + ncol] = acc;
                         }
                     } else {
-                        facc[q] = __int2float_rn(acc);
+                        const float f = __int2float_rn(acc);
+                        if (q & 1) facc[q >> 1].y = f; else facc[q >> 1].x = f;
                     }
                 }
             }
@@ -497,39 +554,18 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
 #pragma unroll
             for (int q = 0; q < C::kHalf; ++q) {
                 const float sxq = __shfl_sync(0xffffffffu, my_sx, q);
+                const float f = (q & 1) ? facc[q >> 1].y : facc[q >> 1].x;
                 if (C::kGroup)
-                    val[q] = __fmul_rn(facc[q], sxq);
+                    val[q] = __fmul_rn(f, sxq);
                 else
-                    val[q] = __fmul_rn(__fmul_rn(facc[q], sxq), wscale_pc);
+                    val[q] = __fmul_rn(__fmul_rn(f, sxq), wscale_pc);
             }
-            if (EPI == kEpiSwiGLU) {
-                // up lanes (64..127) hand their values to the gate lanes of the same channel
-                const uint32_t xph = ti & 1u;
-                if (is_up) {
-                    if (!mbar_wait(xempty, xph ^ 1u, abort_flag, a.err)) { ok = false; break; }
-#pragma unroll
-                    for (int q = 0; q < C::kHalf; ++q) xchg[(r - 64) * C::kXchgStride + c0 + q] = val[q];
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(xfull);
-                } else {
-                    if (!mbar_wait(xfull, xph, abort_flag, a.err)) { ok = false; break; }
-#pragma unroll
-                    for (int q = 0; q < C::kHalf; ++q) {
-                        const int j = c0 + q;
-                        if (j < nvalid && col_ok) {
-                            const float gv = val[q];
-                            const float uv = xchg[r * C::kXchgStride + j];
-                            const float d = __fadd_rn(1.0f, expf(-gv));
-                            a.out[(size_t)(row0 + j) * a.ldo + col] = __fmul_rn(__fdiv_rn(gv, d), uv);
-                        }
-                    }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(xempty);
-                }
-            } else if (col_ok) {
+            if (col_ok) {
+                // gate/up tiles: gate channels to the first half of the row, up to the second
+                const int ocol = (EPI == kEpiGateUp && is_up) ? a.n_valid + col : col;
 #pragma unroll
                 for (int q = 0; q < C::kHalf; ++q)
-                    if (c0 + q < nvalid) a.out[(size_t)(row0 + c0 + q) * a.ldo + col] = val[q];
+                    if (c0 + q < nvalid) a.out[(size_t)(row0 + c0 + q) * a.ldo + ocol] = val[q];
             }
         }
         if (!ok) *abort_flag = 1;
@@ -548,9 +584,8 @@ static size_t gemm_smem_bytes(int E) {
     using C = GemmCfg<FMT, NT>;
     size_t b = 1024;  // alignment slack
     b += (size_t)C::kLoadStages * C::kLoadBytes;
-    b += (size_t)kScaleStages * C::kScaleBytes;
-    b += sizeof(float) * (64 * C::kXchgStride + 2);
-    b += sizeof(uint64_t) * (3 * C::kLoadStages + 2 * kScaleStages + 2 * C::kNSlot + 3);
+    b += sizeof(uint64_t) * (2 * C::kLoadStages + (C::kAStages > 0 ? C::kAStages : 1) +
+                             2 * C::kNSlot + 1);
     b += sizeof(int) * (2 * (size_t)E + 2);
     // one CTA per SM: the kernel allocates all 512 TMEM columns
     return b < 120 * 1024 ? 120 * 1024 : b;
@@ -586,7 +621,7 @@ template <int FMT>
 static int launch_gemm_epi(const CUtensorMap& map, const GemmArgs& a, int epi, int nt,
                            int num_sms, cudaStream_t s) {
     switch (epi) {
-        case kEpiSwiGLU: return launch_gemm_nt<FMT, kEpiSwiGLU>(map, a, nt, num_sms, s);
+        case kEpiGateUp: return launch_gemm_nt<FMT, kEpiGateUp>(map, a, nt, num_sms, s);
         case kEpiStore: return launch_gemm_nt<FMT, kEpiStore>(map, a, nt, num_sms, s);
         case kEpiAcc: return launch_gemm_nt<FMT, kEpiAcc>(map, a, nt, num_sms, s);
         default: return -1;

@@ -9,8 +9,10 @@ namespace moe {
 
 // Weight formats (values match MOE_B200_W* in include/moe_b200.h).
 enum { kFmtW4PC = 0, kFmtW4G32 = 1, kFmtW8PC = 2 };
-// GEMM epilogues.
-enum { kEpiSwiGLU = 0, kEpiStore = 1, kEpiAcc = 2 };
+// GEMM epilogues. GateUp: a gate/up tile (64 gate + 64 up channels) stores its
+// dequantised values as gate | up halves of a [rows][2n] row, the layout the
+// SwiGLU of the requantisation kernel reads. Store: [rows][n]. Acc: int32 dump.
+enum { kEpiGateUp = 0, kEpiStore = 1, kEpiAcc = 2 };
 // Activation quantisation rules.
 enum { kQuantMoe = 0, kQuantDense = 1 };
 
@@ -40,7 +42,7 @@ struct GemmArgs {
     size_t ws_tile_stride;    // bytes
     int kblocks;              // K / 128
     int row_tiles;            // weight row tiles of 128
-    float* out;               // SwiGLU: middle [rows][ldo]; store: y [rows][ldo]
+    float* out;               // GateUp: gate | up [rows][ldo = 2n]; Store: y [rows][ldo]
     int ldo;
     int n_valid;              // valid output channels (I or H)
     int32_t* acc_out;         // accumulator dump
@@ -65,7 +67,7 @@ void launch_route_scatter(const int32_t* ids, const float* routes, int n, int E,
 void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k,
                          const int32_t* pos, int8_t* q_rows, float* s_rows, int8_t* q_perm,
                          float* s_perm, uint32_t* err, cudaStream_t s);
-void launch_requant(const float* mid, const int32_t* count, int max_rows, int I, int ld_q,
+void launch_requant(const float* gate_up, const int32_t* count, int max_rows, int I, int ld_q,
                     int rule, int8_t* q, float* sc, cudaStream_t s);
 void launch_combine(const float* y, const int32_t* pos, const float* routes, const float* shared,
                     const float* residual, int T, int H, int k, float* out, cudaStream_t s);

@@ -168,8 +168,8 @@ def test_dispatch_and_accumulators_bit_exact(cuda, oracle, name, T):
 
     # middle (fp tolerance) and the down accumulators fed with the GPU's own codes
     Ki = (I + 127) // 128 * 128
-    mid = dev_view(torch, moe, "middle", (A, I), np.float32)
-    assert_close(mid, d["middle"], what="SwiGLU middle")
+    gu = dev_view(torch, moe, "gate_up", (A, 2 * I), np.float32)
+    assert_close(oracle.swiglu(gu, I), d["middle"], what="SwiGLU middle")
     qm = dev_view(torch, moe, "q_m", (A, Ki), np.int8)[:, :I]
     flips = np.abs(qm.astype(np.int32) - d["qm"].astype(np.int32))
     assert flips.max() <= 1 and (flips > 0).mean() < 1e-3, "middle codes differ beyond rounding"
