@@ -109,24 +109,44 @@ int make_act_map(CUtensorMap* map, const void* base, int rows, int cols, int nt)
     return r == CUDA_SUCCESS ? MOE_B200_OK : MOE_B200_ERR_CUDA;
 }
 
+// The same over an fp16 copy: 64 elements per 128-byte swizzle row, box =
+// 64 x nt rows x 4 = the 256 k of one group-32 stage.
+int make_act_map_h(CUtensorMap* map, const void* base, int rows, int cols, int nt) {
+    auto enc = get_encode();
+    if (!enc || cols % kKAlign) return MOE_B200_ERR_CUDA;
+    cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(cols / 64)};
+    cuuint64_t strides[2] = {(cuuint64_t)cols * 2, 128};
+    cuuint32_t box[3] = {64, (cuuint32_t)nt, (cuuint32_t)(2 * kKPS)};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? MOE_B200_OK : MOE_B200_ERR_CUDA;
+}
+
 constexpr int kNTs[3] = {16, 32, 64};
 int nt_index(int nt) { return nt == 16 ? 0 : nt == 32 ? 1 : 2; }
-// Token tile (MMA N) from the expected rows per expert; group-32 weights keep
-// four K=32 buffers per k-block in TMEM next to the unpacked weights, which
-// caps their tile at 32 tokens.
-int choose_nt(long rows, int experts, int fmt) {
+// Token tile (MMA N) from the expected rows per expert. An MMA costs the same
+// for N <= 64, so tiles grow to 64 once an expert averages more than 16 rows.
+int choose_nt(long rows, int experts) {
     const long avg = experts > 0 ? (rows + experts - 1) / experts : rows;
-    if (avg <= 16) return 16;
-    if (avg <= 32 || fmt == kFmtW4G32) return 32;
+    if (avg <= 8) return 16;
+    if (avg <= 16) return 32;
     return 64;
 }
+// The exact int8 group-32 kernel keeps four K=32 buffers per k-block in TMEM,
+// which caps its tile at 32 tokens.
+int exact_nt(int nt, int fmt) { return fmt == kFmtW4G32 && nt > 32 ? 32 : nt; }
+// Group-32 down projections (their output is not requantised) run on the fp16
+// tensor cores; gate/up projections keep the exact per-group sums.
+int down_fmt(int fmt) { return fmt == kFmtW4G32 ? kFmtW4G32H : fmt; }
 
 // ---- packed matrices ------------------------------------------------------
 
 struct PackedMat {
     uint8_t* w = nullptr;
     void* s = nullptr;
-    size_t w_expert_stride = 0, w_tile_stride = 0;
+    size_t w_expert_stride = 0, w_tile_stride = 0, w_stage_stride = 0;
     size_t s_expert_stride = 0, s_tile_stride = 0;
     int fmt = 0, kblocks = 0, row_tiles = 0, experts = 0;
     int k = 0, n = 0;        // logical K and output channels (n = I for SwiGLU)
@@ -152,35 +172,50 @@ inline int tile_channel(const PackedMat& m, int rt, int lr) {
     return c < m.n ? c : -1;
 }
 
+// Group-32 stage: 256 k of 128 rows = 16 KB of nibbles (row r: 128 bytes, its
+// 16-byte chunk c at position c ^ (r & 7), conflict-free for one row per
+// thread) followed by the rows' 8 group scales (fp16, 16 bytes per row).
+// Chunk c is group c of the stage; its word w holds k = 32c + 8w + j with j
+// even in nibble j/2 and j odd in nibble 4 + j/2 as the offset-binary code
+// w + 8, so one mask of 0x000F000F after a shift by 4i yields the fp16 pair
+// (k = 2i, 2i + 1) and byte permutes yield int8 in k order.
+constexpr size_t kG32StageW = 128 * 128;
+constexpr size_t kG32Stage = kG32StageW + 128 * 16;
+
 // Packs one reference-layout matrix (codes [K][N], N = 2n for SwiGLU) into
-// tile-major device order. For each 128-row tile: stages of kKPS k-blocks of
-// weights, so one bulk copy moves a whole stage. Scales: per-channel formats
-// f32 [128] per tile; group-32 fp16 [stage][row][kKPS k-blocks][4 groups],
-// 16 bytes per row and stage (one vector load for the epilogue thread of
-// that row). host_w / host_s point at this expert's slot.
+// tile-major device order, per 128-row tile and load stage (kKPS k-blocks of
+// 128 k). Per-channel formats: the stage's weight blocks (W8: the tensor
+// core's 128-byte-swizzle K-major layout; W4: 64 bytes per row, 16-byte chunk
+// c (k 32c..32c+31) at chunk c ^ ((r >> 1) & 3), byte b of word w holding k =
+// 32c+8w+b in its low nibble and k+4 in its high nibble), f32 scales [128] per
+// tile in host_s. Group-32: the stage layout above. host_w / host_s point at
+// this expert's slot.
 void pack_expert(const PackedMat& m, const int8_t* codes, const float* scales,
                  const uint16_t* gscales, uint8_t* host_w, uint8_t* host_s) {
     const int K = m.k;
     const int N = m.swiglu ? 2 * m.n : m.n;
     const bool w4 = m.fmt != kFmtW8PC;
     const size_t tile_bytes = w4 ? 8192 : 16384;
-    const size_t stage_bytes = kKPS * tile_bytes;
     for (int rt = 0; rt < m.row_tiles; ++rt) {
         for (int lr = 0; lr < 128; ++lr) {
             const int ch = tile_channel(m, rt, lr);
             for (int kb = 0; kb < m.kblocks; ++kb) {
-                uint8_t* stage = host_w + (size_t)rt * m.w_tile_stride + (kb / kKPS) * stage_bytes;
+                uint8_t* stage = host_w + (size_t)rt * m.w_tile_stride + (kb / kKPS) * m.w_stage_stride;
                 uint8_t* tile = stage + (size_t)(kb % kKPS) * tile_bytes;
                 for (int kbyte = 0; kbyte < 128; ++kbyte) {
                     const int k = kb * 128 + kbyte;
                     const int8_t code = (ch >= 0 && k < K) ? codes[(size_t)k * N + ch] : 0;
-                    if (!w4) {
-                        // W8: the tensor core's 128-byte-swizzle K-major operand layout
+                    if (m.fmt == kFmtW4G32) {
+                        const int ks = (kb % kKPS) * 128 + kbyte;  // k within the stage
+                        const int c = ks / 32, w = (ks % 32) / 8, j = ks % 8;
+                        const int p = (j & 1) ? 4 + j / 2 : j / 2;
+                        const size_t pb = (size_t)lr * 128 + ((c ^ (lr & 7)) * 16) + w * 4 + p / 2;
+                        const uint8_t nib = (uint8_t)((code + 8) & 0xF);
+                        stage[pb] = (p & 1) ? (uint8_t)((stage[pb] & 0x0F) | (nib << 4))
+                                            : (uint8_t)((stage[pb] & 0xF0) | nib);
+                    } else if (!w4) {
                         tile[sw128(lr, kbyte)] = (uint8_t)code;
                     } else {
-                        // W4: row lr owns 64 bytes; 16-byte chunk c (k 32c..32c+31) sits
-                        // at chunk c ^ ((lr >> 1) & 3); byte b of word w holds k =
-                        // 32c+8w+b in its low nibble and k+4 in its high nibble
                         const int c = kbyte / 32, w = (kbyte % 32) / 8, e = kbyte % 8;
                         const size_t pb = (size_t)lr * 64 + ((c ^ ((lr >> 1) & 3)) * 16) + w * 4 + (e & 3);
                         const uint8_t nib = (uint8_t)code & 0xF;
@@ -191,12 +226,11 @@ void pack_expert(const PackedMat& m, const int8_t* codes, const float* scales,
                     }
                 }
                 if (m.fmt == kFmtW4G32) {
-                    uint16_t* st = reinterpret_cast<uint16_t*>(host_s + (size_t)rt * m.s_tile_stride +
-                                                               (size_t)(kb / kKPS) * 128 * kKPS * 8) +
-                                   (size_t)lr * kKPS * 4 + (kb % kKPS) * 4;
+                    uint16_t* st = reinterpret_cast<uint16_t*>(stage + kG32StageW + (size_t)lr * 16);
                     for (int j = 0; j < 4; ++j) {
                         const int g = kb * 4 + j;
-                        st[j] = (ch >= 0 && g * 32 < K) ? gscales[(size_t)g * N + ch] : (uint16_t)0;
+                        st[(kb % kKPS) * 4 + j] =
+                            (ch >= 0 && g * 32 < K) ? gscales[(size_t)g * N + ch] : (uint16_t)0;
                     }
                 }
             }
@@ -218,10 +252,11 @@ int setup_mat(PackedMat& m, int fmt, int experts, int K, int n, bool swiglu) {
     m.row_tiles = swiglu ? (n + 63) / 64 : (n + 127) / 128;
     const size_t tile_bytes = fmt == kFmtW8PC ? 16384 : 8192;
     const size_t stages = (size_t)(m.kblocks / kKPS);
-    m.w_tile_stride = stages * kKPS * tile_bytes;
+    static_assert(kKPS == 2, "group-32 stages hold 256 k (8 groups)");
+    m.w_stage_stride = fmt == kFmtW4G32 ? kG32Stage : kKPS * tile_bytes;
+    m.w_tile_stride = stages * m.w_stage_stride;
     m.w_expert_stride = (size_t)m.row_tiles * m.w_tile_stride;
-    // group-32: fp16 [stage][128 rows][kKPS][4]; per-channel: f32 [128]
-    m.s_tile_stride = fmt == kFmtW4G32 ? stages * 128 * kKPS * 8 : 512;
+    m.s_tile_stride = 512;  // per-channel f32 scales of one tile (group scales live in w)
     m.s_expert_stride = (size_t)m.row_tiles * m.s_tile_stride;
     return MOE_B200_OK;
 }
@@ -262,6 +297,7 @@ struct moe_b200_workspace {
     int32_t *hist = nullptr, *offsets = nullptr, *perm = nullptr, *pos = nullptr;
     int32_t *shared_offsets = nullptr, *counters = nullptr;
     int8_t* a_perm = nullptr;
+    __half *q_m_h = nullptr, *sq_m_h = nullptr;  // fp16 copies of the middle codes (group-32 down)
     float* s_perm = nullptr;
     // routed experts
     float* gate_up = nullptr;  // dequantised gate | up rows [n][2I]
@@ -273,6 +309,7 @@ struct moe_b200_workspace {
     float* logits = nullptr;
     uint32_t* err = nullptr;
     CUtensorMap map_a[3], map_qm[3], map_qx[3], map_qxd[3], map_sqm[3];
+    CUtensorMap map_qm_h[3], map_sqm_h[3];
     cudaEvent_t ev[12] = {};
     // stage-profiling ring of device calls
     static constexpr int kProfSlots = 64, kProfEvents = 9;
@@ -320,6 +357,7 @@ GemmArgs gemm_args(moe_b200_workspace* ws, const PackedMat& m, const float* act_
     a.w = m.w;
     a.w_expert_stride = m.w_expert_stride;
     a.w_tile_stride = m.w_tile_stride;
+    a.w_stage_stride = m.w_stage_stride;
     a.wscale = m.s;
     a.ws_expert_stride = m.s_expert_stride;
     a.ws_tile_stride = m.s_tile_stride;
@@ -337,21 +375,25 @@ GemmArgs gemm_args(moe_b200_workspace* ws, const PackedMat& m, const float* act_
 int run_shared(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
                cudaStream_t s) {
     const int rule = w->shared_mode == MOE_B200_SHARED_JOINT ? kQuantMoe : kQuantDense;
-    const int nt = choose_nt(rows, 1, w->sgu.fmt);
-    const CUtensorMap* amap = &ws->map_qx[nt_index(nt)];
+    const int nt = choose_nt(rows, 1);
+    const int nt_g = exact_nt(nt, w->sgu.fmt);
+    const bool hd = w->sdn.fmt == kFmtW4G32;
+    const CUtensorMap* amap = &ws->map_qx[nt_index(nt_g)];
     const float* ascale = ws->s_x;
     if (w->shared_mode != MOE_B200_SHARED_JOINT) {
         launch_quant_gather(d_x, rows, ws->H, ws->Kh, kQuantDense, 1, nullptr, ws->q_xd, ws->s_xd,
-                            nullptr, nullptr, ws->err, s);
-        amap = &ws->map_qxd[nt_index(nt)];
+                            nullptr, nullptr, nullptr, nullptr, ws->err, s);
+        amap = &ws->map_qxd[nt_index(nt_g)];
         ascale = ws->s_xd;
     }
     GemmArgs g = gemm_args(ws, w->sgu, ascale, ws->shared_offsets, 1, rows, ws->s_middle, 2 * w->Is);
-    if (launch_gemm(*amap, g, w->sgu.fmt, kEpiGateUp, nt, ws->num_sms, s)) return MOE_B200_ERR_UNSUPPORTED;
+    if (launch_gemm(*amap, g, w->sgu.fmt, kEpiGateUp, nt_g, ws->num_sms, s))
+        return MOE_B200_ERR_UNSUPPORTED;
     launch_requant(ws->s_middle, ws->shared_offsets + 1, rows, w->Is, ws->Kis, rule, ws->sq_m,
-                   ws->ss_m, s);
+                   hd ? ws->sq_m_h : nullptr, ws->ss_m, s);
     GemmArgs d = gemm_args(ws, w->sdn, ws->ss_m, ws->shared_offsets, 1, rows, ws->s_y, ws->H);
-    if (launch_gemm(ws->map_sqm[nt_index(nt)], d, w->sdn.fmt, kEpiStore, nt, ws->num_sms, s))
+    if (launch_gemm(hd ? ws->map_sqm_h[nt_index(nt)] : ws->map_sqm[nt_index(nt)], d,
+                    down_fmt(w->sdn.fmt), kEpiStore, nt, ws->num_sms, s))
         return MOE_B200_ERR_UNSUPPORTED;
     return MOE_B200_OK;
 }
@@ -395,17 +437,22 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
                          ws->shared_offsets, rows, s);
     mark(2);
     launch_quant_gather(d_x, rows, H, ws->Kh, kQuantMoe, k, ws->pos, ws->q_x, ws->s_x, ws->a_perm,
-                        ws->s_perm, ws->err, s);
+                        ws->s_perm, nullptr, nullptr, ws->err, s);
     mark(3);
-    const int nt = choose_nt(n, E, w->gu.fmt);
+    const int nt = choose_nt(n, E);
+    const int nt_g = exact_nt(nt, w->gu.fmt);
     GemmArgs g = gemm_args(ws, w->gu, ws->s_perm, ws->offsets, E, n, ws->gate_up, 2 * I);
-    if (launch_gemm(ws->map_a[nt_index(nt)], g, w->gu.fmt, kEpiGateUp, nt, ws->num_sms, s))
+    if (launch_gemm(ws->map_a[nt_index(nt_g)], g, w->gu.fmt, kEpiGateUp, nt_g, ws->num_sms, s))
         return MOE_B200_ERR_UNSUPPORTED;
     mark(4);
-    launch_requant(ws->gate_up, ws->offsets + E, (int)n, I, ws->Ki, kQuantMoe, ws->q_m, ws->s_m, s);
+    // group-32 down projections read an fp16 copy of the middle codes
+    const bool hd = w->dn.fmt == kFmtW4G32;
+    launch_requant(ws->gate_up, ws->offsets + E, (int)n, I, ws->Ki, kQuantMoe, ws->q_m,
+                   hd ? ws->q_m_h : nullptr, ws->s_m, s);
     mark(5);
     GemmArgs d = gemm_args(ws, w->dn, ws->s_m, ws->offsets, E, n, ws->y, H);
-    if (launch_gemm(ws->map_qm[nt_index(nt)], d, w->dn.fmt, kEpiStore, nt, ws->num_sms, s))
+    if (launch_gemm(hd ? ws->map_qm_h[nt_index(nt)] : ws->map_qm[nt_index(nt)], d,
+                    down_fmt(w->dn.fmt), kEpiStore, nt, ws->num_sms, s))
         return MOE_B200_ERR_UNSUPPORTED;
     mark(6);
     if (w->shared) {
@@ -417,7 +464,7 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
                    d_out, s);
     mark(8);
     ws->last_rows = rows;
-    ws->last_nt_gu = nt;
+    ws->last_nt_gu = nt_g;
     ws->last_nt_dn = nt;
     ws->last_w = w;
     ws->last_stream = s;
@@ -633,6 +680,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     rc |= ws_alloc(ws, &ws->shared_offsets, 2);
     rc |= ws_alloc(ws, &ws->counters, T);
     rc |= ws_alloc(ws, &ws->a_perm, (n + pad_rows) * ws->Kh);
+    rc |= ws_alloc(ws, &ws->q_m_h, (n + pad_rows) * ws->Ki);
     rc |= ws_alloc(ws, &ws->s_perm, n);
     rc |= ws_alloc(ws, &ws->gate_up, n * 2 * ws->I);
     rc |= ws_alloc(ws, &ws->q_m, (n + pad_rows) * ws->Ki);
@@ -645,6 +693,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
         rc |= ws_alloc(ws, &ws->s_xd, T);
         rc |= ws_alloc(ws, &ws->s_middle, T * 2 * ws->Is);
         rc |= ws_alloc(ws, &ws->sq_m, (T + pad_rows) * ws->Kis);
+        rc |= ws_alloc(ws, &ws->sq_m_h, (T + pad_rows) * ws->Kis);
         rc |= ws_alloc(ws, &ws->ss_m, T);
         rc |= ws_alloc(ws, &ws->s_y, T * ws->H);
     }
@@ -657,14 +706,17 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     cudaMemset(ws->a_perm, 0, (size_t)(n + pad_rows) * ws->Kh);
     cudaMemset(ws->q_m, 0, (size_t)(n + pad_rows) * ws->Ki);
     cudaMemset(ws->q_x, 0, (size_t)(T + pad_rows) * ws->Kh);
+    cudaMemset(ws->q_m_h, 0, sizeof(__half) * (size_t)(n + pad_rows) * ws->Ki);
     for (int i = 0; i < 3 && rc == MOE_B200_OK; ++i) {
         const int nt = kNTs[i];
         rc |= make_act_map(&ws->map_a[i], ws->a_perm, (int)(n + pad_rows), ws->Kh, nt);
         rc |= make_act_map(&ws->map_qm[i], ws->q_m, (int)(n + pad_rows), ws->Ki, nt);
         rc |= make_act_map(&ws->map_qx[i], ws->q_x, (int)(T + pad_rows), ws->Kh, nt);
+        rc |= make_act_map_h(&ws->map_qm_h[i], ws->q_m_h, (int)(n + pad_rows), ws->Ki, nt);
         if (ws->Is > 0) {
             rc |= make_act_map(&ws->map_qxd[i], ws->q_xd, (int)(T + pad_rows), ws->Kh, nt);
             rc |= make_act_map(&ws->map_sqm[i], ws->sq_m, (int)(T + pad_rows), ws->Kis, nt);
+            rc |= make_act_map_h(&ws->map_sqm_h[i], ws->sq_m_h, (int)(T + pad_rows), ws->Kis, nt);
         }
     }
     if (rc == MOE_B200_OK && cudaStreamCreateWithFlags(&ws->own_stream, cudaStreamNonBlocking) != cudaSuccess)
@@ -938,7 +990,7 @@ int moe_b200_debug_accumulators(moe_b200_workspace* ws, const moe_b200_weights* 
     const int ld = which == 0 ? 2 * w->I : w->H;
     if ((uint64_t)n * G * ld > capacity_elems) return MOE_B200_ERR_CAPACITY;
     cudaMemsetAsync(d_acc, 0, sizeof(int32_t) * (size_t)n * G * ld, s);
-    const int nt = which == 0 ? ws->last_nt_gu : ws->last_nt_dn;
+    const int nt = exact_nt(which == 0 ? ws->last_nt_gu : ws->last_nt_dn, m.fmt);
     GemmArgs a = which == 0 ? gemm_args(ws, m, ws->s_perm, ws->offsets, ws->E, n, nullptr, 0)
                             : gemm_args(ws, m, ws->s_m, ws->offsets, ws->E, n, nullptr, 0);
     a.acc_out = d_acc;

@@ -154,6 +154,16 @@ __device__ __forceinline__ uint32_t quant4(float4 v, float s, float inv, int rul
            ((uint32_t)(quant_one(v.w, s, inv, rule) & 0xFF) << 24);
 }
 
+// The four int8 codes of a packed word as two fp16 pairs (exact: |q| <= 127),
+// the activation operand of the fp16 tensor-core path of group-32 weights.
+__device__ __forceinline__ uint2 codes_to_half4(uint32_t packed) {
+    const __half2 a = __halves2half2(__int2half_rn((int8_t)(packed & 0xFF)),
+                                     __int2half_rn((int8_t)((packed >> 8) & 0xFF)));
+    const __half2 b = __halves2half2(__int2half_rn((int8_t)((packed >> 16) & 0xFF)),
+                                     __int2half_rn((int8_t)(packed >> 24)));
+    return make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+}
+
 __device__ __forceinline__ float amax4(float4 v) {
     return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 }
@@ -184,7 +194,7 @@ template <int V>
 __global__ void __launch_bounds__(256)
 quant_gather_kernel(const float* __restrict__ x, int H, int ld_q, int rule, int k,
                     const int32_t* __restrict__ pos, int8_t* q_rows, float* s_rows,
-                    int8_t* q_perm, float* s_perm, uint32_t* err) {
+                    int8_t* q_perm, float* s_perm, __half* h_rows, __half* h_perm, uint32_t* err) {
     __shared__ float red[8];
     __shared__ int slots[32];
     __shared__ int nslot_s;
@@ -225,6 +235,13 @@ quant_gather_kernel(const float* __restrict__ x, int H, int ld_q, int rule, int 
             if (q_rows) reinterpret_cast<uint32_t*>(q_rows + (size_t)t * ld_q)[c] = packed;
             for (int j = 0; j < nslot; ++j)
                 reinterpret_cast<uint32_t*>(q_perm + (size_t)slots[j] * ld_q)[c] = packed;
+            if (h_rows || h_perm) {
+                const uint2 h = codes_to_half4(packed);
+                if (h_rows) reinterpret_cast<uint2*>(h_rows + (size_t)t * ld_q)[c] = h;
+                if (h_perm)
+                    for (int j = 0; j < nslot; ++j)
+                        reinterpret_cast<uint2*>(h_perm + (size_t)slots[j] * ld_q)[c] = h;
+            }
         }
     }
 }
@@ -243,7 +260,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 template <int V>
 __global__ void __launch_bounds__(128)
 requant_kernel(const float* __restrict__ gate_up, const int32_t* __restrict__ count, int I,
-               int ld_q, int rule, int8_t* q, float* sc) {
+               int ld_q, int rule, int8_t* q, __half* qh, float* sc) {
     __shared__ float red[4];
     const int row = blockIdx.x;
     if (row >= *count) return;
@@ -272,7 +289,11 @@ requant_kernel(const float* __restrict__ gate_up, const int32_t* __restrict__ co
 #pragma unroll
     for (int i = 0; i < V; ++i) {
         const int c = threadIdx.x + 128 * i;
-        if (c < n4) qr[c] = quant4(v[i], s, inv, rule);
+        if (c < n4) {
+            const uint32_t packed = quant4(v[i], s, inv, rule);
+            qr[c] = packed;
+            if (qh) reinterpret_cast<uint2*>(qh + (size_t)row * ld_q)[c] = codes_to_half4(packed);
+        }
     }
 }
 
@@ -343,10 +364,11 @@ void launch_route_scatter(const int32_t* ids, const float* routes, int n, int E,
 
 void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k,
                          const int32_t* pos, int8_t* q_rows, float* s_rows, int8_t* q_perm,
-                         float* s_perm, uint32_t* err, cudaStream_t s) {
+                         float* s_perm, __half* h_rows, __half* h_perm, uint32_t* err,
+                         cudaStream_t s) {
     if (T == 0) return;
     const int v = (H / 4 + 255) / 256;
-#define QG(V) quant_gather_kernel<V><<<T, 256, 0, s>>>(x, H, ld_q, rule, k, pos, q_rows, s_rows, q_perm, s_perm, err)
+#define QG(V) quant_gather_kernel<V><<<T, 256, 0, s>>>(x, H, ld_q, rule, k, pos, q_rows, s_rows, q_perm, s_perm, h_rows, h_perm, err)
     if (v <= 1) QG(1);
     else if (v <= 2) QG(2);
     else if (v <= 4) QG(4);
@@ -355,10 +377,10 @@ void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k
 }
 
 void launch_requant(const float* gate_up, const int32_t* count, int max_rows, int I, int ld_q,
-                    int rule, int8_t* q, float* sc, cudaStream_t s) {
+                    int rule, int8_t* q, __half* qh, float* sc, cudaStream_t s) {
     if (max_rows == 0) return;
     const int v = (I / 4 + 127) / 128;
-#define RQ(V) requant_kernel<V><<<max_rows, 128, 0, s>>>(gate_up, count, I, ld_q, rule, q, sc)
+#define RQ(V) requant_kernel<V><<<max_rows, 128, 0, s>>>(gate_up, count, I, ld_q, rule, q, qh, sc)
     if (v <= 1) RQ(1);
     else if (v <= 2) RQ(2);
     else if (v <= 4) RQ(4);

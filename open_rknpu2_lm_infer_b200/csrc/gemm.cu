@@ -1,50 +1,67 @@
-// Grouped expert GEMMs on the sm_100a tensor cores (tcgen05, kind::i8).
+// Grouped expert GEMMs on the sm_100a tensor cores (tcgen05).
 //
 // Replaces the gate/up and down GEMMs of the reference's native MoE operator
 // (rk_npu_moe_w8_run_f32, called at src/npu/moe.rs:372-386; arithmetic restated
 // from llm_generated_docs/MINICPMV47_35A3_FUSED_MOE_20261019.md:77 and
-// MOE_CPU_FUSION_20261023.md:12-13): exact INT32 accumulation of int8
-// activations x int4/int8 weights, then dequantisation.
+// MOE_CPU_FUSION_20261023.md:12-13): int8 activations x int4/int8 weights.
 //
 // Layout ("swap-AB"): the weight tile is the MMA's M=128 operand and the
 // tokens of one expert are the N operand, so one TMEM lane = one output
 // channel and TMEM columns = tokens. Small token counts (decode) cost N=16
-// columns instead of a 128-row M tile, and each epilogue thread owns a
-// channel whose per-group scale it reads once per group.
+// columns instead of a 128-row M tile.
 //
-// Warp roles (704 threads):
-//   warp 0       producer: per load stage (kKPS k-blocks) one bulk copy of the
-//                weight blocks (+ group scales) and one 3-D TMA copy of the
-//                permuted activation rows. A copy request costs ~0.2 us per SM
-//                whatever its size, so a stage moves >= 16 KB per request.
-//   warp 1       TMEM allocator + single-thread MMA issuer
-//   warps 2..5   W4 formats: unpack int4 -> int8 straight into tensor memory,
-//                one warp per TMEM lane quadrant, one weight row per thread;
-//                the MMA then reads its weight operand from TMEM (no shared
-//                memory operand, no proxy fence). W8: idle.
+// Formats:
+//   W8 / W4 per-channel  kind::i8, exact int32 accumulation over all of K,
+//                        one dequantisation per tile: (acc * s_x) * s_w.
+//   W4 group-32 (G32H)   kind::f16: the unpack warps write w * s_group (one
+//                        fp16 rounding of an exact product of an int4 code and
+//                        an fp16 scale); the activation codes are exact in
+//                        fp16; all of K accumulates in fp32. One accumulator
+//                        per tile instead of one per group: a K=32 MMA per
+//                        group with a TMEM read-back per k-block is bound by
+//                        that round trip (measured ~3.5x slower).
+//   W4 group-32 (exact)  kind::i8, one MMA (K = 32 = one group) per TMEM
+//                        buffer; the four buffers of a k-block form a slot.
+//                        Every buffer holds the bits of 12582912.0f before its
+//                        MMA, which adds the int32 sum to them, so the result
+//                        read back as a float is exactly 12582912 + 16*acc
+//                        (|16*acc| < 2^22). The epilogue re-arms the buffers
+//                        right after loading them and computes
+//                        f = fma(D - 12582912, s/16, f) two values per
+//                        instruction (f32x2), equal to fma((float)acc, s, f) bit
+//                        for bit. Used where the result is requantised (the
+//                        gate/up GEMM: a rounding difference there flips int8
+//                        middle codes) and for the accumulator dump; G32H where
+//                        it is not (the down GEMM).
+//
+// A load stage covers 256 k: one bulk copy of the weights (group-32: with the
+// stage's group scales) and one 3-D TMA copy of the permuted activation rows.
+// A copy request costs ~0.2 us per SM whatever its size, so stages are large.
+//
+// Warp roles (448 threads):
+//   warp 0       producer
+//   warp 1       TMEM allocator + single-thread MMA issuer. Each mbarrier wait
+//                on this thread stalls the MMA issue (~150 cycles even when the
+//                phase is complete), so it waits on as few barriers as it can.
+//   warps 2..5   W4 formats: unpack into tensor memory, one warp per TMEM lane
+//                quadrant, one weight row per thread; the MMA reads its weight
+//                operand from TMEM (no shared-memory operand, no proxy fence).
 //   warps 6..13  epilogue, two warps per TMEM lane quadrant, each owning half
-//                of the token columns. The epilogue shares each SM sub-partition
-//                with an unpack warp, so it is kept to few instructions per value.
-//
-// Group-32 formats: one MMA (K = 32 = one group) per TMEM buffer; the four
-// buffers of a k-block form a slot. Every buffer holds the bits of 12582912.0f
-// (0x4B400000) before its MMA, which adds the int32 sum to them, so the result
-// read back as a float is exactly 12582912 + 16*acc (|16*acc| < 2^22). The
-// epilogue re-arms the buffers right after loading them and computes
-// f = fma(D - 12582912, s/16, f) two values per instruction (f32x2): an exact
-// subtraction and one FMA, equal to fma((float)acc, s, f) bit for bit. Per-channel formats: all of K accumulates in TMEM,
-// one dequant per tile.
+//                of the token columns.
 #include "kernels.cuh"
 
 namespace moe {
 
-constexpr int kGemmThreads = 448;
+constexpr int kProdWarp = 0;          // copy producer
+constexpr int kMmaWarp = 1;           // TMEM allocator + MMA issuer
 constexpr int kConvWarp0 = 2;         // first unpack warp
 constexpr int kConvWarps = 4;
 constexpr int kEpiWarp0 = 6;          // first epilogue warp
 constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 32 * (kEpiWarp0 + kEpiWarps);
 constexpr int kTileRows = 128;        // weight rows per tile (MMA M)
-constexpr int kKBlock = 128;          // K bytes per k-block (one 128B swizzle row)
+constexpr int kKBlock = 128;          // int8 k per k-block (one 128-byte swizzle row)
+constexpr int kStageK = kKPS * kKBlock;  // k per load stage (256)
 // Shared memory: the load ring gets what is left of 227 KB after the tile
 // tables (up to 1024 experts), barriers and the 1 KB alignment slack.
 constexpr int kSmemTotal = 227 * 1024;
@@ -53,38 +70,70 @@ constexpr int kMaxLoadStages = 8;
 constexpr uint32_t kMagicBits = 0x4B400000u;  // 12582912.0f
 constexpr float kMagic = 12582912.0f;
 
+// kind::f16 instruction descriptor: fp16 A and B, fp32 accumulate, both
+// operands K-major, M x N tile.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, fp16 x fp16 -> fp32, one CTA.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 template <int FMT, int NT>
 struct GemmCfg {
-    static constexpr bool kW4 = (FMT == kFmtW4G32 || FMT == kFmtW4PC);
-    static constexpr bool kGroup = (FMT == kFmtW4G32);
-    static constexpr int kWBytes = kW4 ? kTileRows * kKBlock / 2 : kTileRows * kKBlock;
-    static constexpr int kActBytes = NT * kKBlock;           // per k-block
-    static constexpr int kStageW = kKPS * kWBytes;           // weight request of one stage
-    // load stage: [activations kKPS x NT x 128][weights]; W8 weights are the MMA
-    // operand tiles, W4 weights are unpacked into TMEM.
-    static constexpr int kLoadBytes = kKPS * kActBytes + kStageW;
+    static constexpr bool kF16 = (FMT == kFmtW4G32H);
+    static constexpr bool kGroup = (FMT == kFmtW4G32);  // exact per-group sums
+    static constexpr bool kW4 = (FMT != kFmtW8PC);
+    static constexpr bool kG32Pack = kF16 || kGroup;     // group-32 stage layout
+    // weights of one stage in HBM and the part of them one request copies
+    static constexpr int kStageWStride = kG32Pack ? 128 * 128 + 128 * 16
+                                                  : kKPS * kTileRows * (kW4 ? kKBlock / 2 : kKBlock);
+    static constexpr int kStageW = kGroup ? 128 * 128 : kStageWStride;
+    // activations of one stage: int8 kKPS atoms of NT x 128 B, fp16 2*kKPS
+    static constexpr int kAtoms = kF16 ? 2 * kKPS : kKPS;
+    static constexpr int kStageAct = kAtoms * NT * 128;
+    // load stage: [activations][weights (+ group scales)]
+    static constexpr int kLoadBytes = kStageAct + kStageW;
     static constexpr int kLoadBudget = kSmemTotal - kSmemFixed;
     static constexpr int kLoadStages = kLoadBudget / kLoadBytes > kMaxLoadStages
                                            ? kMaxLoadStages : kLoadBudget / kLoadBytes;
-    // TMEM: [W4 weight operand ring: kAStages x kKPS x 32 columns][accumulators].
-    // The operand ring is shallower than the load ring: unpacking is quick,
-    // while HBM latency needs many stages of loads in flight.
-    static constexpr int kACols = 32;                        // one k-block of int8 weights
-    static constexpr int kAStages = kW4 ? (kGroup ? 2 : 4) : 0;
-    static constexpr int kARegion = kAStages * kKPS * kACols;
-    // group formats: slots of one k-block (4 group buffers of NT columns);
-    // per-channel formats: two tile accumulators.
+    // TMEM: [W4 weight operand ring: kAStages x kStageACols][accumulators]. The
+    // operand ring is shallower than the load ring: unpacking is quick, while
+    // HBM latency needs many stages of loads in flight.
+    static constexpr int kStageACols = kF16 ? 128 : (kW4 ? kKPS * 32 : 0);
+    static constexpr int kAStages = kW4 ? (kF16 || kGroup ? 2 : 4) : 0;
+    static constexpr int kARegion = kAStages * kStageACols;
+    // exact group path: slots of one k-block (4 group buffers of NT columns);
+    // other formats: two tile accumulators.
     static constexpr int kSlotCols = kGroup ? 4 * NT : NT;
     static constexpr int kAccFree = 512 - kARegion;
     static constexpr int kNSlot = kGroup ? ((kAccFree / kSlotCols) < 4 ? (kAccFree / kSlotCols) : 4)
                                          : 2;
     static constexpr int kAllocCols = 512;
     static constexpr int kHalf = NT / 2;                      // columns per epilogue warp
+    static constexpr int kMmaPerStage = kF16 ? kStageK / 16 : kKPS * 4;
+    static_assert(kLoadBytes % 1024 == 0, "stage alignment of the swizzled operands");
     static_assert(kLoadStages >= 2, "smem budget");
     static_assert(kLoadStages >= kAStages, "operand ring reuse is ordered by the load ring");
-    static_assert(kNSlot >= 2, "TMEM budget: group formats need NT <= 32");
+    static_assert(kNSlot >= 2, "TMEM budget: the exact group path needs NT <= 32");
     static_assert(kARegion + kNSlot * kSlotCols <= 512, "TMEM budget");
     static_assert(kHalf % 2 == 0, "paired f32x2 epilogue math");
+};
+
+// Group scales of (tile, stage) for one weight row: 16 bytes (8 groups of
+// fp16) after the stage's weights, read through the read-only path two stages
+// ahead of use.
+struct ScaleCursor {
+    int t, st;
+    const uint8_t* base;  // weights of the current tile
 };
 
 struct TileCoord {
@@ -108,12 +157,28 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const int* tb, const int
     return c;
 }
 
-// Group scales of (tile, stage) for one weight row: 16 bytes, kKPS k-blocks x 4
-// groups of fp16, read through the read-only path two stages ahead of use.
-struct ScaleCursor {
-    int t, st;
-    const uint8_t* base;  // scales of the current tile
-};
+// Group-32 packed word (8 offset-binary nibbles; k = 8w + j, j even in nibble
+// j/2, j odd in nibble 4 + j/2) -> fp16 pairs (k 2i, 2i+1) times the group
+// scale: (1024 + n) - 1032 = w exactly, then one rounding of w * s.
+__device__ __forceinline__ void g32_word_to_half(uint32_t word, __half2 s2, uint32_t* out) {
+    const __half2 bias = __float2half2_rn(1032.0f);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t h = ((word >> (4 * i)) & 0x000F000Fu) | 0x64006400u;
+        const __half2 w = __hsub2(*reinterpret_cast<const __half2*>(&h), bias);
+        const __half2 v = __hmul2(w, s2);
+        out[i] = *reinterpret_cast<const uint32_t*>(&v);
+    }
+}
+
+// The same word -> 16*w as int8 in k order (two words: k 0..3, k 4..7).
+__device__ __forceinline__ void g32_word_to_i8(uint32_t word, uint32_t* out) {
+    const uint32_t t = word ^ 0x88888888u;        // offset-binary -> two's complement
+    const uint32_t lo = (t << 4) & 0xF0F0F0F0u;   // nibbles 0,2,4,6 = k 0,4,1,5
+    const uint32_t hi = t & 0xF0F0F0F0u;          // nibbles 1,3,5,7 = k 2,6,3,7
+    out[0] = __byte_perm(lo, hi, 0x6420);         // k 0,1,2,3
+    out[1] = __byte_perm(lo, hi, 0x7531);         // k 4,5,6,7
+}
 
 template <int FMT, int EPI, int NT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -130,7 +195,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     uint64_t* lfull = bars;             // TMA bytes of stage s landed
     uint64_t* lempty = lfull + SL;      // MMAs that read stage s completed
     uint64_t* ofull = lempty + SL;      // W4 operand slot a unpacked into TMEM
-    uint64_t* tfull = ofull + (AS > 0 ? AS : 1);
+    uint64_t* tfull = ofull + AS1;
     uint64_t* tempty = tfull + C::kNSlot;
     uint64_t* done = tempty + C::kNSlot;
     int* tcnt = reinterpret_cast<int*>(done + 1);
@@ -141,9 +206,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int E = a.num_experts;
-    // k-block j (< kKPS) of stage s
-    auto act_at = [&](int s, int j) { return load + s * C::kLoadBytes + j * C::kActBytes; };
-    auto w_at = [&](int s) { return load + s * C::kLoadBytes + kKPS * C::kActBytes; };
+    auto act_at = [&](int s) { return load + s * C::kLoadBytes; };
+    auto w_at = [&](int s) { return load + s * C::kLoadBytes + C::kStageAct; };
 
     if (threadIdx.x == 0) {
         abort_s = 0;
@@ -160,7 +224,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
         fence_barrier_init();
     }
     // tile table: tcnt[e] = token tiles of expert e, tb[e] = its first tile index
-    if (warp == 2) {
+    if (warp == kConvWarp0) {
         const int per = (E + 31) / 32;
         int local = 0;
         for (int i = 0; i < per; ++i) {
@@ -188,11 +252,11 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
         }
         if (lane == 31) total_tiles_s = incl * a.row_tiles;
     }
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         tmem_alloc(&tmem_base_s, C::kAllocCols);
         tmem_relinquish();
     }
-    if (warp == 0 && lane == 0) prefetch_tensormap(&act_map);
+    if (warp == kProdWarp && lane == 0) prefetch_tensormap(&act_map);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -205,9 +269,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     // lane quadrant of this warp's TMEM accesses
     const int quad = warp & 3;
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-    const int half = (warp - kEpiWarp0) >> 2;  // epilogue column half (0..1)
     if (C::kGroup && warp >= kEpiWarp0) {
         // every group buffer starts as the float 12582912.0
+        const int half = (warp - kEpiWarp0) >> 2;
         for (int b = 0; b < C::kNSlot * 4; ++b)
             tmem_fill<C::kHalf>(acc_base + lane_addr + b * NT + half * C::kHalf, kMagicBits);
         tmem_wait_st();
@@ -216,7 +280,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     __syncthreads();
     tc_fence_after();
 
-    if (warp == 0) {
+    if (warp == kProdWarp) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             uint32_t it = 0;  // stage counter
@@ -232,9 +296,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&lfull[s], C::kStageW + kKPS * C::kActBytes);
-                    bulk_g2s(w_at(s), wtile + (size_t)st * C::kStageW, C::kStageW, &lfull[s]);
-                    tma_load_3d(act_at(s, 0), &act_map, 0, row0, st * kKPS, &lfull[s]);
+                    mbar_arrive_expect_tx(&lfull[s], C::kStageW + C::kStageAct);
+                    bulk_g2s(w_at(s), wtile + (size_t)st * a.w_stage_stride, C::kStageW, &lfull[s]);
+                    tma_load_3d(act_at(s), &act_map, 0, row0, st * C::kAtoms, &lfull[s]);
                 }
             }
             // drain: every issued copy lands before the CTA can exit
@@ -242,15 +306,13 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             for (uint32_t d = it > (uint32_t)SL ? it - SL : 0u; d < it; ++d)
                 mbar_wait(&lfull[d % SL], (d / SL) & 1u, &never, a.err);
         }
-    } else if (warp == 1) {
+    } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
-        // At most one tcgen05.commit per k-block (TMEM slot full) plus one per
-        // stage (stage empty). Each mbarrier wait on this thread stalls the MMA
-        // issue (~150 cycles even when the phase is complete), so it waits on as
-        // few as possible: W4 stages only on the unpack warps' barrier (they
-        // waited for the stage's copies first), W8 stages on the copies.
+        // One tcgen05.commit per stage (stage empty, which also frees the W4
+        // operand slot) and per tile (accumulator full); the exact group path
+        // commits per k-block instead of per tile.
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_i8(kTileRows, NT);
+            constexpr uint32_t idesc = C::kF16 ? idesc_f16(kTileRows, NT) : idesc_i8(kTileRows, NT);
             uint32_t it = 0, kbc = 0, ti = 0;  // stage, k-block and tile counters
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++ti) {
@@ -264,43 +326,57 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                 for (int st = 0; st < kstages && ok; ++st, ++it) {
                     const int s = it % SL;
                     const int ao = it % AS1;
+                    // W4 stages: the unpack warps' barrier alone (they waited for the
+                    // stage's copies before arriving); W8 stages: the copies
                     if (C::kW4 ? !mbar_wait(&ofull[ao], (it / AS1) & 1u, abort_flag, a.err)
                                : !mbar_wait(&lfull[s], (it / SL) & 1u, abort_flag, a.err)) {
                         ok = false;
                         break;
                     }
+                    tc_fence_after();
+                    const uint32_t ab = smem_u32(act_at(s));
+                    const uint32_t a_tmem = tmem_base + ao * C::kStageACols;
+                    if constexpr (C::kF16) {
+                        // 16 MMAs of k = 16: A columns 8j.., B atom j/4 at byte 32*(j%4)
 #pragma unroll
-                    for (int jk = 0; jk < kKPS; ++jk, ++kbc) {
-                        uint32_t slot = 0;
-                        if (C::kGroup) {
-                            slot = kbc % C::kNSlot;
-                            if (!mbar_wait(&tempty[slot], ((kbc / C::kNSlot) & 1u) ^ 1u, abort_flag,
-                                           a.err)) {
-                                ok = false;
-                                break;
+                        for (int j = 0; j < C::kMmaPerStage; ++j) {
+                            const uint64_t db = smem_desc_k_sw128(ab + (j >> 2) * NT * 128 + 32 * (j & 3));
+                            mma_f16_ts(acc_base + dcol, a_tmem + 8 * j, db, idesc,
+                                       (st > 0 || j > 0) ? 1u : 0u);
+                        }
+                    } else {
+#pragma unroll
+                        for (int jk = 0; jk < kKPS; ++jk, ++kbc) {
+                            uint32_t slot = 0;
+                            if (C::kGroup) {
+                                slot = kbc % C::kNSlot;
+                                if (!mbar_wait(&tempty[slot], ((kbc / C::kNSlot) & 1u) ^ 1u, abort_flag,
+                                               a.err)) {
+                                    ok = false;
+                                    break;
+                                }
+                                tc_fence_after();
                             }
-                        }
-                        tc_fence_after();
-                        const uint32_t ab = smem_u32(act_at(s, jk));
-                        const uint32_t a_tmem = tmem_base + (ao * kKPS + jk) * C::kACols;
-                        const uint32_t wa = smem_u32(w_at(s) + jk * C::kWBytes);
+                            const uint32_t abk = ab + jk * NT * 128;
+                            const uint32_t wa = smem_u32(w_at(s) + jk * kTileRows * kKBlock);
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const uint64_t db = smem_desc_k_sw128(ab + 32 * j);
-                            const uint32_t d = C::kGroup ? acc_base + slot * C::kSlotCols + j * NT
-                                                         : acc_base + dcol;
-                            // group formats: each buffer adds one group's sum to the
-                            // magic float; per-channel formats: accumulate over K
-                            const uint32_t acc = C::kGroup ? 1u : ((st > 0 || jk > 0 || j > 0) ? 1u : 0u);
-                            if (C::kW4)
-                                mma_i8_ts(d, a_tmem + 8 * j, db, idesc, acc);
-                            else
-                                mma_i8(d, smem_desc_k_sw128(wa + 32 * j), db, idesc, acc);
+                            for (int j = 0; j < 4; ++j) {
+                                const uint64_t db = smem_desc_k_sw128(abk + 32 * j);
+                                // exact group path: each buffer adds one group's sum to the
+                                // magic float; per-channel: accumulate over K
+                                const uint32_t d = C::kGroup ? acc_base + slot * C::kSlotCols + j * NT
+                                                             : acc_base + dcol;
+                                const uint32_t acc =
+                                    C::kGroup ? 1u : ((st > 0 || jk > 0 || j > 0) ? 1u : 0u);
+                                if (C::kW4)
+                                    mma_i8_ts(d, a_tmem + jk * 32 + 8 * j, db, idesc, acc);
+                                else
+                                    mma_i8(d, smem_desc_k_sw128(wa + 32 * j), db, idesc, acc);
+                            }
+                            if (C::kGroup) mma_commit(&tfull[slot]);
                         }
-                        if (C::kGroup) mma_commit(&tfull[slot]);
+                        if (!ok) break;
                     }
-                    if (!ok) break;
-                    // also frees the stage's W4 operand slot for the unpack warps
                     mma_commit(&lempty[s]);
                 }
                 if (!C::kGroup && ok) mma_commit(&tfull[ti % 2u]);
@@ -310,7 +386,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             int never = 0;
             mbar_wait(done, 0, &never, a.err);
         }
-    } else if (warp < kEpiWarp0) {
+    } else if (warp >= kConvWarp0 && warp < kConvWarp0 + kConvWarps) {
         // ------------------------------------------------------------ int4 unpack
         if (C::kW4) {
             const int r = quad * 32 + lane;  // weight row = TMEM lane
@@ -335,56 +411,96 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                         break;
                     }
                     tc_fence_after();
+                    const uint32_t a_cols = tmem_base + lane_addr + ao * C::kStageACols;
+                    if constexpr (C::kG32Pack) {
+                        // row r: 128 bytes, 16-byte chunk c = group c of the stage at
+                        // position c ^ (r & 7)
+                        const uint8_t* rowp = w_at(s) + r * 128;
+                        if constexpr (C::kF16) {
+                            const uint4 sc = *reinterpret_cast<const uint4*>(w_at(s) + 128 * 128 + r * 16);
+                            const uint32_t sw[4] = {sc.x, sc.y, sc.z, sc.w};
 #pragma unroll
-                    for (int jk = 0; jk < kKPS; ++jk) {
-                        // row r of the k-block: 64 bytes in four 16-byte chunks,
-                        // chunk c stored at position c ^ ((r >> 1) & 3) (conflict-free)
-                        const uint8_t* rowp = w_at(s) + jk * C::kWBytes + r * 64;
-                        uint32_t o[32];
+                            for (int cp = 0; cp < 4; ++cp) {  // two chunks = 32 columns
+                                uint32_t o[32];
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            const uint4 p =
-                                *reinterpret_cast<const uint4*>(rowp + ((c ^ ((r >> 1) & 3)) << 4));
-                            // packed byte b of word w holds k = 32c+8w+b (low nibble) and
-                            // k + 4 (high nibble); each lands as 16 * value.
-                            o[8 * c + 0] = (p.x << 4) & 0xF0F0F0F0u;
-                            o[8 * c + 1] = p.x & 0xF0F0F0F0u;
-                            o[8 * c + 2] = (p.y << 4) & 0xF0F0F0F0u;
-                            o[8 * c + 3] = p.y & 0xF0F0F0F0u;
-                            o[8 * c + 4] = (p.z << 4) & 0xF0F0F0F0u;
-                            o[8 * c + 5] = p.z & 0xF0F0F0F0u;
-                            o[8 * c + 6] = (p.w << 4) & 0xF0F0F0F0u;
-                            o[8 * c + 7] = p.w & 0xF0F0F0F0u;
+                                for (int h = 0; h < 2; ++h) {
+                                    const int c = 2 * cp + h;
+                                    const uint4 p = *reinterpret_cast<const uint4*>(rowp + ((c ^ (r & 7)) << 4));
+                                    const __half2 s2 = __half2half2(reinterpret_cast<const __half*>(sw)[c]);
+                                    g32_word_to_half(p.x, s2, o + 16 * h + 0);
+                                    g32_word_to_half(p.y, s2, o + 16 * h + 4);
+                                    g32_word_to_half(p.z, s2, o + 16 * h + 8);
+                                    g32_word_to_half(p.w, s2, o + 16 * h + 12);
+                                }
+                                tmem_st32(a_cols + 32 * cp, o);
+                            }
+                        } else {
+#pragma unroll
+                            for (int jk = 0; jk < kKPS; ++jk) {  // k-block: chunks 4jk..4jk+3
+                                uint32_t o[32];
+#pragma unroll
+                                for (int h = 0; h < 4; ++h) {
+                                    const int c = 4 * jk + h;
+                                    const uint4 p = *reinterpret_cast<const uint4*>(rowp + ((c ^ (r & 7)) << 4));
+                                    g32_word_to_i8(p.x, o + 8 * h + 0);
+                                    g32_word_to_i8(p.y, o + 8 * h + 2);
+                                    g32_word_to_i8(p.z, o + 8 * h + 4);
+                                    g32_word_to_i8(p.w, o + 8 * h + 6);
+                                }
+                                tmem_st32(a_cols + 32 * jk, o);
+                            }
                         }
-                        tmem_st32(tmem_base + lane_addr + (ao * kKPS + jk) * C::kACols, o);
+                    } else {
+#pragma unroll
+                        for (int jk = 0; jk < kKPS; ++jk) {
+                            // row r of the k-block: 64 bytes in four 16-byte chunks,
+                            // chunk c stored at position c ^ ((r >> 1) & 3) (conflict-free)
+                            const uint8_t* rowp = w_at(s) + jk * (kTileRows * kKBlock / 2) + r * 64;
+                            uint32_t o[32];
+#pragma unroll
+                            for (int c = 0; c < 4; ++c) {
+                                const uint4 p =
+                                    *reinterpret_cast<const uint4*>(rowp + ((c ^ ((r >> 1) & 3)) << 4));
+                                // packed byte b of word w holds k = 32c+8w+b (low nibble) and
+                                // k + 4 (high nibble); each lands as 16 * value.
+                                o[8 * c + 0] = (p.x << 4) & 0xF0F0F0F0u;
+                                o[8 * c + 1] = p.x & 0xF0F0F0F0u;
+                                o[8 * c + 2] = (p.y << 4) & 0xF0F0F0F0u;
+                                o[8 * c + 3] = p.y & 0xF0F0F0F0u;
+                                o[8 * c + 4] = (p.z << 4) & 0xF0F0F0F0u;
+                                o[8 * c + 5] = p.z & 0xF0F0F0F0u;
+                                o[8 * c + 6] = (p.w << 4) & 0xF0F0F0F0u;
+                                o[8 * c + 7] = p.w & 0xF0F0F0F0u;
+                            }
+                            tmem_st32(a_cols + 32 * jk, o);
+                        }
                     }
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
-                    // the MMA issuer waits on this barrier alone: these warps have
-                    // observed the stage's copies (lfull) before arriving
                     if (lane == 0) mbar_arrive(&ofull[ao]);
                 }
             }
         }
-    } else {
+    } else if (warp >= kEpiWarp0) {
         // ------------------------------------------------------------ epilogue
-        const int r = quad * 32 + lane;  // weight row within the tile = TMEM lane
-        const int c0 = half * C::kHalf;  // first token column of this warp
+        const int half = (warp - kEpiWarp0) >> 2;  // column half (0..1)
+        const int r = quad * 32 + lane;             // weight row within the tile = TMEM lane
+        const int c0 = half * C::kHalf;             // first token column of this warp
         // group scales: a cursor two stages ahead of use over the same tile order
         ScaleCursor cur{(int)blockIdx.x, 0, nullptr};
         auto cursor_tile = [&](ScaleCursor& k) {
             k.base = nullptr;
             if (k.t < total) {
                 const TileCoord c = decode_tile(k.t, tb, tcnt, E);
-                k.base = reinterpret_cast<const uint8_t*>(a.wscale) + (size_t)c.e * a.ws_expert_stride +
-                         (size_t)c.rt * a.ws_tile_stride;
+                k.base = a.w + (size_t)c.e * a.w_expert_stride + (size_t)c.rt * a.w_tile_stride;
             }
         };
         auto cursor_load = [&](ScaleCursor& k) -> uint4 {
             uint4 v = make_uint4(0u, 0u, 0u, 0u);
             if (k.base)
-                v = __ldg(reinterpret_cast<const uint4*>(k.base + ((size_t)k.st * kTileRows + r) * 16));
+                v = __ldg(reinterpret_cast<const uint4*>(k.base + (size_t)k.st * a.w_stage_stride +
+                                                         C::kStageW + r * 16));
             if (++k.st == kstages) {
                 k.st = 0;
                 k.t += gridDim.x;
@@ -393,8 +509,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             return v;
         };
         uint4 pf0 = make_uint4(0u, 0u, 0u, 0u), pf1 = pf0;
-        if (C::kGroup) {
-            static_assert(kKPS == 2 || !C::kGroup, "16 bytes of group scales per row and stage");
+        if (C::kGroup && EPI != kEpiAcc) {
             cursor_tile(cur);
             pf0 = cursor_load(cur);
             pf1 = cursor_load(cur);
@@ -417,25 +532,17 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                 col = c.rt * kTileRows + r;
             }
             const bool col_ok = col < a.n_valid;
-            // lane q prefetches the scale of token column c0 + q (one register across
-            // the K loop); the values are broadcast by shuffles at the tile end
+            const int ocol = is_up ? a.n_valid + col : col;  // gate | up halves of a row
+
+            // lane q prefetches the scale of token column c0 + q; broadcast by shuffles
             const float my_sx = (lane < C::kHalf && c0 + lane < nvalid) ? a.act_scale[row0 + c0 + lane]
                                                                         : 0.0f;
-            float wscale_pc = 0.0f;
-            if (!C::kGroup) {
-                const float* sp = reinterpret_cast<const float*>(
-                    reinterpret_cast<const uint8_t*>(a.wscale) + (size_t)c.e * a.ws_expert_stride +
-                    (size_t)c.rt * a.ws_tile_stride);
-                wscale_pc = sp[r];
-            }
-            // this warp's token columns hold no token at all (the expert's last tile):
-            // it still takes part in every slot handshake but skips the loads and math
-            const bool active = c0 < nvalid;
-            float2 facc[C::kHalf / 2];
+            if constexpr (C::kGroup) {
+                // one slot of 4 group buffers per k-block: load, re-arm, release, fold
+                float2 facc[C::kHalf / 2];
 #pragma unroll
-            for (int q = 0; q < C::kHalf / 2; ++q) facc[q] = make_float2(0.0f, 0.0f);
-
-            if (C::kGroup) {
+                for (int q = 0; q < C::kHalf / 2; ++q) facc[q] = make_float2(0.0f, 0.0f);
+                const bool active = c0 < nvalid;  // idle warps still take part in the handshakes
                 for (int st = 0; st < kstages && ok; ++st) {
                     const uint4 sc = pf0;
                     pf0 = pf1;
@@ -446,18 +553,15 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                     {
                         const uint32_t w[4] = {sc.x, sc.y, sc.z, sc.w};
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            sg[i] = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-                            if (C::kW4) sg[i] = __fmul2_rn(sg[i], make_float2(0.0625f, 0.0625f));
-                        }
+                        for (int i = 0; i < 4; ++i)
+                            sg[i] = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&w[i])),
+                                               make_float2(0.0625f, 0.0625f));
                     }
 #pragma unroll 1
                     for (int jk = 0; jk < kKPS; ++jk, ++it) {
                         const int kb = st * kKPS + jk;
                         const float2 sga = jk ? sg[2] : sg[0];  // groups 0, 1 of this k-block
                         const float2 sgb = jk ? sg[3] : sg[1];  // groups 2, 3
-                        // one TMEM slot per k-block: wait once, load its four group
-                        // buffers, re-arm them, release the slot, then do the math
                         const uint32_t slot = it % C::kNSlot;
                         if (!mbar_wait(&tfull[slot], (it / C::kNSlot) & 1u, abort_flag, a.err)) {
                             ok = false;
@@ -469,7 +573,6 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                         // round is loaded, re-armed and folded into its columns' sums
                         // (the group order per column stays 0..3)
                         constexpr int kRound = C::kHalf < 8 ? C::kHalf : 8;
-                        const int ncol = is_up ? a.n_valid + col : col;
 #pragma unroll
                         for (int r0 = 0; r0 < C::kHalf; r0 += kRound) {
                             uint32_t v[4][kRound];
@@ -486,17 +589,12 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                             if (!active) continue;
                             if (EPI == kEpiAcc) {
 #pragma unroll
-                                for (int j = 0; j < 4; ++j) {
+                                for (int j = 0; j < 4; ++j)
 #pragma unroll
-                                    for (int q = 0; q < kRound; ++q) {
-                                        if (c0 + r0 + q < nvalid && col_ok) {
-                                            int acc = (int)(v[j][q] - kMagicBits);
-                                            if (C::kW4) acc >>= 4;
+                                    for (int q = 0; q < kRound; ++q)
+                                        if (c0 + r0 + q < nvalid && col_ok)
                                             a.acc_out[((size_t)(row0 + c0 + r0 + q) * (a.kblocks * 4) + kb * 4 +
-                                                       j) * a.acc_ld + ncol] = acc;
-                                        }
-                                    }
-                                }
+                                                       j) * a.acc_ld + ocol] = (int)(v[j][q] - kMagicBits) >> 4;
                             } else {
                                 const float2 nm = make_float2(-kMagic, -kMagic);
 #pragma unroll
@@ -520,52 +618,61 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                         if (lane == 0) mbar_arrive(&tempty[slot]);
                     }
                 }
-                if (!ok) break;
-            } else {
-                const uint32_t buf = ti % 2u;
-                if (!mbar_wait(&tfull[buf], (ti / 2u) & 1u, abort_flag, a.err)) break;
-                tc_fence_after();
-                uint32_t v[C::kHalf];
-                tmem_ld<C::kHalf>(acc_base + lane_addr + buf * NT + c0, v);
-                tmem_wait_ld();
-                tmem_ld_pin(v);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[buf]);
+                if (EPI == kEpiAcc || !ok) continue;
 #pragma unroll
                 for (int q = 0; q < C::kHalf; ++q) {
-                    int acc = (int)v[q];
-                    if (C::kW4) acc >>= 4;
-                    if (EPI == kEpiAcc) {
-                        if (c0 + q < nvalid && col_ok) {
-                            const int ncol = is_up ? a.n_valid + col : col;
-                            a.acc_out[(size_t)(row0 + c0 + q) * a.acc_ld + ncol] = acc;
-                        }
-                    } else {
-                        const float f = __int2float_rn(acc);
-                        if (q & 1) facc[q >> 1].y = f; else facc[q >> 1].x = f;
-                    }
+                    const int j = c0 + q;
+                    const float sxq = __shfl_sync(0xffffffffu, my_sx, q);
+                    const float f = (q & 1) ? facc[q >> 1].y : facc[q >> 1].x;
+                    if (j < nvalid && col_ok)
+                        a.out[(size_t)(row0 + j) * a.ldo + (EPI == kEpiGateUp ? ocol : col)] = __fmul_rn(f, sxq);
                 }
+                continue;
             }
-            if (EPI == kEpiAcc) continue;
 
-            // dequantise with the per-token activation scale
-            float val[C::kHalf];
+            float wscale_pc = 0.0f;
+            if (!C::kF16) {
+                const float* sp = reinterpret_cast<const float*>(
+                    reinterpret_cast<const uint8_t*>(a.wscale) + (size_t)c.e * a.ws_expert_stride +
+                    (size_t)c.rt * a.ws_tile_stride);
+                wscale_pc = sp[r];
+            }
+            const uint32_t buf = ti % 2u;
+            if (!mbar_wait(&tfull[buf], (ti / 2u) & 1u, abort_flag, a.err)) break;
+            tc_fence_after();
+            // the warp's columns in chunks of at most 32 (registers)
+            constexpr int kChunk = C::kHalf < 32 ? C::kHalf : 32;
+            uint32_t v[C::kHalf];
+#pragma unroll
+            for (int q0 = 0; q0 < C::kHalf; q0 += kChunk) {
+                uint32_t (&vc)[kChunk] = *reinterpret_cast<uint32_t(*)[kChunk]>(v + q0);
+                tmem_ld<kChunk>(acc_base + lane_addr + buf * NT + c0 + q0, vc);
+            }
+            tmem_wait_ld();
+            tmem_ld_pin(v);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
 #pragma unroll
             for (int q = 0; q < C::kHalf; ++q) {
-                const float sxq = __shfl_sync(0xffffffffu, my_sx, q);
-                const float f = (q & 1) ? facc[q >> 1].y : facc[q >> 1].x;
-                if (C::kGroup)
-                    val[q] = __fmul_rn(f, sxq);
-                else
-                    val[q] = __fmul_rn(__fmul_rn(f, sxq), wscale_pc);
-            }
-            if (col_ok) {
-                // gate/up tiles: gate channels to the first half of the row, up to the second
-                const int ocol = (EPI == kEpiGateUp && is_up) ? a.n_valid + col : col;
-#pragma unroll
-                for (int q = 0; q < C::kHalf; ++q)
-                    if (c0 + q < nvalid) a.out[(size_t)(row0 + c0 + q) * a.ldo + ocol] = val[q];
+                const int j = c0 + q;
+                if (EPI == kEpiAcc) {
+                    int acc = (int)v[q];
+                    if (C::kW4) acc >>= 4;
+                    if (j < nvalid && col_ok) a.acc_out[(size_t)(row0 + j) * a.acc_ld + ocol] = acc;
+                } else {
+                    const float sxq = __shfl_sync(0xffffffffu, my_sx, q);
+                    float val;
+                    if (C::kF16) {
+                        val = __fmul_rn(__uint_as_float(v[q]), sxq);
+                    } else {
+                        int acc = (int)v[q];
+                        if (C::kW4) acc >>= 4;
+                        val = __fmul_rn(__fmul_rn(__int2float_rn(acc), sxq), wscale_pc);
+                    }
+                    if (j < nvalid && col_ok)
+                        a.out[(size_t)(row0 + j) * a.ldo + (EPI == kEpiGateUp ? ocol : col)] = val;
+                }
             }
         }
         if (!ok) *abort_flag = 1;
@@ -573,7 +680,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem_base, C::kAllocCols);
     }
@@ -620,11 +727,15 @@ static int launch_gemm_nt(const CUtensorMap& map, const GemmArgs& a, int nt, int
 template <int FMT>
 static int launch_gemm_epi(const CUtensorMap& map, const GemmArgs& a, int epi, int nt,
                            int num_sms, cudaStream_t s) {
-    switch (epi) {
-        case kEpiGateUp: return launch_gemm_nt<FMT, kEpiGateUp>(map, a, nt, num_sms, s);
-        case kEpiStore: return launch_gemm_nt<FMT, kEpiStore>(map, a, nt, num_sms, s);
-        case kEpiAcc: return launch_gemm_nt<FMT, kEpiAcc>(map, a, nt, num_sms, s);
-        default: return -1;
+    {
+        switch (epi) {
+            case kEpiGateUp: return launch_gemm_nt<FMT, kEpiGateUp>(map, a, nt, num_sms, s);
+            case kEpiStore: return launch_gemm_nt<FMT, kEpiStore>(map, a, nt, num_sms, s);
+            case kEpiAcc:
+                if constexpr (FMT != kFmtW4G32H) return launch_gemm_nt<FMT, kEpiAcc>(map, a, nt, num_sms, s);
+                return -1;
+            default: return -1;
+        }
     }
 }
 
@@ -632,6 +743,7 @@ int launch_gemm(const CUtensorMap& map, const GemmArgs& a, int fmt, int epi, int
                 int num_sms, cudaStream_t s) {
     switch (fmt) {
         case kFmtW4G32: return launch_gemm_epi<kFmtW4G32>(map, a, epi, nt, num_sms, s);
+        case kFmtW4G32H: return launch_gemm_epi<kFmtW4G32H>(map, a, epi, nt, num_sms, s);
         case kFmtW4PC: return launch_gemm_epi<kFmtW4PC>(map, a, epi, nt, num_sms, s);
         case kFmtW8PC: return launch_gemm_epi<kFmtW8PC>(map, a, epi, nt, num_sms, s);
         default: return -1;

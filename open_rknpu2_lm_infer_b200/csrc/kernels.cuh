@@ -7,8 +7,12 @@
 
 namespace moe {
 
-// Weight formats (values match MOE_B200_W* in include/moe_b200.h).
-enum { kFmtW4PC = 0, kFmtW4G32 = 1, kFmtW8PC = 2 };
+// Weight formats (values 0..2 match MOE_B200_W* in include/moe_b200.h).
+// kFmtW4G32 runs on the int8 tensor cores with one exact int32 sum per group
+// (the accumulator dump); kFmtW4G32H is the same packed bank on the fp16
+// tensor cores: the unpack warps write w * s_group (one fp16 rounding) and
+// the MMA accumulates all of K in fp32, one accumulator per tile.
+enum { kFmtW4PC = 0, kFmtW4G32 = 1, kFmtW8PC = 2, kFmtW4G32H = 3 };
 // GEMM epilogues. GateUp: a gate/up tile (64 gate + 64 up channels) stores its
 // dequantised values as gate | up halves of a [rows][2n] row, the layout the
 // SwiGLU of the requantisation kernel reads. Store: [rows][n]. Acc: int32 dump.
@@ -37,6 +41,7 @@ struct GemmArgs {
     const uint8_t* w;         // tile-major packed weights
     size_t w_expert_stride;   // bytes
     size_t w_tile_stride;     // bytes per 128-row tile (all k-blocks)
+    size_t w_stage_stride;    // bytes per load stage within a tile
     const void* wscale;       // scales, tile-major
     size_t ws_expert_stride;  // bytes
     size_t ws_tile_stride;    // bytes
@@ -64,11 +69,13 @@ void launch_route_count(const int32_t* ids, const float* routes, int n, int E, i
 void launch_route_scatter(const int32_t* ids, const float* routes, int n, int E,
                           const int32_t* hist, int32_t* offsets, int32_t* perm, int32_t* pos,
                           int32_t* shared_offsets, int T, cudaStream_t s);
+// h_rows / h_perm / qh (may be null): the same codes as fp16, for kFmtW4G32H.
 void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k,
                          const int32_t* pos, int8_t* q_rows, float* s_rows, int8_t* q_perm,
-                         float* s_perm, uint32_t* err, cudaStream_t s);
+                         float* s_perm, __half* h_rows, __half* h_perm, uint32_t* err,
+                         cudaStream_t s);
 void launch_requant(const float* gate_up, const int32_t* count, int max_rows, int I, int ld_q,
-                    int rule, int8_t* q, float* sc, cudaStream_t s);
+                    int rule, int8_t* q, __half* qh, float* sc, cudaStream_t s);
 void launch_combine(const float* y, const int32_t* pos, const float* routes, const float* shared,
                     const float* residual, int T, int H, int k, float* out, cudaStream_t s);
 
