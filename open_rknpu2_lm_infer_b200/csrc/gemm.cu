@@ -55,10 +55,7 @@ namespace moe {
 constexpr int kProdWarp = 0;          // copy producer
 constexpr int kMmaWarp = 1;           // TMEM allocator + MMA issuer
 constexpr int kConvWarp0 = 2;         // first unpack warp
-constexpr int kConvWarps = 4;
-constexpr int kEpiWarp0 = 6;          // first epilogue warp
 constexpr int kEpiWarps = 8;
-constexpr int kGemmThreads = 32 * (kEpiWarp0 + kEpiWarps);
 constexpr int kTileRows = 128;        // weight rows per tile (MMA M)
 constexpr int kKBlock = 128;          // int8 k per k-block (one 128-byte swizzle row)
 constexpr int kStageK = kKPS * kKBlock;  // k per load stage (256)
@@ -120,6 +117,11 @@ struct GemmCfg {
     static constexpr int kAllocCols = 512;
     static constexpr int kHalf = NT / 2;                      // columns per epilogue warp
     static constexpr int kMmaPerStage = kF16 ? kStageK / 16 : kKPS * 4;
+    // unpack warps: one per TMEM lane quadrant; two for the fp16 conversion
+    // (each converts half of a stage's groups), the heaviest per weight
+    static constexpr int kConvWarps = kF16 ? 8 : 4;
+    static constexpr int kEpiWarp0 = kConvWarp0 + kConvWarps;  // first epilogue warp
+    static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
     static_assert(kLoadBytes % 1024 == 0, "stage alignment of the swizzled operands");
     static_assert(kLoadStages >= 2, "smem budget");
     static_assert(kLoadStages >= kAStages, "operand ring reuse is ordered by the load ring");
@@ -181,7 +183,7 @@ __device__ __forceinline__ void g32_word_to_i8(uint32_t word, uint32_t* out) {
 }
 
 template <int FMT, int EPI, int NT>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(GemmCfg<FMT, NT>::kThreads, 1)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs a) {
     using C = GemmCfg<FMT, NT>;
     constexpr int SL = C::kLoadStages;
@@ -215,7 +217,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             mbar_init(&lfull[i], 1);
             mbar_init(&lempty[i], 1);
         }
-        for (int i = 0; i < AS; ++i) mbar_init(&ofull[i], kConvWarps);
+        for (int i = 0; i < AS; ++i) mbar_init(&ofull[i], C::kConvWarps);
         for (int i = 0; i < C::kNSlot; ++i) {
             mbar_init(&tfull[i], 1);
             mbar_init(&tempty[i], kEpiWarps);
@@ -269,9 +271,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     // lane quadrant of this warp's TMEM accesses
     const int quad = warp & 3;
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-    if (C::kGroup && warp >= kEpiWarp0) {
+    if (C::kGroup && warp >= C::kEpiWarp0) {
         // every group buffer starts as the float 12582912.0
-        const int half = (warp - kEpiWarp0) >> 2;
+        const int half = (warp - C::kEpiWarp0) >> 2;
         for (int b = 0; b < C::kNSlot * 4; ++b)
             tmem_fill<C::kHalf>(acc_base + lane_addr + b * NT + half * C::kHalf, kMagicBits);
         tmem_wait_st();
@@ -386,7 +388,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             int never = 0;
             mbar_wait(done, 0, &never, a.err);
         }
-    } else if (warp >= kConvWarp0 && warp < kConvWarp0 + kConvWarps) {
+    } else if (warp >= kConvWarp0 && warp < kConvWarp0 + C::kConvWarps) {
         // ------------------------------------------------------------ int4 unpack
         if (C::kW4) {
             const int r = quad * 32 + lane;  // weight row = TMEM lane
@@ -418,15 +420,21 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                         const uint8_t* rowp = w_at(s) + r * 128;
                         if constexpr (C::kF16) {
                             const uint4 sc = *reinterpret_cast<const uint4*>(w_at(s) + 128 * 128 + r * 16);
-                            const uint32_t sw[4] = {sc.x, sc.y, sc.z, sc.w};
+                            const int sub = (warp - kConvWarp0) >> 2;  // which half of the groups
+                            // this warp's 4 group scales (fp16 pairs): groups 4*sub .. 4*sub+3
+                            const uint32_t sg01 = sub ? sc.z : sc.x, sg23 = sub ? sc.w : sc.y;
 #pragma unroll
-                            for (int cp = 0; cp < 4; ++cp) {  // two chunks = 32 columns
+                            for (int cq = 0; cq < 2; ++cq) {  // two chunks = 32 columns
+                                const int cp = 2 * sub + cq;
                                 uint32_t o[32];
 #pragma unroll
                                 for (int h = 0; h < 2; ++h) {
-                                    const int c = 2 * cp + h;
+                                    const int cl = 2 * cq + h;  // group within this warp's four
+                                    const int c = 4 * sub + cl;
                                     const uint4 p = *reinterpret_cast<const uint4*>(rowp + ((c ^ (r & 7)) << 4));
-                                    const __half2 s2 = __half2half2(reinterpret_cast<const __half*>(sw)[c]);
+                                    const uint32_t sw = cl < 2 ? sg01 : sg23;
+                                    const __half2 s2 = __half2half2(__ushort_as_half(
+                                        (unsigned short)((cl & 1) ? (sw >> 16) : (sw & 0xFFFFu))));
                                     g32_word_to_half(p.x, s2, o + 16 * h + 0);
                                     g32_word_to_half(p.y, s2, o + 16 * h + 4);
                                     g32_word_to_half(p.z, s2, o + 16 * h + 8);
@@ -482,9 +490,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                 }
             }
         }
-    } else if (warp >= kEpiWarp0) {
+    } else if (warp >= C::kEpiWarp0) {
         // ------------------------------------------------------------ epilogue
-        const int half = (warp - kEpiWarp0) >> 2;  // column half (0..1)
+        const int half = (warp - C::kEpiWarp0) >> 2;  // column half (0..1)
         const int r = quad * 32 + lane;             // weight row within the tile = TMEM lane
         const int c0 = half * C::kHalf;             // first token column of this warp
         // group scales: a cursor two stages ahead of use over the same tile order
@@ -707,7 +715,7 @@ static int launch_gemm_t(const CUtensorMap& map, const GemmArgs& a, int num_sms,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const long upper = ((long)(a.max_rows + NT - 1) / NT + a.num_experts) * a.row_tiles;
     const int grid = (int)(upper < num_sms ? (upper > 0 ? upper : 1) : num_sms);
-    grouped_gemm_kernel<FMT, EPI, NT><<<grid, kGemmThreads, smem, s>>>(map, a);
+    grouped_gemm_kernel<FMT, EPI, NT><<<grid, GemmCfg<FMT, NT>::kThreads, smem, s>>>(map, a);
     return 0;
 }
 
