@@ -124,15 +124,17 @@ def layer_bytes(spec, T, U, A):
     H, I = spec.hidden, spec.inter
     w = 3 * H * I // 2 + 3 * H * I // 32 * 2          # int4 codes + fp16 group scales
     b = U * w + spec.experts * H * 4 + 3 * T * H * 4  # router f32, x in, residual, out
-    b += A * H + A * I * 4 * 2 + A * I + A * H * 4 * 2  # permuted rows, middle, codes, y
+    # permuted int8 rows; gate | up f32 written and read; middle codes int8 + fp16; y
+    b += A * H + A * 2 * I * 4 * 2 + A * I * 3 + A * H * 4 * 2
     return b
 
 
 def gate_up_bytes(spec, U, A):
     """Algorithmic bytes of one gate/up GEMM launch: int4 codes + fp16 scales of
-    the experts hit, the permuted int8 activation rows, the fp32 middle written."""
+    the experts hit, the permuted int8 activation rows, the f32 gate | up rows
+    written."""
     H, I = spec.hidden, spec.inter
-    return U * (2 * I * H // 2 + 2 * I * H // 32 * 2) + A * H + A * I * 4
+    return U * (2 * I * H // 2 + 2 * I * H // 32 * 2) + A * H + A * 2 * I * 4
 
 
 # ---------------------------------------------------------------- ours
@@ -237,7 +239,7 @@ def run_ours(args):
     traffic = measured_traffic(f"{CONFIG}_T{T}_gate_up")
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                 "frac": (achieved / hbm_peak) if achieved else None, "traffic": traffic,
-                "kernel": "grouped_gemm_kernel<W4G32, SwiGLU> (gate/up)",
+                "kernel": "grouped_gemm_kernel<W4G32, GateUp> (gate/up, exact int8 group sums)",
                 "algorithmic_bytes_per_launch": gu_bytes, "kernel_us": gate_us,
                 "peak_kind": f"{pk_kind} (hbm_gbs, STREAM-style copy)"}
 
