@@ -11,8 +11,10 @@ SwiGLU, requant, down GEMM, combine + residual) on inputs resident in HBM.
 input/residual copied from pinned host memory and the output read back.
 Decode (T=1) and 4096-token prefill are reported under "extra".
 
-With N > 1 (torchrun) every rank runs its own replica of the layer on its own
-512 tokens (weak scaling); the time is the max over ranks.
+With N > 1 (torchrun) the layer runs expert parallel: rank g owns experts
+[g*E/N, (g+1)*E/N) and routes its own 512 tokens, rows travel to the expert
+owners and back with NCCL all-to-all (weak scaling); the time is the max over
+ranks.
 `--impl reference` times the CPU restatement of the reference path (the
 oracle, all host threads) on the same workload, on rank 0 only.
 """
@@ -287,6 +289,145 @@ def run_ours(args):
         print(json.dumps(result), flush=True)
 
 
+def run_ep(args):
+    """N > 1: the expert-parallel layer (open_rknpu2_lm_infer_b200.ep). Rank g
+    owns experts [g*E/N, (g+1)*E/N) and routes its own 512 tokens; rows travel
+    to the expert owners and back with NCCL all-to-all. Weak scaling: the
+    tokens per GPU are fixed; the time is the max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from open_rknpu2_lm_infer_b200 import _lib as L
+    from open_rknpu2_lm_infer_b200 import synthetic as S
+    from open_rknpu2_lm_infer_b200.ep import DeviceOps, ep_forward
+    from open_rknpu2_lm_infer_b200.moe import Backend
+
+    world, rank, local = setup_dist()
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    spec = S.CONFIGS[CONFIG]
+    T = args.tokens
+    P = spec.experts // world
+    layer = S.make_layer(spec, seed=SEED)
+    be = Backend(device=local, max_rows=world * T)
+    moe = be.load_moe(layer.gate[rank * P:(rank + 1) * P], layer.down[rank * P:(rank + 1) * P],
+                      spec.top)
+    router = be.router(layer.router, spec.top, layer.bias)
+    ops = DeviceOps(be, moe, router, world, T)
+    lib = be.lib
+    x = torch.from_numpy(S.make_input(spec, T, seed=SEED + rank, stream=4)).cuda()
+    res = torch.from_numpy(S.make_input(spec, T, seed=SEED + rank, stream=5)).cuda()
+    stream = torch.cuda.current_stream()
+
+    def step():
+        return ep_forward(ops, dist, None, x, res)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ops.status()
+    dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    lib.moe_b200_workspace_profile(moe.workspace, 1)
+    launches0 = lib.moe_b200_workspace_launches(ops.ws) + lib.moe_b200_workspace_launches(moe.workspace)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sent = recv = 0
+    e0.record(stream)
+    for _ in range(args.steps):
+        _, plan = step()
+        sent += plan.n_send
+        recv += plan.n_recv
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = clocks.stop()
+    launches = (lib.moe_b200_workspace_launches(ops.ws) +
+                lib.moe_b200_workspace_launches(moe.workspace) - launches0)
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    stages = []
+    for i in range(args.steps):
+        tm = L.Timings()
+        if lib.moe_b200_workspace_profile_read(moe.workspace, i, tm) == 0:
+            stages.append(tm.as_dict())
+    lib.moe_b200_workspace_profile(moe.workspace, 0)
+    gate_us = statistics.mean(s_["gate_us"] for s_ in stages) if stages else float("nan")
+    rows_here = recv // max(args.steps, 1)
+    # the experts of this rank hit by its received rows: all of them at this size
+    U = P
+    gu_bytes = gate_up_bytes(spec, U, rows_here)
+    pk, pk_kind = peaks()
+    hbm_peak = pk["hbm_gbs"]
+    achieved = gu_bytes / (gate_us * 1e-6) / 1e9 if gate_us == gate_us and gate_us > 0 else None
+
+    # e2e: pinned host input/residual copied in and the output read back per step
+    xh = torch.empty((T, spec.hidden), dtype=torch.float32, pin_memory=True)
+    rh = torch.empty_like(xh, pin_memory=True)
+    oh = torch.empty_like(xh, pin_memory=True)
+    xh.copy_(x.cpu())
+    rh.copy_(res.cpu())
+    dist.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        x.copy_(xh, non_blocking=True)
+        res.copy_(rh, non_blocking=True)
+        out, _ = step()
+        oh.copy_(out, non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / args.steps
+    t = torch.tensor([e2e_ms], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    ops.status()
+    row_bytes = ops.row_bytes
+    result = {
+        "metric": METRIC, "value": world * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic: seeded activations ~N(0,1); weights ~N(0,0.02) quantised to int4 "
+                "group-32 with fp16 scales",
+        "config": {"workload": f"{CONFIG}: Qwen3-30B-A3B-shaped W4A8 MoE layer, {T}-token prefill "
+                               "per GPU, router-inclusive forward with residual, expert parallel",
+                   "hidden": spec.hidden, "experts": spec.experts, "top_k": spec.top,
+                   "intermediate": spec.inter, "weights": "int4 g32 fp16 scales",
+                   "tokens_per_gpu": T, "global_batch": T * world, "seq_len": T,
+                   "parallelism": f"ep{world} ({P} experts per GPU, NCCL all-to-all dispatch and combine)",
+                   "l2": "no flush: the expert weights read per step exceed the 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": (achieved / hbm_peak) if achieved else None, "traffic": None,
+                     "kernel": "grouped_gemm_kernel<W4G32, GateUp> (gate/up of the received rows, rank 0)",
+                     "algorithmic_bytes_per_launch": gu_bytes, "kernel_us": gate_us,
+                     "peak_kind": f"{pk_kind} (hbm_gbs, STREAM-style copy)"},
+        "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": 2 * T * spec.hidden * 4,
+                "d2h_bytes_per_step": T * spec.hidden * 4, "ms_per_step": e2e_ms,
+                "api": "ep_forward over moe_b200_ep_* (pinned host buffers)"},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "exchange": {"rows_sent_per_step_rank0": sent // max(args.steps, 1),
+                     "rows_received_per_step_rank0": rows_here,
+                     "dispatch_bytes_per_row": row_bytes + 8,
+                     "combine_bytes_per_row": spec.hidden * 4},
+    }
+    ops.close()
+    moe.close()
+    router.close()
+    be.close()
+    dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
 def cudart_copy(dst: np.ndarray, src_ptr: int):
     import torch
 
@@ -458,6 +599,8 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         run_reference(args)
+    elif int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        run_ep(args)
     else:
         run_ours(args)
 

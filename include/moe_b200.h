@@ -212,6 +212,43 @@ int moe_b200_workspace_profile_read(moe_b200_workspace *ws, int32_t call, moe_b2
 /* Number of kernels this workspace has launched since creation. */
 int64_t moe_b200_workspace_launches(const moe_b200_workspace *ws);
 
+/* ---- expert parallelism (no counterpart in the reference: its experts run
+ * on one device). Rank g of G owns experts [g*P, (g+1)*P), P = experts per
+ * rank; the caller moves the packed rows between ranks (NCCL all-to-all) and
+ * owns every d_* buffer. Rows are moe_b200_workspace_row_bytes(ws) bytes
+ * apart (H rounded up to 256). ---------------------------------------------- */
+
+/* Row stride, in bytes, of the int8 rows the expert-parallel entry points read
+ * and write (the workspace's padded hidden size). */
+int64_t moe_b200_workspace_row_bytes(const moe_b200_workspace *ws);
+
+/* Token owner, step 1: A8-quantises rows (MoE rule) and packs one int8 row per
+ * kept assignment into d_send_q, grouped by destination rank (expert / P) and
+ * in assignment order t*k+r within a rank; d_send_scale / d_send_expert get
+ * the row's scale and its expert id local to the destination; d_send_counts
+ * [world] the rows per destination; d_pos [rows*k] the send slot of each
+ * assignment (-1 when pruned). ws: a workspace over all E experts. */
+int moe_b200_ep_pack(moe_b200_workspace *ws, int32_t rows, const float *d_x,
+                     const int32_t *d_ids, const float *d_routes, int32_t experts_per_rank,
+                     int32_t world, int8_t *d_send_q, float *d_send_scale,
+                     int32_t *d_send_expert, int32_t *d_send_counts, int32_t *d_pos,
+                     void *stream);
+
+/* Expert owner, step 2: the grouped expert FFN (gate/up, SwiGLU, requant,
+ * down) of n received rows, expert ids local to w (a bank of P experts);
+ * d_y [n][H] f32 in the received order. ws: a workspace over the P experts
+ * with max_rows * top >= n. */
+int moe_b200_ep_expert_rows(moe_b200_workspace *ws, const moe_b200_weights *w, int32_t n,
+                            const int8_t *d_q, const float *d_scale, const int32_t *d_expert,
+                            float *d_y, void *stream);
+
+/* Token owner, step 3: out[t] = (residual[t] +) sum over ranks r ascending of
+ * fma(y_back[pos[t*k+r]], routes[t,r]) for kept assignments, the order of the
+ * single-device combine. */
+int moe_b200_ep_combine(moe_b200_workspace *ws, int32_t rows, const float *d_y_back,
+                        const int32_t *d_pos, const float *d_routes, const float *d_residual,
+                        float *d_out, void *stream);
+
 /* Router + top-k that allocates nothing (no counterpart in the reference; an
  * addition for callers that cannot call cudaMalloc, such as an engine whose
  * own pool owns all device memory, or a hot path that must not risk an

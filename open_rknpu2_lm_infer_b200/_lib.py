@@ -105,6 +105,16 @@ SIGNATURES = [
     ("moe_b200_workspace_profile", C.c_int, [C.c_void_p, C.c_int32]),
     ("moe_b200_workspace_profile_read", C.c_int, [C.c_void_p, C.c_int32, C.POINTER(Timings)]),
     ("moe_b200_workspace_launches", C.c_int64, [C.c_void_p]),
+    ("moe_b200_workspace_row_bytes", C.c_int64, [C.c_void_p]),
+    ("moe_b200_ep_pack", C.c_int,
+     [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32,
+      C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("moe_b200_ep_expert_rows", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+      C.c_void_p]),
+    ("moe_b200_ep_combine", C.c_int,
+     [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+      C.c_void_p]),
     ("moe_b200_route_noalloc", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
       C.c_float, C.c_void_p, C.c_void_p, C.c_void_p]),

@@ -894,6 +894,103 @@ int moe_b200_forward_device(moe_b200_workspace* ws, const moe_b200_weights* w,
     return run_pipeline(ws, w, rows, d_input, ws->ids, ws->routes, d_residual, d_output, s, evs);
 }
 
+int64_t moe_b200_workspace_row_bytes(const moe_b200_workspace* ws) { return ws ? ws->Kh : 0; }
+
+int moe_b200_ep_pack(moe_b200_workspace* ws, int32_t rows, const float* d_x, const int32_t* d_ids,
+                     const float* d_routes, int32_t experts_per_rank, int32_t world,
+                     int8_t* d_send_q, float* d_send_scale, int32_t* d_send_expert,
+                     int32_t* d_send_counts, int32_t* d_pos, void* stream) {
+    if (!ws || rows < 0 || experts_per_rank <= 0 || world <= 0 || world > 1024) return MOE_B200_ERR_INVALID;
+    if (rows > ws->max_rows) return MOE_B200_ERR_CAPACITY;
+    if (rows == 0) return MOE_B200_OK;
+    if (!d_x || !d_ids || !d_routes || !d_send_q || !d_send_scale || !d_send_expert ||
+        !d_send_counts || !d_pos || !aligned16(d_x) || !aligned16(d_send_q))
+        return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ws->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int n = rows * ws->k;
+    const int limit = experts_per_rank * world;
+    ws->launches += 5;
+    // group the assignments by destination rank (stable, assignment order)
+    launch_route_count(d_ids, d_routes, n, world, ws->hist, ws->err, s, limit, experts_per_rank);
+    launch_route_scatter(d_ids, d_routes, n, world, ws->hist, ws->offsets, ws->perm, d_pos,
+                         nullptr, rows, s, limit, experts_per_rank);
+    // quantise each token once and write its row into every kept slot
+    launch_quant_gather(d_x, rows, ws->H, ws->Kh, kQuantMoe, ws->k, d_pos, nullptr, nullptr,
+                        d_send_q, d_send_scale, nullptr, nullptr, ws->err, s);
+    launch_ep_expert_ids(d_ids, d_pos, n, experts_per_rank, d_send_expert, s);
+    // per-destination counts from the offsets
+    launch_ep_counts(ws->offsets, world, d_send_counts, s);
+    return cuda_rc(cudaPeekAtLastError());
+}
+
+int moe_b200_ep_expert_rows(moe_b200_workspace* ws, const moe_b200_weights* w, int32_t n,
+                            const int8_t* d_q, const float* d_scale, const int32_t* d_expert,
+                            float* d_y, void* stream) {
+    int rc = compatible(ws, w);
+    if (rc) return rc;
+    if (w->shared) return MOE_B200_ERR_UNSUPPORTED;  // the owner computes the shared expert
+    if (n < 0) return MOE_B200_ERR_INVALID;
+    if (n > ws->n_max) return MOE_B200_ERR_CAPACITY;
+    if (n == 0) return MOE_B200_OK;
+    if (!d_q || !d_scale || !d_expert || !d_y || !aligned16(d_q) || !aligned16(d_y))
+        return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ws->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int E = ws->E, H = ws->H, I = ws->I;
+    ws->launches += 6;
+    // stage events of the profiling ring: schedule+gather, gate/up, requant, down
+    cudaEvent_t* evs = prof_slot(ws, 0);
+    auto mark = [&](int i) {
+        if (evs) cudaEventRecord(evs[i], s);
+    };
+    mark(0);
+    mark(1);
+    // rows -> permuted order by local expert (every row kept, one expert each)
+    launch_route_count(d_expert, nullptr, n, E, ws->hist, ws->err, s);
+    launch_route_scatter(d_expert, nullptr, n, E, ws->hist, ws->offsets, ws->perm, ws->pos,
+                         nullptr, n, s);
+    launch_ep_gather_rows(d_q, d_scale, ws->pos, n, ws->Kh, ws->a_perm, ws->s_perm, s);
+    mark(2);
+    mark(3);
+    const int nt = choose_nt(n, E);
+    const int nt_g = exact_nt(nt, w->gu.fmt);
+    GemmArgs g = gemm_args(ws, w->gu, ws->s_perm, ws->offsets, E, n, ws->gate_up, 2 * I);
+    if (launch_gemm(ws->map_a[nt_index(nt_g)], g, w->gu.fmt, kEpiGateUp, nt_g, ws->num_sms, s))
+        return MOE_B200_ERR_UNSUPPORTED;
+    mark(4);
+    const bool hd = w->dn.fmt == kFmtW4G32;
+    launch_requant(ws->gate_up, ws->offsets + E, n, I, ws->Ki, kQuantMoe, ws->q_m,
+                   hd ? ws->q_m_h : nullptr, ws->s_m, s);
+    mark(5);
+    // down GEMM straight into the received order (permuted row p -> row perm[p])
+    GemmArgs d = gemm_args(ws, w->dn, ws->s_m, ws->offsets, E, n, d_y, H);
+    d.out_rows = ws->perm;
+    if (launch_gemm(hd ? ws->map_qm_h[nt_index(nt)] : ws->map_qm[nt_index(nt)], d,
+                    down_fmt(w->dn.fmt), kEpiStore, nt, ws->num_sms, s))
+        return MOE_B200_ERR_UNSUPPORTED;
+    mark(6);
+    mark(7);
+    mark(8);
+    return cuda_rc(cudaPeekAtLastError());
+}
+
+int moe_b200_ep_combine(moe_b200_workspace* ws, int32_t rows, const float* d_y_back,
+                        const int32_t* d_pos, const float* d_routes, const float* d_residual,
+                        float* d_out, void* stream) {
+    if (!ws || rows < 0) return MOE_B200_ERR_INVALID;
+    if (rows > ws->max_rows) return MOE_B200_ERR_CAPACITY;
+    if (rows == 0) return MOE_B200_OK;
+    if (!d_y_back || !d_pos || !d_routes || !d_out || !aligned16(d_y_back) ||
+        !aligned16(d_residual) || !aligned16(d_out))
+        return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ws->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    ws->launches += 1;
+    launch_combine(d_y_back, d_pos, d_routes, nullptr, d_residual, rows, ws->H, ws->k, d_out, s);
+    return cuda_rc(cudaPeekAtLastError());
+}
+
 int moe_b200_forward_f32(moe_b200_workspace* ws, const moe_b200_weights* w,
                          const moe_b200_router* r, int32_t rows, const float* input,
                          const float* residual, float* output, int32_t* ids, float* routes,

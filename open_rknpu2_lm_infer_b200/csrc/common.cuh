@@ -1,5 +1,5 @@
 // Device-side building blocks for the sm_100a MoE kernels: mbarriers with
-// bounded waits, bulk/tensor async copies (never cluster-multicast), tcgen05
+// bounded waits, bulk/tensor async copies (each into this CTA only), tcgen05
 // TMEM allocation, MMA issue and TMEM loads, written as inline PTX.
 #pragma once
 #include <cuda.h>
@@ -95,7 +95,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// 1-D bulk copy global -> shared, completing on an mbarrier (no multicast).
+// 1-D bulk copy global -> this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
                                          uint64_t* bar) {
     asm volatile(
@@ -105,7 +105,7 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
         : "memory");
 }
 
-// 2-D tiled tensor copy global -> shared (no multicast). x must be a multiple
+// 2-D tiled tensor copy global -> this CTA's shared memory. x must be a multiple
 // of 16 bytes for the 8-bit element type used here.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int32_t x,
                                             int32_t y, uint64_t* bar) {
@@ -116,7 +116,7 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
-// 3-D tiled tensor copy global -> shared (no multicast).
+// 3-D tiled tensor copy global -> this CTA's shared memory.
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int32_t x,
                                             int32_t y, int32_t z, uint64_t* bar) {
     asm volatile(
@@ -193,7 +193,7 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 }
 
 // Arrive on an mbarrier once every previously issued tcgen05 op of this
-// thread has completed (single-CTA form, no multicast).
+// thread has completed (single-CTA form).
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      smem_u32(bar))

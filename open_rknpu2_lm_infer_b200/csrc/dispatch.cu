@@ -24,23 +24,27 @@ namespace moe {
 
 __device__ __forceinline__ bool route_kept(float w) { return w > 0.0f; }
 
+// Keys: id / div for ids in [0, id_limit) (div = 1: the expert; div = experts
+// per rank: the destination rank of expert parallelism). routes == nullptr:
+// every assignment is kept.
 __global__ void route_count_kernel(const int32_t* __restrict__ ids, const float* __restrict__ routes,
-                                   int n, int E, int32_t* hist, uint32_t* err) {
+                                   int n, int E, int id_limit, int div, int32_t* hist,
+                                   uint32_t* err) {
     extern __shared__ int32_t hist_s[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) hist_s[e] = 0;
     __syncthreads();
     const int a0 = blockIdx.x * kRouteChunk;
     const int a1 = min(n, a0 + kRouteChunk);
     for (int a = a0 + threadIdx.x; a < a1; a += blockDim.x) {
-        const float w = routes[a];
+        const float w = routes ? routes[a] : 1.0f;
         if (!(w >= 0.0f)) atomicOr(err, kErrBadRoute);  // negative or NaN
         if (!route_kept(w)) continue;
-        const int e = ids[a];
-        if (e < 0 || e >= E) {
+        const int id = ids[a];
+        if (id < 0 || id >= id_limit) {
             atomicOr(err, kErrBadExpert);
             continue;
         }
-        atomicAdd(&hist_s[e], 1);
+        atomicAdd(&hist_s[id / div], 1);
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) hist[(size_t)blockIdx.x * E + e] = hist_s[e];
@@ -49,8 +53,9 @@ __global__ void route_count_kernel(const int32_t* __restrict__ ids, const float*
 // 256 threads. smem: off[E+1], base[E], wcnt[8][E].
 __global__ void __launch_bounds__(256)
 route_scatter_kernel(const int32_t* __restrict__ ids, const float* __restrict__ routes, int n,
-                     int E, const int32_t* __restrict__ hist, int32_t* offsets, int32_t* perm,
-                     int32_t* pos, int32_t* shared_offsets, int T) {
+                     int E, int id_limit, int div, const int32_t* __restrict__ hist,
+                     int32_t* offsets, int32_t* perm, int32_t* pos, int32_t* shared_offsets,
+                     int T) {
     extern __shared__ int32_t sm[];
     int32_t* off_s = sm;               // E+1
     int32_t* base_s = off_s + E + 1;   // E
@@ -109,9 +114,9 @@ route_scatter_kernel(const int32_t* __restrict__ ids, const float* __restrict__ 
         const int a = r0 + threadIdx.x;
         int e = -1;
         if (a < a1) {
-            const float w = routes[a];
+            const float w = routes ? routes[a] : 1.0f;
             const int id = ids[a];
-            if (route_kept(w) && id >= 0 && id < E) e = id;
+            if (route_kept(w) && id >= 0 && id < id_limit) e = id / div;
         }
         const unsigned peers = __match_any_sync(0xffffffffu, e);
         const int rank_w = __popc(peers & lt);
@@ -344,22 +349,67 @@ combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ pos,
 }
 
 void launch_route_count(const int32_t* ids, const float* routes, int n, int E, int32_t* hist,
-                        uint32_t* err, cudaStream_t s) {
+                        uint32_t* err, cudaStream_t s, int id_limit, int div) {
     const int nb = (n + kRouteChunk - 1) / kRouteChunk;
     if (nb == 0) return;
-    route_count_kernel<<<nb, 256, sizeof(int32_t) * E, s>>>(ids, routes, n, E, hist, err);
+    route_count_kernel<<<nb, 256, sizeof(int32_t) * E, s>>>(
+        ids, routes, n, E, id_limit > 0 ? id_limit : E, div, hist, err);
 }
 
 void launch_route_scatter(const int32_t* ids, const float* routes, int n, int E,
                           const int32_t* hist, int32_t* offsets, int32_t* perm, int32_t* pos,
-                          int32_t* shared_offsets, int T, cudaStream_t s) {
+                          int32_t* shared_offsets, int T, cudaStream_t s, int id_limit, int div) {
     const int nb = (n + kRouteChunk - 1) / kRouteChunk;
     const size_t smem = sizeof(int32_t) * (size_t)(E + 1 + E + 8 * E);
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem);
-    route_scatter_kernel<<<nb > 0 ? nb : 1, 256, smem, s>>>(ids, routes, n, E, hist, offsets,
-                                                            perm, pos, shared_offsets, T);
+    route_scatter_kernel<<<nb > 0 ? nb : 1, 256, smem, s>>>(
+        ids, routes, n, E, id_limit > 0 ? id_limit : E, div, hist, offsets, perm, pos,
+        shared_offsets, T);
+}
+
+// Expert parallelism: the destination-local expert id of each packed row.
+__global__ void ep_expert_ids_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ pos,
+                                     int n, int per_rank, int32_t* send_expert) {
+    const int a = blockIdx.x * blockDim.x + threadIdx.x;
+    if (a >= n) return;
+    const int p = pos[a];
+    if (p >= 0) send_expert[p] = ids[a] % per_rank;
+}
+
+void launch_ep_expert_ids(const int32_t* ids, const int32_t* pos, int n, int per_rank,
+                          int32_t* send_expert, cudaStream_t s) {
+    if (n == 0) return;
+    ep_expert_ids_kernel<<<(n + 255) / 256, 256, 0, s>>>(ids, pos, n, per_rank, send_expert);
+}
+
+// Rows per destination rank from the grouping offsets.
+__global__ void ep_counts_kernel(const int32_t* __restrict__ offsets, int world, int32_t* counts) {
+    for (int g = threadIdx.x; g < world; g += blockDim.x) counts[g] = offsets[g + 1] - offsets[g];
+}
+
+void launch_ep_counts(const int32_t* offsets, int world, int32_t* counts, cudaStream_t s) {
+    ep_counts_kernel<<<1, 256, 0, s>>>(offsets, world, counts);
+}
+
+// Received rows -> permuted order: row i (ld bytes) to slot pos[i], its scale too.
+__global__ void ep_gather_rows_kernel(const int8_t* __restrict__ q, const float* __restrict__ scale,
+                                      const int32_t* __restrict__ pos, int ld, int8_t* q_perm,
+                                      float* s_perm) {
+    const int i = blockIdx.x;
+    const int p = pos[i];
+    if (p < 0) return;
+    const uint4* src = reinterpret_cast<const uint4*>(q + (size_t)i * ld);
+    uint4* dst = reinterpret_cast<uint4*>(q_perm + (size_t)p * ld);
+    for (int c = threadIdx.x; c < ld / 16; c += blockDim.x) dst[c] = src[c];
+    if (threadIdx.x == 0) s_perm[p] = scale[i];
+}
+
+void launch_ep_gather_rows(const int8_t* q, const float* scale, const int32_t* pos, int n, int ld,
+                           int8_t* q_perm, float* s_perm, cudaStream_t s) {
+    if (n == 0) return;
+    ep_gather_rows_kernel<<<n, 128, 0, s>>>(q, scale, pos, ld, q_perm, s_perm);
 }
 
 void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k,

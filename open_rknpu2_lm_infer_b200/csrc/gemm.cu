@@ -632,8 +632,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                     const int j = c0 + q;
                     const float sxq = __shfl_sync(0xffffffffu, my_sx, q);
                     const float f = (q & 1) ? facc[q >> 1].y : facc[q >> 1].x;
-                    if (j < nvalid && col_ok)
-                        a.out[(size_t)(row0 + j) * a.ldo + (EPI == kEpiGateUp ? ocol : col)] = __fmul_rn(f, sxq);
+                    if (j < nvalid && col_ok) {
+                        const int orow = (EPI == kEpiStore && a.out_rows) ? a.out_rows[row0 + j] : row0 + j;
+                        a.out[(size_t)orow * a.ldo + (EPI == kEpiGateUp ? ocol : col)] = __fmul_rn(f, sxq);
+                    }
                 }
                 continue;
             }
@@ -678,8 +680,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                         if (C::kW4) acc >>= 4;
                         val = __fmul_rn(__fmul_rn(__int2float_rn(acc), sxq), wscale_pc);
                     }
-                    if (j < nvalid && col_ok)
-                        a.out[(size_t)(row0 + j) * a.ldo + (EPI == kEpiGateUp ? ocol : col)] = val;
+                    if (j < nvalid && col_ok) {
+                        const int orow = (EPI == kEpiStore && a.out_rows) ? a.out_rows[row0 + j] : row0 + j;
+                        a.out[(size_t)orow * a.ldo + (EPI == kEpiGateUp ? ocol : col)] = val;
+                    }
                 }
             }
         }

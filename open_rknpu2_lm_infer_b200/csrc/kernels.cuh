@@ -48,6 +48,7 @@ struct GemmArgs {
     int kblocks;              // K / 128
     int row_tiles;            // weight row tiles of 128
     float* out;               // GateUp: gate | up [rows][ldo = 2n]; Store: y [rows][ldo]
+    const int32_t* out_rows;  // Store: output row of each permuted row (null: the same)
     int ldo;
     int n_valid;              // valid output channels (I or H)
     int32_t* acc_out;         // accumulator dump
@@ -64,11 +65,21 @@ int launch_gemm(const CUtensorMap& map, const GemmArgs& a, int fmt, int epi, int
                 int num_sms, cudaStream_t s);
 
 // dispatch.cu
+// Grouping of assignments by key = id / div (ids in [0, id_limit), default E;
+// routes == nullptr keeps every assignment): stable ranks, offsets [E+1],
+// perm (slot -> assignment), pos (assignment -> slot or -1).
 void launch_route_count(const int32_t* ids, const float* routes, int n, int E, int32_t* hist,
-                        uint32_t* err, cudaStream_t s);
+                        uint32_t* err, cudaStream_t s, int id_limit = 0, int div = 1);
 void launch_route_scatter(const int32_t* ids, const float* routes, int n, int E,
                           const int32_t* hist, int32_t* offsets, int32_t* perm, int32_t* pos,
-                          int32_t* shared_offsets, int T, cudaStream_t s);
+                          int32_t* shared_offsets, int T, cudaStream_t s, int id_limit = 0,
+                          int div = 1);
+// expert parallelism helpers
+void launch_ep_expert_ids(const int32_t* ids, const int32_t* pos, int n, int per_rank,
+                          int32_t* send_expert, cudaStream_t s);
+void launch_ep_counts(const int32_t* offsets, int world, int32_t* counts, cudaStream_t s);
+void launch_ep_gather_rows(const int8_t* q, const float* scale, const int32_t* pos, int n, int ld,
+                           int8_t* q_perm, float* s_perm, cudaStream_t s);
 // h_rows / h_perm / qh (may be null): the same codes as fp16, for kFmtW4G32H.
 void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k,
                          const int32_t* pos, int8_t* q_rows, float* s_rows, int8_t* q_perm,
