@@ -42,8 +42,15 @@ extern "C" {
 
 /* Routed-expert weight formats. */
 #define MOE_B200_W4_PER_CHANNEL 0 /* reference native format: int4 codes, f32 scale per n */
-#define MOE_B200_W4_G32_FP16 1    /* int4 codes, fp16 scale per (32 k, n) group */
+/* int4 codes, fp16 scale per (32 k, n) group. The gate/up GEMM keeps one exact
+ * int32 sum per group (its output is requantised, where a rounding difference
+ * would flip int8 codes); the down GEMM runs on the fp16 tensor cores with
+ * w * s rounded once to fp16 and fp32 accumulation (outputs within the
+ * 1e-2 rel / 1e-3 abs contract, ~3x faster than exact group sums). */
+#define MOE_B200_W4_G32_FP16 1
 #define MOE_B200_W8_PER_CHANNEL 2 /* int8 codes, f32 scale per n */
+/* The same group-32 bank with both GEMMs on exact int32 group sums. */
+#define MOE_B200_W4_G32_FP16_EXACT 3
 
 /* Router accumulation order (src/model/cpu.rs:96-153, dense_dot). */
 #define MOE_B200_ROUTER_NEON16 0     /* aarch64 F32 branch: 4x4-lane FMA + fixed tree */
@@ -78,7 +85,7 @@ typedef struct {
 } moe_b200_config;
 
 /* Replaces rk_npu_moe_w8_expert (src/npu/moe.rs:121-126). The *_group_scales
- * pointers are read only for MOE_B200_W4_G32_FP16: IEEE fp16 bits laid out
+ * pointers are read only for the group-32 formats: IEEE fp16 bits laid out
  * [k/32][n]. */
 typedef struct {
     const int8_t *gate_up;

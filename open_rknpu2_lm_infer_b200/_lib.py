@@ -28,6 +28,7 @@ NOALLOC_MAX_LOGITS = 1 << 20
 W4_PER_CHANNEL = 0
 W4_G32_FP16 = 1
 W8_PER_CHANNEL = 2
+W4_G32_FP16_EXACT = 3
 ROUTER_NEON16 = 0
 ROUTER_SEQUENTIAL = 1
 SHARED_JOINT = 0

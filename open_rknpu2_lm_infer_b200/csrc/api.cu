@@ -138,8 +138,9 @@ int choose_nt(long rows, int experts) {
 // which caps its tile at 32 tokens.
 int exact_nt(int nt, int fmt) { return fmt == kFmtW4G32 && nt > 32 ? 32 : nt; }
 // Group-32 down projections (their output is not requantised) run on the fp16
-// tensor cores; gate/up projections keep the exact per-group sums.
-int down_fmt(int fmt) { return fmt == kFmtW4G32 ? kFmtW4G32H : fmt; }
+// tensor cores unless the bank asks for exact group sums; gate/up projections
+// always keep the exact per-group sums.
+int down_fmt(int fmt, bool exact) { return fmt == kFmtW4G32 && !exact ? kFmtW4G32H : fmt; }
 
 // ---- packed matrices ------------------------------------------------------
 
@@ -269,6 +270,7 @@ struct moe_b200_weights {
     int device = 0;
     int H = 0, I = 0, E = 0, shared = 0, Is = 0, top = 0;
     int shared_mode = MOE_B200_SHARED_DENSE;
+    bool exact_down = false;  // group-32: down GEMM on exact int32 group sums too
     PackedMat gu, dn, sgu, sdn;
     uint64_t bytes = 0;
 };
@@ -377,7 +379,7 @@ int run_shared(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, cons
     const int rule = w->shared_mode == MOE_B200_SHARED_JOINT ? kQuantMoe : kQuantDense;
     const int nt = choose_nt(rows, 1);
     const int nt_g = exact_nt(nt, w->sgu.fmt);
-    const bool hd = w->sdn.fmt == kFmtW4G32;
+    const bool hd = down_fmt(w->sdn.fmt, false) == kFmtW4G32H;
     const CUtensorMap* amap = &ws->map_qx[nt_index(nt_g)];
     const float* ascale = ws->s_x;
     if (w->shared_mode != MOE_B200_SHARED_JOINT) {
@@ -393,7 +395,7 @@ int run_shared(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, cons
                    hd ? ws->sq_m_h : nullptr, ws->ss_m, s);
     GemmArgs d = gemm_args(ws, w->sdn, ws->ss_m, ws->shared_offsets, 1, rows, ws->s_y, ws->H);
     if (launch_gemm(hd ? ws->map_sqm_h[nt_index(nt)] : ws->map_sqm[nt_index(nt)], d,
-                    down_fmt(w->sdn.fmt), kEpiStore, nt, ws->num_sms, s))
+                    down_fmt(w->sdn.fmt, false), kEpiStore, nt, ws->num_sms, s))
         return MOE_B200_ERR_UNSUPPORTED;
     return MOE_B200_OK;
 }
@@ -446,13 +448,15 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
         return MOE_B200_ERR_UNSUPPORTED;
     mark(4);
     // group-32 down projections read an fp16 copy of the middle codes
-    const bool hd = w->dn.fmt == kFmtW4G32;
+    const int dfmt = down_fmt(w->dn.fmt, w->exact_down);
+    const bool hd = dfmt == kFmtW4G32H;
+    const int nt_d = exact_nt(nt, dfmt);
     launch_requant(ws->gate_up, ws->offsets + E, (int)n, I, ws->Ki, kQuantMoe, ws->q_m,
                    hd ? ws->q_m_h : nullptr, ws->s_m, s);
     mark(5);
     GemmArgs d = gemm_args(ws, w->dn, ws->s_m, ws->offsets, E, n, ws->y, H);
-    if (launch_gemm(hd ? ws->map_qm_h[nt_index(nt)] : ws->map_qm[nt_index(nt)], d,
-                    down_fmt(w->dn.fmt), kEpiStore, nt, ws->num_sms, s))
+    if (launch_gemm(hd ? ws->map_qm_h[nt_index(nt_d)] : ws->map_qm[nt_index(nt_d)], d, dfmt,
+                    kEpiStore, nt_d, ws->num_sms, s))
         return MOE_B200_ERR_UNSUPPORTED;
     mark(6);
     if (w->shared) {
@@ -465,7 +469,7 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
     mark(8);
     ws->last_rows = rows;
     ws->last_nt_gu = nt_g;
-    ws->last_nt_dn = nt;
+    ws->last_nt_dn = nt_d;
     ws->last_w = w;
     ws->last_stream = s;
     cudaError_t e = cudaPeekAtLastError();
@@ -569,7 +573,9 @@ moe_b200_weights* moe_b200_weights_create(const moe_b200_config* cfg,
     if (format) fmt = *format;
     const int H = cfg->weights.hidden, I = cfg->weights.intermediate, E = cfg->weights.routed_experts;
     const int Is = cfg->weights.shared_intermediate > 0 ? cfg->weights.shared_intermediate : I;
-    if (fmt.routed_format < 0 || fmt.routed_format > 2) return nullptr;
+    if (fmt.routed_format < 0 || fmt.routed_format > MOE_B200_W4_G32_FP16_EXACT) return nullptr;
+    const bool exact_down = fmt.routed_format == MOE_B200_W4_G32_FP16_EXACT;
+    if (exact_down) fmt.routed_format = MOE_B200_W4_G32_FP16;  // one packing for both
     if (fmt.shared_format != MOE_B200_W8_PER_CHANNEL && fmt.shared_format != MOE_B200_W4_PER_CHANNEL)
         return nullptr;
     if (cfg->weights.shared_expert && fmt.shared_mode == MOE_B200_SHARED_JOINT && Is != I)
@@ -592,6 +598,7 @@ moe_b200_weights* moe_b200_weights_create(const moe_b200_config* cfg,
     w->shared = cfg->weights.shared_expert;
     w->Is = Is;
     w->shared_mode = fmt.shared_mode;
+    w->exact_down = exact_down;
     setup_mat(w->gu, fmt.routed_format, E, H, I, true);
     setup_mat(w->dn, fmt.routed_format, E, I, H, false);
     if (w->shared) {
@@ -959,15 +966,17 @@ int moe_b200_ep_expert_rows(moe_b200_workspace* ws, const moe_b200_weights* w, i
     if (launch_gemm(ws->map_a[nt_index(nt_g)], g, w->gu.fmt, kEpiGateUp, nt_g, ws->num_sms, s))
         return MOE_B200_ERR_UNSUPPORTED;
     mark(4);
-    const bool hd = w->dn.fmt == kFmtW4G32;
+    const int dfmt = down_fmt(w->dn.fmt, w->exact_down);
+    const bool hd = dfmt == kFmtW4G32H;
+    const int nt_d = exact_nt(nt, dfmt);
     launch_requant(ws->gate_up, ws->offsets + E, n, I, ws->Ki, kQuantMoe, ws->q_m,
                    hd ? ws->q_m_h : nullptr, ws->s_m, s);
     mark(5);
     // down GEMM straight into the received order (permuted row p -> row perm[p])
     GemmArgs d = gemm_args(ws, w->dn, ws->s_m, ws->offsets, E, n, d_y, H);
     d.out_rows = ws->perm;
-    if (launch_gemm(hd ? ws->map_qm_h[nt_index(nt)] : ws->map_qm[nt_index(nt)], d,
-                    down_fmt(w->dn.fmt), kEpiStore, nt, ws->num_sms, s))
+    if (launch_gemm(hd ? ws->map_qm_h[nt_index(nt_d)] : ws->map_qm[nt_index(nt_d)], d, dfmt,
+                    kEpiStore, nt_d, ws->num_sms, s))
         return MOE_B200_ERR_UNSUPPORTED;
     mark(6);
     mark(7);

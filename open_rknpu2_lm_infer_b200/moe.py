@@ -111,8 +111,11 @@ class Backend:
         self.weight_bytes = 0
 
     # ---- bank construction (src/npu/moe.rs:70-220) --------------------------
-    def load_moe(self, gate: list[QuantMatrix], down: list[QuantMatrix], top: int) -> "Moe":
-        return self._load(gate, down, top, None, None)
+    def load_moe(self, gate: list[QuantMatrix], down: list[QuantMatrix], top: int,
+                 exact: bool = False) -> "Moe":
+        """exact: group-32 banks run the down GEMM on exact int32 group sums too
+        (MOE_B200_W4_G32_FP16_EXACT) instead of the fp16 tensor cores."""
+        return self._load(gate, down, top, None, None, exact)
 
     def load_moe_with_shared(self, gate, down, top, shared: tuple[QuantMatrix, QuantMatrix],
                              mode: int | None = None) -> "Moe":
@@ -122,7 +125,7 @@ class Backend:
         # the full-K variant is the default schedule here
         return self._load(gate, down, top, None, None)
 
-    def _load(self, gate, down, top, shared, mode) -> "Moe":
+    def _load(self, gate, down, top, shared, mode, exact=False) -> "Moe":
         if not gate or len(gate) != len(down):
             raise ValueError("invalid expert bank")
         for m in [*gate, *down]:
@@ -173,7 +176,10 @@ class Backend:
         table = (L.Expert * (e + (1 if shared is not None else 0)))()
         for i in range(e):
             table[i] = expert(gate[i], down[i])
-        fmt = L.Format(fmts.pop(), L.W8_PER_CHANNEL, L.SHARED_DENSE if mode is None else mode)
+        routed = fmts.pop()
+        if exact and routed == L.W4_G32_FP16:
+            routed = L.W4_G32_FP16_EXACT
+        fmt = L.Format(routed, L.W8_PER_CHANNEL, L.SHARED_DENSE if mode is None else mode)
         if shared is not None:
             table[e] = expert(*shared)
             fmt.shared_format = L.W8_PER_CHANNEL if shared[0].bits == 8 else L.W4_PER_CHANNEL

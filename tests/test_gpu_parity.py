@@ -41,13 +41,13 @@ def layer_for(spec, seed=3):
     return _LAYERS[key]
 
 
-def build(layer, max_rows, shared_mode=None, order=0, min_weight=0.0):
+def build(layer, max_rows, shared_mode=None, order=0, min_weight=0.0, exact=False):
     be = Backend(device=0, max_rows=max_rows)
     spec = layer.spec
     if layer.shared is not None:
         moe = be.load_moe_with_shared(layer.gate, layer.down, spec.top, layer.shared, shared_mode)
     else:
-        moe = be.load_moe(layer.gate, layer.down, spec.top)
+        moe = be.load_moe(layer.gate, layer.down, spec.top, exact=exact)
     router = be.router(layer.router, spec.top, layer.bias, order, min_weight)
     return be, moe, router
 
@@ -62,17 +62,20 @@ SPECS = {
     "joint": S.small_spec("c1", routed="w4pc", shared_inter=512),
 }
 
+# "_exact": the group-32 bank with both GEMMs on exact int32 group sums
 CASES = [("c1", 32), ("c1", 1), ("c2_e32", 1), ("c2_e32", 37), ("c2_e32", 300),
-         ("c3_e32", 64), ("w4pc", 48), ("w8pc", 48), ("joint", 40), ("c2", 512)]
+         ("c3_e32", 64), ("w4pc", 48), ("w8pc", 48), ("joint", 40), ("c2", 512),
+         ("c2_e32_exact", 37), ("c2_exact", 512), ("c1_exact", 32)]
 
 
 @pytest.mark.parametrize("name,T", CASES)
 def test_forward_matches_oracle(cuda, oracle, name, T):
-    spec = SPECS[name]
+    exact = name.endswith("_exact")
+    spec = SPECS[name.removesuffix("_exact")]
     layer = layer_for(spec)
     x = S.make_input(spec, T, seed=11)
     res = S.make_input(spec, T, seed=12, stream=5)
-    be, moe, router = build(layer, max_rows=max(T, 8))
+    be, moe, router = build(layer, max_rows=max(T, 8), exact=exact)
     out, ids, routes = moe.forward(router, x, res)
     ref, d = oracle.OracleLayer(layer).forward(x, res, dump=True)
     assert np.array_equal(ids, d["ids"]), "expert ids differ"
@@ -311,3 +314,18 @@ def test_allocation_failure_is_reported(cuda, tmp_path):
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
                        timeout=300)
     assert f"CODE {L.ERR_NOMEM}" in r.stdout, r.stdout + r.stderr
+
+
+def test_exact_group_format_reaches_the_library(cuda, oracle):
+    """The exact and the fp16 down projection give different roundings of the
+    same layer: outputs close, not identical."""
+    spec = SPECS["c2_e32"]
+    layer = layer_for(spec)
+    x = S.make_input(spec, 64, seed=41)
+    outs = []
+    for exact in (False, True):
+        be, moe, router = build(layer, max_rows=64, exact=exact)
+        outs.append(moe.forward(router, x)[0])
+        moe.close(); router.close(); be.close()
+    assert not np.array_equal(outs[0], outs[1])
+    assert_close(outs[0], outs[1], what="fp16 vs exact down projection")
