@@ -219,6 +219,20 @@ int moe_b200_workspace_profile_read(moe_b200_workspace *ws, int32_t call, moe_b2
 /* Number of kernels this workspace has launched since creation. */
 int64_t moe_b200_workspace_launches(const moe_b200_workspace *ws);
 
+/* ---- CUDA-graph replay (no counterpart in the reference): one router-
+ * inclusive device forward of a fixed row count over fixed device buffers,
+ * captured once; each replay is a single launch, which removes the host's
+ * per-kernel launch cost (the bulk of a decode step). The buffers, weights,
+ * router and workspace must outlive the graph; one replay at a time per
+ * workspace. --------------------------------------------------------------- */
+typedef struct moe_b200_graph moe_b200_graph;
+moe_b200_graph *moe_b200_graph_create(moe_b200_workspace *ws, const moe_b200_weights *w,
+                                      const moe_b200_router *r, int32_t rows,
+                                      const float *d_input, const float *d_residual,
+                                      float *d_output);
+int moe_b200_graph_launch(moe_b200_graph *g, void *stream);
+void moe_b200_graph_free(moe_b200_graph *g);
+
 /* ---- expert parallelism (no counterpart in the reference: its experts run
  * on one device). Rank g of G owns experts [g*P, (g+1)*P), P = experts per
  * rank; the caller moves the packed rows between ranks (NCCL all-to-all) and

@@ -107,6 +107,10 @@ SIGNATURES = [
     ("moe_b200_workspace_profile_read", C.c_int, [C.c_void_p, C.c_int32, C.POINTER(Timings)]),
     ("moe_b200_workspace_launches", C.c_int64, [C.c_void_p]),
     ("moe_b200_workspace_row_bytes", C.c_int64, [C.c_void_p]),
+    ("moe_b200_graph_create", C.c_void_p,
+     [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("moe_b200_graph_launch", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("moe_b200_graph_free", None, [C.c_void_p]),
     ("moe_b200_ep_pack", C.c_int,
      [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32,
       C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),

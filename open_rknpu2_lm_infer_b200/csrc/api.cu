@@ -901,6 +901,73 @@ int moe_b200_forward_device(moe_b200_workspace* ws, const moe_b200_weights* w,
     return run_pipeline(ws, w, rows, d_input, ws->ids, ws->routes, d_residual, d_output, s, evs);
 }
 
+struct moe_b200_graph {
+    int device = 0;
+    moe_b200_workspace* ws = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int64_t launches = 0;  // kernels per replay
+};
+
+moe_b200_graph* moe_b200_graph_create(moe_b200_workspace* ws, const moe_b200_weights* w,
+                                      const moe_b200_router* r, int32_t rows,
+                                      const float* d_input, const float* d_residual,
+                                      float* d_output) {
+    if (compatible(ws, w) || !r || r->H != ws->H || r->E != ws->E) return nullptr;
+    if (rows <= 0 || rows > ws->max_rows || !d_input || !d_output || !aligned16(d_input) ||
+        !aligned16(d_residual) || !aligned16(d_output))
+        return nullptr;
+    DeviceGuard guard(ws->device);
+    cudaStream_t s = ws->own_stream;
+    const bool prof = ws->profiling;
+    ws->profiling = false;  // no event records inside the graph
+    const int64_t l0 = ws->launches;
+    int rc = MOE_B200_OK;
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        ws->profiling = prof;
+        return nullptr;
+    }
+    rc = route_impl(ws, r, rows, d_input, nullptr, ws->ids, ws->routes, s);
+    if (rc == MOE_B200_OK)
+        rc = run_pipeline(ws, w, rows, d_input, ws->ids, ws->routes, d_residual, d_output, s, nullptr);
+    const cudaError_t e = cudaStreamEndCapture(s, &g);
+    ws->profiling = prof;
+    if (rc != MOE_B200_OK || e != cudaSuccess || !g) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        return nullptr;
+    }
+    cudaGraphExec_t x = nullptr;
+    if (cudaGraphInstantiate(&x, g, 0) != cudaSuccess) {
+        cudaGraphDestroy(g);
+        return nullptr;
+    }
+    auto* out = new moe_b200_graph();
+    out->device = ws->device;
+    out->ws = ws;
+    out->graph = g;
+    out->exec = x;
+    out->launches = ws->launches - l0;
+    ws->launches = l0;  // replays count their kernels
+    return out;
+}
+
+int moe_b200_graph_launch(moe_b200_graph* g, void* stream) {
+    if (!g) return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(g->device);
+    g->ws->launches += g->launches;
+    return cuda_rc(cudaGraphLaunch(g->exec, static_cast<cudaStream_t>(stream)));
+}
+
+void moe_b200_graph_free(moe_b200_graph* g) {
+    if (!g) return;
+    DeviceGuard guard(g->device);
+    if (g->exec) cudaGraphExecDestroy(g->exec);
+    if (g->graph) cudaGraphDestroy(g->graph);
+    delete g;
+}
+
 int64_t moe_b200_workspace_row_bytes(const moe_b200_workspace* ws) { return ws ? ws->Kh : 0; }
 
 int moe_b200_ep_pack(moe_b200_workspace* ws, int32_t rows, const float* d_x, const int32_t* d_ids,

@@ -16,7 +16,7 @@ import numpy as np
 from . import _lib as L
 from ._lib import MoeError, check
 
-__all__ = ["QuantMatrix", "Backend", "Moe", "Router", "MoeError"]
+__all__ = ["QuantMatrix", "Backend", "Moe", "Router", "Graph", "MoeError"]
 
 
 @dataclass
@@ -339,6 +339,15 @@ class Moe:
                                                   d_logits, d_ids, d_routes, stream)
         check(rc, "MoE router")
 
+    def graph(self, router: Router, rows: int, d_input: int, d_residual: int | None,
+              d_output: int) -> "Graph":
+        """Captures forward_device over these device buffers into a CUDA graph."""
+        raw = self.owner.lib.moe_b200_graph_create(self.workspace, self.weights.raw, router.raw,
+                                                   rows, d_input, d_residual, d_output)
+        if not raw:
+            raise MoeError("cannot capture the MoE forward into a CUDA graph", L.ERR_CUDA)
+        return Graph(_Handle(raw, self.owner.lib.moe_b200_graph_free), self.owner.lib)
+
     def status(self) -> None:
         check(self.owner.lib.moe_b200_workspace_status(self.workspace), "device status")
 
@@ -355,3 +364,17 @@ class Moe:
 
     def close(self):
         self.weights.close()
+
+
+class Graph:
+    """A captured router-inclusive forward (moe_b200_graph_*): one launch per replay."""
+
+    def __init__(self, handle: _Handle, lib):
+        self.handle = handle
+        self.lib = lib
+
+    def launch(self, stream: int = 0) -> None:
+        check(self.lib.moe_b200_graph_launch(self.handle.raw, stream), "graph replay")
+
+    def close(self):
+        self.handle.close()

@@ -329,3 +329,27 @@ def test_exact_group_format_reaches_the_library(cuda, oracle):
         moe.close(); router.close(); be.close()
     assert not np.array_equal(outs[0], outs[1])
     assert_close(outs[0], outs[1], what="fp16 vs exact down projection")
+
+
+@pytest.mark.parametrize("name,T", [("c2_e32", 1), ("c2_e32", 37), ("c1", 32)])
+def test_graph_replay_matches_forward(cuda, oracle, name, T):
+    """A captured forward (moe_b200_graph_*) replays the same layer bit for bit,
+    and reads its input buffer afresh on every replay."""
+    torch = cuda
+    spec = SPECS[name]
+    layer = layer_for(spec)
+    be, moe, router = build(layer, max_rows=max(T, 8))
+    s = torch.cuda.current_stream().cuda_stream
+    x = torch.from_numpy(S.make_input(spec, T, seed=51)).cuda()
+    res = torch.from_numpy(S.make_input(spec, T, seed=52, stream=5)).cuda()
+    out_g = torch.empty_like(x)
+    g = moe.graph(router, T, x.data_ptr(), res.data_ptr(), out_g.data_ptr())
+    for seed in (51, 53):
+        x.copy_(torch.from_numpy(S.make_input(spec, T, seed=seed)))
+        ref = torch.empty_like(x)
+        moe.forward_device(router, T, x.data_ptr(), res.data_ptr(), ref.data_ptr(), s)
+        g.launch(s)
+        torch.cuda.synchronize()
+        moe.status()
+        assert torch.equal(out_g, ref), f"replay differs (input seed {seed})"
+    g.close(); moe.close(); router.close(); be.close()
