@@ -289,6 +289,8 @@ struct moe_b200_workspace {
     std::vector<void*> allocs;
     uint64_t bytes = 0;
     cudaStream_t own_stream = nullptr;
+    cudaStream_t copy_stream = nullptr;  // host-API residual upload, overlapped with the layer
+    cudaEvent_t res_ready = nullptr;
     cudaStream_t last_stream = nullptr;
     // staging for the host-pointer API
     float *x = nullptr, *out = nullptr, *res = nullptr, *routes = nullptr;
@@ -425,7 +427,7 @@ cudaEvent_t* prof_slot(moe_b200_workspace* ws, int flags) {
 // stage events for run_profiled-style timings.
 int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
                  const int32_t* d_ids, const float* d_routes, const float* d_res, float* d_out,
-                 cudaStream_t s, cudaEvent_t* evs) {
+                 cudaStream_t s, cudaEvent_t* evs, cudaEvent_t res_ready = nullptr) {
     const int E = ws->E, k = ws->k, H = ws->H, I = ws->I;
     const long n = (long)rows * k;
     auto mark = [&](int i) {
@@ -464,6 +466,7 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
         if (rc) return rc;
     }
     mark(7);
+    if (res_ready) cudaStreamWaitEvent(s, res_ready, 0);  // residual uploaded on the side
     launch_combine(ws->y, ws->pos, d_routes, w->shared ? ws->s_y : nullptr, d_res, rows, H, k,
                    d_out, s);
     mark(8);
@@ -726,6 +729,10 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
             rc |= make_act_map_h(&ws->map_sqm_h[i], ws->sq_m_h, (int)(T + pad_rows), ws->Kis, nt);
         }
     }
+    if (rc == MOE_B200_OK &&
+        (cudaStreamCreateWithFlags(&ws->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
+         cudaEventCreateWithFlags(&ws->res_ready, cudaEventDisableTiming) != cudaSuccess))
+        rc = MOE_B200_ERR_CUDA;
     if (rc == MOE_B200_OK && cudaStreamCreateWithFlags(&ws->own_stream, cudaStreamNonBlocking) != cudaSuccess)
         rc = MOE_B200_ERR_CUDA;
     for (int i = 0; i < 12 && rc == MOE_B200_OK; ++i)
@@ -746,6 +753,11 @@ void moe_b200_workspace_free(moe_b200_workspace* ws) {
         if (ws->ev[i]) cudaEventDestroy(ws->ev[i]);
     for (cudaEvent_t e : ws->prof_ev) cudaEventDestroy(e);
     if (ws->own_stream) cudaStreamDestroy(ws->own_stream);
+    if (ws->copy_stream) {
+        cudaStreamSynchronize(ws->copy_stream);
+        cudaStreamDestroy(ws->copy_stream);
+    }
+    if (ws->res_ready) cudaEventDestroy(ws->res_ready);
     delete ws;
 }
 
@@ -1083,12 +1095,16 @@ int moe_b200_forward_f32(moe_b200_workspace* ws, const moe_b200_weights* w,
     const size_t xb = sizeof(float) * (size_t)rows * ws->H, nb = (size_t)rows * ws->k;
     if (timings) cudaEventRecord(ws->ev[10], s);
     cudaMemcpyAsync(ws->x, input, xb, cudaMemcpyHostToDevice, s);
-    if (residual) cudaMemcpyAsync(ws->res, residual, xb, cudaMemcpyHostToDevice, s);
+    // the residual is read only by the final combine: upload it beside the layer
+    if (residual) {
+        cudaMemcpyAsync(ws->res, residual, xb, cudaMemcpyHostToDevice, ws->copy_stream);
+        cudaEventRecord(ws->res_ready, ws->copy_stream);
+    }
     if (timings) cudaEventRecord(ws->ev[0], s);
     rc = route_impl(ws, r, rows, ws->x, nullptr, ws->ids, ws->routes, s);
     if (rc) return rc;
     rc = run_pipeline(ws, w, rows, ws->x, ws->ids, ws->routes, residual ? ws->res : nullptr,
-                      ws->out, s, timings ? ws->ev : nullptr);
+                      ws->out, s, timings ? ws->ev : nullptr, residual ? ws->res_ready : nullptr);
     if (rc) return rc;
     cudaMemcpyAsync(output, ws->out, xb, cudaMemcpyDeviceToHost, s);
     if (ids) cudaMemcpyAsync(ids, ws->ids, sizeof(int32_t) * nb, cudaMemcpyDeviceToHost, s);

@@ -307,9 +307,11 @@ class Moe:
         check(rc, "grouped routed FFN")
 
     def forward(self, router: Router, input: np.ndarray, residual: np.ndarray | None = None,
-                timings: bool = False):
+                timings: bool = False, out: np.ndarray | None = None,
+                ids: np.ndarray | None = None, routes: np.ndarray | None = None):
         """Router-inclusive layer on host buffers: returns (output, ids, routes[, timings]).
-        output = residual + (routed + shared) (src/model/qwen35/decoder.rs:215-217)."""
+        output = residual + (routed + shared) (src/model/qwen35/decoder.rs:215-217).
+        out / ids / routes may be caller-owned (e.g. page-locked) arrays."""
         inp = np.ascontiguousarray(input, dtype=np.float32)
         rows = inp.size // self.hidden
         if inp.size != rows * self.hidden:
@@ -317,9 +319,16 @@ class Moe:
         res = None if residual is None else np.ascontiguousarray(residual, dtype=np.float32)
         if res is not None and res.size != inp.size:
             raise ValueError("residual shape mismatch")
-        out = np.empty((rows, self.hidden), np.float32)
-        ids = np.empty((rows, self.top), np.int32)
-        routes = np.empty((rows, self.top), np.float32)
+
+        def own(a, shape, dt):
+            if a is None:
+                return np.empty(shape, dt)
+            if a.dtype != dt or a.size != shape[0] * shape[1] or not a.flags.c_contiguous:
+                raise ValueError("output buffer shape mismatch")
+            return a
+        out = own(out, (rows, self.hidden), np.float32)
+        ids = own(ids, (rows, self.top), np.int32)
+        routes = own(routes, (rows, self.top), np.float32)
         t = L.Timings() if timings else None
         rc = self.owner.lib.moe_b200_forward_f32(
             self.workspace, self.weights.raw, router.raw, rows, _ptr(inp), _ptr(res), _ptr(out),
