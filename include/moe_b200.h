@@ -55,6 +55,13 @@ extern "C" {
 /* Router accumulation order (src/model/cpu.rs:96-153, dense_dot). */
 #define MOE_B200_ROUTER_NEON16 0     /* aarch64 F32 branch: 4x4-lane FMA + fixed tree */
 #define MOE_B200_ROUTER_SEQUENTIAL 1 /* x86 scalar loop: separately rounded mul + add */
+#define MOE_B200_ROUTER_TF32 2       /* Ling's TF32 linear (src/npu/tf32.rs): operands
+                                        narrowed to TF32, f32 sums (within 5e-5 of the
+                                        f64 sum, the reference's own bound) */
+
+/* Routing rules. */
+#define MOE_B200_ROUTE_SOFTMAX 0          /* routes(), src/model/qwen35/moe.rs:51-67 */
+#define MOE_B200_ROUTE_GROUPED_SIGMOID 1  /* Ling, src/model/ling3tiny/moe.rs:146-223 */
 
 /* Shared expert arithmetic. */
 #define MOE_B200_SHARED_JOINT 0 /* MoE input quantisation, nearest-even (joint bank) */
@@ -170,8 +177,40 @@ moe_b200_router *moe_b200_router_create(const moe_b200_config *cfg, const float 
                                         const float *bias, int32_t order, float min_weight);
 void moe_b200_router_free(moe_b200_router *r);
 
+/* Router options beyond moe_b200_router_create (no counterpart in the
+ * reference's native ABI: these replace the CPU-side routing of
+ * src/model/ling3tiny/moe.rs:146-223 and the shared-expert gate merge of
+ * src/model/qwen35/moe.rs:334-347). */
+typedef struct {
+    int32_t order;            /* MOE_B200_ROUTER_* */
+    int32_t rule;             /* MOE_B200_ROUTE_* */
+    float min_weight;         /* softmax rule only: pruning threshold, 0 = off */
+    const float *bias;        /* [experts] added to every logit, or NULL */
+    /* MOE_B200_ROUTE_GROUPED_SIGMOID (Ling: n_group, topk_group,
+     * routed_scaling_factor, gate.expert_bias): score = sigmoid(logit);
+     * selected = score + expert_bias; experts / groups >= 2, groups <= 32,
+     * top_groups <= groups, top <= top_groups * experts / groups,
+     * experts <= 256 */
+    int32_t groups, top_groups;
+    float routing_scale;
+    const float *expert_bias; /* [experts] */
+    /* shared-expert gate row [hidden] f32 (mlp.shared_expert_gate.weight), or
+     * NULL. With a gate the forward adds sigmoid(gate . x) * shared instead
+     * of shared; the gate logit is computed in the router's dot order as
+     * one more row after the experts, so router logits have experts + 1
+     * columns (the last is the gate logit). */
+    const float *shared_gate;
+} moe_b200_router_options;
+
+/* Defaults: NEON16 order, softmax rule, no bias, no pruning, no gate. */
+void moe_b200_router_options_init(moe_b200_router_options *opt);
+/* NULL on an invalid option set. */
+moe_b200_router *moe_b200_router_create_ex(const moe_b200_config *cfg, const float *router,
+                                           const moe_b200_router_options *opt);
+
 /* Host pointers, synchronous: output = residual + (routed + shared); residual
- * may be NULL. ids/routes, if not NULL, receive the routing [rows][top]. */
+ * may be NULL. ids/routes, if not NULL, receive the routing [rows][top].
+ * With a gated router the shared term is sigmoid(gate . x) * shared. */
 int moe_b200_forward_f32(moe_b200_workspace *ws, const moe_b200_weights *w,
                          const moe_b200_router *r, int32_t rows, const float *input,
                          const float *residual, float *output, int32_t *ids, float *routes,
@@ -184,7 +223,8 @@ int moe_b200_forward_device(moe_b200_workspace *ws, const moe_b200_weights *w,
 /* ---- stage entry points (extension; for parity checks and expert
  * parallelism). All device pointers, asynchronous. ---------------------- */
 
-/* Router logits (may be NULL) + top-k/softmax/pruning. */
+/* Router logits (may be NULL; [rows][experts], or [rows][experts + 1] for a
+ * router with a shared gate) + the routing rule (top-k, weights, pruning). */
 int moe_b200_route_device(moe_b200_workspace *ws, const moe_b200_router *r, int32_t rows,
                           const float *d_input, float *d_logits, int32_t *d_ids,
                           float *d_routes, void *stream);
@@ -196,7 +236,8 @@ int moe_b200_workspace_status(moe_b200_workspace *ws);
 /* Device address and size of a workspace buffer, for inspection by tests:
  * "q_x","s_x","perm","pos","offsets","a_perm","s_perm","gate_up" (f32
  * [rows][2I]: dequantised gate then up, before SwiGLU),"q_m","s_m","y",
- * "shared_y","logits","ids","routes". Valid until the next call. */
+ * "shared_y","logits" ([rows][experts], or [rows][experts + 1] after a gated
+ * router),"ids","routes". Valid until the next call. */
 int moe_b200_workspace_buffer(moe_b200_workspace *ws, const char *name, void **d_ptr,
                               uint64_t *bytes);
 

@@ -31,6 +31,9 @@ W8_PER_CHANNEL = 2
 W4_G32_FP16_EXACT = 3
 ROUTER_NEON16 = 0
 ROUTER_SEQUENTIAL = 1
+ROUTER_TF32 = 2
+ROUTE_SOFTMAX = 0
+ROUTE_GROUPED_SIGMOID = 1
 SHARED_JOINT = 0
 SHARED_DENSE = 1
 
@@ -55,6 +58,13 @@ class Expert(C.Structure):
 class Format(C.Structure):
     _fields_ = [("routed_format", C.c_int32), ("shared_format", C.c_int32),
                 ("shared_mode", C.c_int32)]
+
+
+class RouterOptions(C.Structure):
+    _fields_ = [("order", C.c_int32), ("rule", C.c_int32), ("min_weight", C.c_float),
+                ("bias", C.c_void_p), ("groups", C.c_int32), ("top_groups", C.c_int32),
+                ("routing_scale", C.c_float), ("expert_bias", C.c_void_p),
+                ("shared_gate", C.c_void_p)]
 
 
 class Timings(C.Structure):
@@ -89,6 +99,9 @@ SIGNATURES = [
     ("moe_b200_router_create", C.c_void_p,
      [C.POINTER(Config), C.c_void_p, C.c_void_p, C.c_int32, C.c_float]),
     ("moe_b200_router_free", None, [C.c_void_p]),
+    ("moe_b200_router_options_init", None, [C.POINTER(RouterOptions)]),
+    ("moe_b200_router_create_ex", C.c_void_p,
+     [C.POINTER(Config), C.c_void_p, C.POINTER(RouterOptions)]),
     ("moe_b200_forward_f32", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
       C.c_void_p, C.c_void_p, C.POINTER(Timings)]),

@@ -12,6 +12,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <cmath>
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -278,8 +280,13 @@ struct moe_b200_weights {
 struct moe_b200_router {
     int device = 0, H = 0, E = 0, order = 0;
     float min_weight = 0.0f;
-    float* w = nullptr;
+    float* w = nullptr;     // [E (+1 gate row)][H]
     float* bias = nullptr;
+    int rule = 0, groups = 1, top_groups = 1;
+    float scale = 1.0f;
+    float* sel_bias = nullptr;
+    bool gate = false;      // row E of w is the shared-expert gate
+    int rows() const { return E + (gate ? 1 : 0); }
 };
 
 struct moe_b200_workspace {
@@ -324,6 +331,7 @@ struct moe_b200_workspace {
     int64_t launches = 0;
     // last call, for accumulator dumps
     int last_rows = 0;
+    int last_logit_cols = 0;  // logits row stride of the last routing call
     int last_nt_gu = 16, last_nt_dn = 16;
     const moe_b200_weights* last_w = nullptr;
 };
@@ -425,9 +433,16 @@ cudaEvent_t* prof_slot(moe_b200_workspace* ws, int flags) {
 
 // The whole routed (+ shared) pipeline on device pointers. ev != null records
 // stage events for run_profiled-style timings.
+// The shared-gate logits of a gated router: column E of the workspace logits.
+struct GateRef {
+    const float* logits = nullptr;
+    int ld = 0;
+};
+
 int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
                  const int32_t* d_ids, const float* d_routes, const float* d_res, float* d_out,
-                 cudaStream_t s, cudaEvent_t* evs, cudaEvent_t res_ready = nullptr) {
+                 cudaStream_t s, cudaEvent_t* evs, cudaEvent_t res_ready = nullptr,
+                 GateRef gate = {}) {
     const int E = ws->E, k = ws->k, H = ws->H, I = ws->I;
     const long n = (long)rows * k;
     auto mark = [&](int i) {
@@ -468,7 +483,7 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
     mark(7);
     if (res_ready) cudaStreamWaitEvent(s, res_ready, 0);  // residual uploaded on the side
     launch_combine(ws->y, ws->pos, d_routes, w->shared ? ws->s_y : nullptr, d_res, rows, H, k,
-                   d_out, s);
+                   d_out, s, gate.logits, gate.ld);
     mark(8);
     ws->last_rows = rows;
     ws->last_nt_gu = nt_g;
@@ -696,7 +711,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     rc |= ws_alloc(ws, &ws->q_m, (n + pad_rows) * ws->Ki);
     rc |= ws_alloc(ws, &ws->s_m, n);
     rc |= ws_alloc(ws, &ws->y, n * ws->H);
-    rc |= ws_alloc(ws, &ws->logits, T * ws->E);
+    rc |= ws_alloc(ws, &ws->logits, T * (ws->E + 1));  // + the shared-gate column
     rc |= ws_alloc(ws, &ws->err, 1);
     if (ws->Is > 0 && rc == MOE_B200_OK) {
         rc |= ws_alloc(ws, &ws->q_xd, (T + pad_rows) * ws->Kh);
@@ -819,33 +834,100 @@ int moe_b200_run_f32(moe_b200_workspace* ws, const moe_b200_weights* w, int32_t 
     return rc;
 }
 
-moe_b200_router* moe_b200_router_create(const moe_b200_config* cfg, const float* router,
-                                        const float* bias, int32_t order, float min_weight) {
-    if (validate_config(cfg) || !router) return nullptr;
-    if (order != MOE_B200_ROUTER_NEON16 && order != MOE_B200_ROUTER_SEQUENTIAL) return nullptr;
-    if (!(min_weight >= 0.0f && min_weight <= 1.0f)) return nullptr;  // pruning::validate
+void moe_b200_router_options_init(moe_b200_router_options* opt) {
+    if (!opt) return;
+    *opt = moe_b200_router_options{};
+    opt->order = MOE_B200_ROUTER_NEON16;
+    opt->rule = MOE_B200_ROUTE_SOFTMAX;
+    opt->groups = 1;
+    opt->top_groups = 1;
+    opt->routing_scale = 1.0f;
+}
+
+static bool finite_all(const float* v, size_t n) {
+    for (size_t i = 0; i < n; ++i)
+        if (!std::isfinite(v[i])) return false;
+    return true;
+}
+
+moe_b200_router* moe_b200_router_create_ex(const moe_b200_config* cfg, const float* router,
+                                           const moe_b200_router_options* opt) {
+    if (validate_config(cfg) || !router || !opt) return nullptr;
+    const int H = cfg->weights.hidden, E = cfg->weights.routed_experts, k = cfg->top;
+    if (opt->order != MOE_B200_ROUTER_NEON16 && opt->order != MOE_B200_ROUTER_SEQUENTIAL &&
+        opt->order != MOE_B200_ROUTER_TF32)
+        return nullptr;
+    if (!(opt->min_weight >= 0.0f && opt->min_weight <= 1.0f)) return nullptr;  // pruning::validate
+    if (opt->rule == MOE_B200_ROUTE_GROUPED_SIGMOID) {
+        // the Ling config check (src/model/ling3tiny/config.rs:113-124) plus
+        // this kernel's limits (one warp per row: E <= 256, groups <= 32)
+        const int g = opt->groups, tg = opt->top_groups;
+        if (g <= 0 || g > 32 || E % g != 0 || E / g < 2 || tg <= 0 || tg > g ||
+            k > tg * (E / g) || !(opt->routing_scale > 0.0f) || !opt->expert_bias ||
+            E > moe::kGroupedMaxExperts || opt->min_weight != 0.0f)
+            return nullptr;
+        if (!finite_all(opt->expert_bias, (size_t)E)) return nullptr;
+    } else if (opt->rule != MOE_B200_ROUTE_SOFTMAX) {
+        return nullptr;
+    }
     if (check_device(cfg->device, nullptr)) return nullptr;
     DeviceGuard guard(cfg->device);
     auto* r = new moe_b200_router();
     r->device = cfg->device;
-    r->H = cfg->weights.hidden;
-    r->E = cfg->weights.routed_experts;
-    r->order = order;
-    r->min_weight = min_weight;
-    const size_t wb = sizeof(float) * (size_t)r->H * r->E;
+    r->H = H;
+    r->E = E;
+    r->order = opt->order;
+    r->min_weight = opt->min_weight;
+    r->rule = opt->rule;
+    r->groups = opt->groups;
+    r->top_groups = opt->top_groups;
+    r->scale = opt->routing_scale;
+    r->gate = opt->shared_gate != nullptr;
+    const size_t row_bytes = sizeof(float) * (size_t)H;
     void* p = nullptr;
-    if (dev_alloc(&p, wb) != cudaSuccess) { delete r; return nullptr; }
+    if (dev_alloc(&p, row_bytes * r->rows()) != cudaSuccess) { delete r; return nullptr; }
     r->w = static_cast<float*>(p);
-    cudaMemcpy(r->w, router, wb, cudaMemcpyHostToDevice);
-    if (bias) {
-        if (dev_alloc(&p, sizeof(float) * r->E) != cudaSuccess) {
-            moe_b200_router_free(r);
-            return nullptr;
+    if (opt->order == MOE_B200_ROUTER_TF32) {
+        // the NPU narrows the resident weights once (src/npu/tf32.rs:114-140)
+        std::vector<float> t((size_t)H * r->rows());
+        std::memcpy(t.data(), router, row_bytes * E);
+        if (r->gate) std::memcpy(t.data() + (size_t)E * H, opt->shared_gate, row_bytes);
+        for (float& v : t) {
+            uint32_t u;
+            std::memcpy(&u, &v, 4);
+            u &= ~0x1FFFu;
+            std::memcpy(&v, &u, 4);
         }
-        r->bias = static_cast<float*>(p);
-        cudaMemcpy(r->bias, bias, sizeof(float) * r->E, cudaMemcpyHostToDevice);
+        cudaMemcpy(r->w, t.data(), row_bytes * r->rows(), cudaMemcpyHostToDevice);
+    } else {
+        cudaMemcpy(r->w, router, row_bytes * E, cudaMemcpyHostToDevice);
+        if (r->gate)
+            cudaMemcpy(r->w + (size_t)E * H, opt->shared_gate, row_bytes, cudaMemcpyHostToDevice);
+    }
+    auto upload = [&](float** dst, const float* src) {
+        if (!src) return true;
+        void* q = nullptr;
+        if (dev_alloc(&q, sizeof(float) * E) != cudaSuccess) return false;
+        *dst = static_cast<float*>(q);
+        return cudaMemcpy(*dst, src, sizeof(float) * E, cudaMemcpyHostToDevice) == cudaSuccess;
+    };
+    if (!upload(&r->bias, opt->bias) ||
+        !upload(&r->sel_bias, opt->rule == MOE_B200_ROUTE_GROUPED_SIGMOID ? opt->expert_bias
+                                                                         : nullptr)) {
+        moe_b200_router_free(r);
+        return nullptr;
     }
     return r;
+}
+
+moe_b200_router* moe_b200_router_create(const moe_b200_config* cfg, const float* router,
+                                        const float* bias, int32_t order, float min_weight) {
+    moe_b200_router_options opt;
+    moe_b200_router_options_init(&opt);
+    opt.order = order;
+    opt.min_weight = min_weight;
+    opt.bias = bias;
+    return moe_b200_router_create_ex(cfg, router, &opt);
 }
 
 void moe_b200_router_free(moe_b200_router* r) {
@@ -853,7 +935,17 @@ void moe_b200_router_free(moe_b200_router* r) {
     DeviceGuard guard(r->device);
     if (r->w) cudaFree(r->w);
     if (r->bias) cudaFree(r->bias);
+    if (r->sel_bias) cudaFree(r->sel_bias);
     delete r;
+}
+
+static GateRef router_gate(const moe_b200_workspace* ws, const moe_b200_router* r) {
+    GateRef g;
+    if (r->gate) {
+        g.logits = ws->logits + r->E;
+        g.ld = r->rows();
+    }
+    return g;
 }
 
 static int route_impl(moe_b200_workspace* ws, const moe_b200_router* r, int rows, const float* d_x,
@@ -865,10 +957,17 @@ static int route_impl(moe_b200_workspace* ws, const moe_b200_router* r, int rows
     a.T = rows;
     a.H = r->H;
     a.E = r->E;
+    a.Ew = r->rows();
     a.k = ws->k;
     a.order = r->order;
     a.min_weight = r->min_weight;
+    a.rule = r->rule;
+    a.sel_bias = r->sel_bias;
+    a.groups = r->groups;
+    a.top_groups = r->top_groups;
+    a.scale = r->scale;
     a.logits = d_logits ? d_logits : ws->logits;
+    ws->last_logit_cols = r->rows();
     a.counters = ws->counters;
     a.ids = d_ids;
     a.weights = d_routes;
@@ -910,7 +1009,8 @@ int moe_b200_forward_device(moe_b200_workspace* ws, const moe_b200_weights* w,
     if (evs) cudaEventRecord(evs[0], s);
     rc = route_impl(ws, r, rows, d_input, nullptr, ws->ids, ws->routes, s);
     if (rc) return rc;
-    return run_pipeline(ws, w, rows, d_input, ws->ids, ws->routes, d_residual, d_output, s, evs);
+    return run_pipeline(ws, w, rows, d_input, ws->ids, ws->routes, d_residual, d_output, s, evs,
+                        nullptr, router_gate(ws, r));
 }
 
 struct moe_b200_graph {
@@ -942,7 +1042,8 @@ moe_b200_graph* moe_b200_graph_create(moe_b200_workspace* ws, const moe_b200_wei
     }
     rc = route_impl(ws, r, rows, d_input, nullptr, ws->ids, ws->routes, s);
     if (rc == MOE_B200_OK)
-        rc = run_pipeline(ws, w, rows, d_input, ws->ids, ws->routes, d_residual, d_output, s, nullptr);
+        rc = run_pipeline(ws, w, rows, d_input, ws->ids, ws->routes, d_residual, d_output, s, nullptr,
+                          nullptr, router_gate(ws, r));
     const cudaError_t e = cudaStreamEndCapture(s, &g);
     ws->profiling = prof;
     if (rc != MOE_B200_OK || e != cudaSuccess || !g) {
@@ -1104,7 +1205,8 @@ int moe_b200_forward_f32(moe_b200_workspace* ws, const moe_b200_weights* w,
     rc = route_impl(ws, r, rows, ws->x, nullptr, ws->ids, ws->routes, s);
     if (rc) return rc;
     rc = run_pipeline(ws, w, rows, ws->x, ws->ids, ws->routes, residual ? ws->res : nullptr,
-                      ws->out, s, timings ? ws->ev : nullptr, residual ? ws->res_ready : nullptr);
+                      ws->out, s, timings ? ws->ev : nullptr, residual ? ws->res_ready : nullptr,
+                      router_gate(ws, r));
     if (rc) return rc;
     cudaMemcpyAsync(output, ws->out, xb, cudaMemcpyDeviceToHost, s);
     if (ids) cudaMemcpyAsync(ids, ws->ids, sizeof(int32_t) * nb, cudaMemcpyDeviceToHost, s);
@@ -1151,7 +1253,8 @@ int moe_b200_workspace_buffer(moe_b200_workspace* ws, const char* name, void** d
         {"s_m", ws->s_m, sizeof(float) * (uint64_t)n},
         {"y", ws->y, sizeof(float) * (uint64_t)n * ws->H},
         {"shared_y", ws->s_y, ws->s_y ? sizeof(float) * (uint64_t)T * ws->H : 0},
-        {"logits", ws->logits, sizeof(float) * (uint64_t)T * ws->E},
+        {"logits", ws->logits,
+         sizeof(float) * (uint64_t)T * (ws->last_logit_cols ? ws->last_logit_cols : ws->E)},
         {"ids", ws->ids, sizeof(int32_t) * (uint64_t)n},
         {"routes", ws->routes, sizeof(float) * (uint64_t)n},
     };

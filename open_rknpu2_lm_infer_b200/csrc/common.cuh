@@ -323,5 +323,28 @@ __device__ __forceinline__ int32_t total_key(float v) {
     int32_t b = __float_as_int(v);
     return b ^ (int32_t)((uint32_t)(b >> 31) >> 1);
 }
+// total_key is an involution on the bit pattern: the key's value back.
+__device__ __forceinline__ float key_value(int32_t key) {
+    return __int_as_float(key ^ (int32_t)((uint32_t)(key >> 31) >> 1));
+}
+
+// f32 exp for the sigmoid gates: the double-precision exp rounded once to
+// f32, i.e. the correctly rounded f32 result up to double rounding. The
+// glibc expf (the C library the reference builds against) differs from it by
+// one ulp on about 1 in 13,000 f32 arguments.
+__device__ __forceinline__ float exp_f32(float x) { return __double2float_rn(exp((double)x)); }
+
+// sigmoid of src/ops/activation.rs:7-14: exp's argument is kept <= 0.
+__device__ __forceinline__ float sigmoid_ref(float x) {
+    if (x >= 0.0f) return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_f32(-x)));
+    const float e = exp_f32(x);
+    return __fdiv_rn(e, __fadd_rn(1.0f, e));
+}
+
+// TF32 narrowing of the NPU linear (src/npu/tf32.rs): the low 13 mantissa
+// bits are dropped (truncation, not rounding).
+__device__ __forceinline__ float tf32_trunc(float v) {
+    return __uint_as_float(__float_as_uint(v) & ~0x1FFFu);
+}
 
 }  // namespace moe

@@ -302,14 +302,20 @@ requant_kernel(const float* __restrict__ gate_up, const int32_t* __restrict__ co
     }
 }
 
-// One CTA (256 threads) per token, float4 columns (H % 4 == 0).
+// One CTA (256 threads) per token, float4 columns (H % 4 == 0). With a shared
+// gate the shared row enters as projected += scale * shared, scale =
+// 1 / (1 + exp(-gate)) (src/model/qwen35/moe.rs:334-347, two roundings).
 __global__ void __launch_bounds__(256)
 combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ pos,
                const float* __restrict__ routes, const float* __restrict__ shared,
-               const float* __restrict__ residual, int H, int k, float* out) {
+               const float* __restrict__ residual, int H, int k, float* out,
+               const float* __restrict__ gate, int gate_ld) {
     __shared__ int ps[32];
     __shared__ float ws[32];
+    __shared__ float gscale;
     const int t = blockIdx.x;
+    if (gate && threadIdx.x == 32)
+        gscale = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_f32(-gate[(size_t)t * gate_ld])));
     if (threadIdx.x < k) {
         const size_t a = (size_t)t * k + threadIdx.x;
         const float w = routes[a];
@@ -331,7 +337,13 @@ combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ pos,
             acc.w = __fmaf_rn(yv.w, w, acc.w);
         }
         if (shared) {
-            const float4 sv = reinterpret_cast<const float4*>(shared + (size_t)t * H)[c];
+            float4 sv = reinterpret_cast<const float4*>(shared + (size_t)t * H)[c];
+            if (gate) {
+                sv.x = __fmul_rn(gscale, sv.x);
+                sv.y = __fmul_rn(gscale, sv.y);
+                sv.z = __fmul_rn(gscale, sv.z);
+                sv.w = __fmul_rn(gscale, sv.w);
+            }
             acc.x = __fadd_rn(acc.x, sv.x);
             acc.y = __fadd_rn(acc.y, sv.y);
             acc.z = __fadd_rn(acc.z, sv.z);
@@ -440,9 +452,11 @@ void launch_requant(const float* gate_up, const int32_t* count, int max_rows, in
 }
 
 void launch_combine(const float* y, const int32_t* pos, const float* routes, const float* shared,
-                    const float* residual, int T, int H, int k, float* out, cudaStream_t s) {
+                    const float* residual, int T, int H, int k, float* out, cudaStream_t s,
+                    const float* gate, int gate_ld) {
     if (T == 0) return;
-    combine_kernel<<<T, 256, 0, s>>>(y, pos, routes, shared, residual, H, k, out);
+    combine_kernel<<<T, 256, 0, s>>>(y, pos, routes, shared, residual, H, k, out,
+                                     shared ? gate : nullptr, gate_ld);
 }
 
 }  // namespace moe

@@ -20,18 +20,31 @@ enum { kEpiGateUp = 0, kEpiStore = 1, kEpiAcc = 2 };
 // Activation quantisation rules.
 enum { kQuantMoe = 0, kQuantDense = 1 };
 
+// Routing rules: softmax over the top-k logits (Qwen), and grouped sigmoid
+// top-k with a selection bias (Ling).
+enum { kRouteSoftmax = 0, kRouteGroupedSigmoid = 1 };
+// Router dot orders (values match MOE_B200_ROUTER_*).
+enum { kOrderNeon16 = 0, kOrderSequential = 1, kOrderTf32 = 2 };
+
 struct RouterArgs {
     const float* x;       // [T][H]
-    const float* w;       // [E][H]
-    const float* bias;    // [E] or null
+    const float* w;       // [Ew][H]: E expert rows, then the shared-gate row if any
+    const float* bias;    // [E] added to the logits, or null
     int T, H, E, k, order;
+    int Ew;               // weight rows = logits row stride (0 means E)
     float min_weight;
-    float* logits;        // [T][E] scratch / output
+    float* logits;        // [T][Ew] scratch / output
     int* counters;        // [ceil(T)] zeroed tile counters
     int32_t* ids;         // [T][k]
     float* weights;       // [T][k]
     uint32_t* err;
+    // grouped sigmoid rule
+    int rule;             // kRoute*
+    const float* sel_bias;  // [E] selection bias
+    int groups, top_groups;
+    float scale;          // routing scale
 };
+constexpr int kGroupedMaxExperts = 256;  // grouped sigmoid: E <= 8 per lane of a warp
 
 struct GemmArgs {
     const float* act_scale;   // per permuted row
@@ -59,6 +72,8 @@ struct GemmArgs {
 
 __device__ void topk_row(const float* row, int E, int k, float min_weight, int32_t* ids,
                          float* weights, int lane, uint32_t* err);
+__device__ void grouped_row(const float* row, const RouterArgs& a, int32_t* ids, float* weights,
+                            int lane);
 
 int launch_router(const RouterArgs& a, cudaStream_t s);
 int launch_gemm(const CUtensorMap& map, const GemmArgs& a, int fmt, int epi, int nt,
@@ -87,8 +102,11 @@ void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k
                          cudaStream_t s);
 void launch_requant(const float* gate_up, const int32_t* count, int max_rows, int I, int ld_q,
                     int rule, int8_t* q, __half* qh, float* sc, cudaStream_t s);
+// gate (may be null): the shared-gate logit of token t at gate[t * gate_ld];
+// the shared row then enters as sigmoid(gate) * shared.
 void launch_combine(const float* y, const int32_t* pos, const float* routes, const float* shared,
-                    const float* residual, int T, int H, int k, float* out, cudaStream_t s);
+                    const float* residual, int T, int H, int k, float* out, cudaStream_t s,
+                    const float* gate = nullptr, int gate_ld = 0);
 
 constexpr int kRouteChunk = 512;  // assignments per route_count / route_scatter CTA
 

@@ -1,16 +1,23 @@
-// Router logits + softmax top-k (+ renormalisation and optional pruning).
+// Router logits + top-k routing (+ renormalisation and optional pruning).
 //
 // Reference semantics (happyme531/open_rknpu2_lm_infer):
-//   logits  : Cpu::dense_head_batch / dense_dot, src/model/cpu.rs:96-153,302-316
-//   top-k   : routes(), src/model/qwen35/moe.rs:51-67 (total_cmp desc, lower id on ties,
+//   logits  : Cpu::dense_head_batch / dense_dot, src/model/cpu.rs:96-153,302-316;
+//             Ling's TF32 NPU linear, src/npu/tf32.rs:142-170 (operands narrowed)
+//   softmax : routes(), src/model/qwen35/moe.rs:51-67 (total_cmp desc, lower id on ties,
 //             weights = exp(l - l_max) / sum over the selected k)
+//   grouped : RoutingScratch::routes, src/model/ling3tiny/moe.rs:146-223 (sigmoid
+//             scores, biased selection, top-2 group sums, top groups, routing scale)
 //   pruning : pruning::apply, src/model/experts/pruning.rs:32-41
+//   gate    : the shared-expert gate row, src/model/qwen35/moe.rs:334-347, is one
+//             more weight row after the E experts (logit column E)
 //
 // The NEON16 order keeps 16 independent FMA lanes per (token, expert) dot —
 // lane j accumulates elements 16i + j — then reduces them with the fixed tree
 // (l[j]+l[j+4]) + (l[j+8]+l[j+12]) and ((v0+v1)+(v2+v3)) of vaddq/vaddvq, and
 // finishes with a separately rounded scalar tail. Every rounding step matches
-// the reference, so logits (and hence expert ids) are bit-identical.
+// the reference, so logits (and hence expert ids) are bit-identical. The TF32
+// order runs the same kernels on operands narrowed to TF32; the reference's
+// NPU fixes no summation order, only a bound (5e-5 of the f64 sum).
 #include "kernels.cuh"
 
 namespace moe {
@@ -27,58 +34,68 @@ __device__ __forceinline__ float neon16_tree(float v) {
     return __fadd_rn(p, __shfl_down_sync(0xffffffffu, p, 2, 16));       // total
 }
 
-// Scalar tail (H % 16 elements, separately rounded products) and the bias.
+template <bool TF32>
+__device__ __forceinline__ float xval(float v) {
+    return TF32 ? tf32_trunc(v) : v;
+}
+
+// Scalar tail (H % 16 elements, separately rounded products) and the logit
+// bias (expert rows only).
+template <bool TF32>
 __device__ __forceinline__ float neon16_finish(float q, const float* wrow, const float* xrow,
-                                               int H16, int H, const float* bias, int e) {
-    for (int h = H16; h < H; ++h) q = __fadd_rn(q, __fmul_rn(wrow[h], xrow[h]));
-    if (bias) q = __fadd_rn(q, bias[e]);
+                                               int H16, int H, const float* bias, int e, int E) {
+    for (int h = H16; h < H; ++h) q = __fadd_rn(q, __fmul_rn(wrow[h], xval<TF32>(xrow[h])));
+    if (bias && e < E) q = __fadd_rn(q, bias[e]);
     return q;
 }
 
-// Last CTA of a token tile (all expert blocks done) runs top-k for its tokens.
-__device__ __forceinline__ void finish_tile(int* tile_counter, int tile, int t0, int nt, int E,
-                                            const float* logits, int k, float min_weight,
-                                            int32_t* ids, float* weights, uint32_t* err) {
+__device__ __forceinline__ void route_row(const RouterArgs& a, int t, int lane) {
+    const float* row = a.logits + (size_t)t * a.Ew;
+    if (a.rule == kRouteGroupedSigmoid)
+        grouped_row(row, a, a.ids + (size_t)t * a.k, a.weights + (size_t)t * a.k, lane);
+    else
+        topk_row(row, a.E, a.k, a.min_weight, a.ids + (size_t)t * a.k,
+                 a.weights + (size_t)t * a.k, lane, a.err);
+}
+
+// Last CTA of a token tile (all expert blocks done) routes its tokens.
+__device__ __forceinline__ void finish_tile(const RouterArgs& a, int tile, int t0, int nt) {
     __shared__ int is_last;
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
-        const int prev = atomicAdd(&tile_counter[tile], 1);
+        const int prev = atomicAdd(&a.counters[tile], 1);
         is_last = (prev == (int)gridDim.y - 1);
     }
     __syncthreads();
     if (!is_last) return;
     __threadfence();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int t = warp; t < nt; t += blockDim.x / 32)
-        topk_row(logits + (size_t)(t0 + t) * E, E, k, min_weight, ids + (size_t)(t0 + t) * k,
-                 weights + (size_t)(t0 + t) * k, lane, err);
-    if (threadIdx.x == 0) tile_counter[tile] = 0;
+    for (int t = warp; t < nt; t += blockDim.x / 32) route_row(a, t0 + t, lane);
+    if (threadIdx.x == 0) a.counters[tile] = 0;
 }
 
-// Decode-sized router: one token, 8 experts per CTA (grid (T, ceil(E/8))),
-// 128 threads = 8 experts x 16 lanes. The CTA's router rows and the token
-// row are staged in shared memory with one batch of 16-byte copies, then each
+// Decode-sized router: one token, 8 weight rows per CTA (grid (T, ceil(Ew/8))),
+// 128 threads = 8 rows x 16 lanes. The CTA's router rows and the token row
+// are staged in shared memory with one batch of 16-byte copies, then each
 // thread runs its lane's sequential FMA chain.
 constexpr int kDecEB = 8;
-__global__ void __launch_bounds__(128)
-router_decode_kernel(const float* __restrict__ x, const float* __restrict__ wr,
-                     const float* __restrict__ bias, int T, int H, int E, float* logits,
-                     int* tile_counter, int k, float min_weight, int32_t* ids, float* weights,
-                     uint32_t* err) {
+template <bool TF32>
+__global__ void __launch_bounds__(128) router_decode_kernel(const RouterArgs a) {
     extern __shared__ __align__(16) float rsm[];
-    const int stride = H + 16;  // padded rows: the two experts of a warp use different banks
+    const int H = a.H;
+    const int stride = H + 16;  // padded rows: the two rows of a warp use different banks
     float* w_s = rsm;                     // [8][stride]
     float* x_s = rsm + kDecEB * stride;   // [H]
     const int t = blockIdx.x, e0 = blockIdx.y * kDecEB;
-    const int ne = min(kDecEB, E - e0);
+    const int ne = min(kDecEB, a.Ew - e0);
     const int H16 = (H / 16) * 16;
     const bool vec = (H & 3) == 0;
     if (vec) {
         const int q4 = H / 4;
         for (int idx = threadIdx.x; idx < (ne + 1) * q4; idx += blockDim.x) {
             const int r = idx / q4, q = idx % q4;
-            const float* src = r < ne ? wr + (size_t)(e0 + r) * H + 4 * q : x + (size_t)t * H + 4 * q;
+            const float* src = r < ne ? a.w + (size_t)(e0 + r) * H + 4 * q : a.x + (size_t)t * H + 4 * q;
             float* dst = r < ne ? w_s + r * stride + 4 * q : x_s + 4 * q;
             asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src));
         }
@@ -86,8 +103,8 @@ router_decode_kernel(const float* __restrict__ x, const float* __restrict__ wr,
     } else {
         for (int idx = threadIdx.x; idx < (ne + 1) * H; idx += blockDim.x) {
             const int r = idx / H, h = idx % H;
-            if (r < ne) w_s[r * stride + h] = wr[(size_t)(e0 + r) * H + h];
-            else x_s[h] = x[(size_t)t * H + h];
+            if (r < ne) w_s[r * stride + h] = a.w[(size_t)(e0 + r) * H + h];
+            else x_s[h] = a.x[(size_t)t * H + h];
         }
     }
     __syncthreads();
@@ -96,32 +113,30 @@ router_decode_kernel(const float* __restrict__ x, const float* __restrict__ wr,
     if (el < ne) {
         const float* wrow = w_s + el * stride;
 #pragma unroll 8
-        for (int i = 0; i < H16; i += 16) acc = __fmaf_rn(wrow[i + j], x_s[i + j], acc);
+        for (int i = 0; i < H16; i += 16)
+            acc = __fmaf_rn(wrow[i + j], xval<TF32>(x_s[i + j]), acc);
     }
     const float q = neon16_tree(acc);
     if (j == 0 && el < ne)
-        logits[(size_t)t * E + e0 + el] =
-            neon16_finish(q, w_s + el * stride, x_s, H16, H, bias, e0 + el);
-    finish_tile(tile_counter, t, t, 1, E, logits, k, min_weight, ids, weights, err);
+        a.logits[(size_t)t * a.Ew + e0 + el] =
+            neon16_finish<TF32>(q, w_s + el * stride, x_s, H16, H, a.bias, e0 + el, a.E);
+    finish_tile(a, t, t, 1);
 }
 
-// Prefill-sized router: TT tokens x EB experts per CTA (grid (ceil(T/TT),
-// ceil(E/EB))), 256 threads = 16 lanes x 16 groups; a group owns EB/16 experts
+// Prefill-sized router: TT tokens x EB weight rows per CTA (grid (ceil(T/TT),
+// ceil(Ew/EB))), 256 threads = 16 lanes x 16 groups; a group owns EB/16 rows
 // for all TT tokens. Hidden dimension streamed in chunks of kCh through a
 // kStg-deep cp.async ring.
-template <int TT, int EB>
-__global__ void __launch_bounds__(kRouterThreads)
-router_tile_kernel(const float* __restrict__ x, const float* __restrict__ wr,
-                   const float* __restrict__ bias, int T, int H, int E, float* logits,
-                   int* tile_counter, int k, float min_weight, int32_t* ids, float* weights,
-                   uint32_t* err) {
+template <int TT, int EB, bool TF32>
+__global__ void __launch_bounds__(kRouterThreads) router_tile_kernel(const RouterArgs a) {
     constexpr int EPG = EB / 16;
     constexpr int kCh = 128, kStg = 4, kWS = kCh + 16;
     constexpr int kStageF = EB * kWS + TT * kCh;
     extern __shared__ __align__(16) float rsm[];
+    const int H = a.H;
     const int tid = threadIdx.x, j = tid & 15, g = tid >> 4;
     const int t0 = blockIdx.x * TT, e0 = blockIdx.y * EB;
-    const int ne = min(EB, E - e0), nt = min(TT, T - t0);
+    const int ne = min(EB, a.Ew - e0), nt = min(TT, a.T - t0);
     const int H16 = (H / 16) * 16;
     const int nchunks = (H16 + kCh - 1) / kCh;
     const bool vec = (H & 3) == 0;
@@ -136,8 +151,8 @@ router_tile_kernel(const float* __restrict__ x, const float* __restrict__ wr,
             if (q >= q4) continue;
             const bool isw = r < EB;
             if (isw ? r >= ne : (r - EB) >= nt) continue;
-            const float* src = isw ? wr + (size_t)(e0 + r) * H + h0 + 4 * q
-                                   : x + (size_t)(t0 + r - EB) * H + h0 + 4 * q;
+            const float* src = isw ? a.w + (size_t)(e0 + r) * H + h0 + 4 * q
+                                   : a.x + (size_t)(t0 + r - EB) * H + h0 + 4 * q;
             float* dst = isw ? w_s + r * kWS + 4 * q : x_s + (r - EB) * kCh + 4 * q;
             if (vec) {
                 asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src));
@@ -172,7 +187,7 @@ router_tile_kernel(const float* __restrict__ x, const float* __restrict__ wr,
             for (int m = 0; m < EPG; ++m) wv[m] = w_s[(g + 16 * m) * kWS + 16 * i + j];
 #pragma unroll
             for (int t = 0; t < TT; ++t) {
-                const float xv = x_s[t * kCh + 16 * i + j];
+                const float xv = xval<TF32>(x_s[t * kCh + 16 * i + j]);
 #pragma unroll
                 for (int m = 0; m < EPG; ++m) acc[t][m] = __fmaf_rn(wv[m], xv, acc[t][m]);
             }
@@ -186,36 +201,32 @@ router_tile_kernel(const float* __restrict__ x, const float* __restrict__ wr,
             const float q = neon16_tree(acc[t][m]);
             const int e = g + 16 * m;
             if (j == 0 && t < nt && e < ne)
-                logits[(size_t)(t0 + t) * E + e0 + e] =
-                    neon16_finish(q, wr + (size_t)(e0 + e) * H, x + (size_t)(t0 + t) * H, H16, H,
-                                  bias, e0 + e);
+                a.logits[(size_t)(t0 + t) * a.Ew + e0 + e] = neon16_finish<TF32>(
+                    q, a.w + (size_t)(e0 + e) * H, a.x + (size_t)(t0 + t) * H, H16, H, a.bias,
+                    e0 + e, a.E);
         }
     }
-    finish_tile(tile_counter, blockIdx.x, t0, nt, E, logits, k, min_weight, ids, weights, err);
+    finish_tile(a, blockIdx.x, t0, nt);
 }
 
-// x86 order: one thread per (token, expert), sequential sum += w*x with a
+// x86 order: one thread per (token, row), sequential sum += w*x with a
 // separately rounded product (src/model/cpu.rs:148-151).
-__global__ void router_sequential_kernel(const float* __restrict__ x, const float* __restrict__ wr,
-                                         const float* __restrict__ bias, int T, int H, int E,
-                                         float* logits) {
+__global__ void router_sequential_kernel(const RouterArgs a) {
     const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (long)T * E) return;
-    const int t = (int)(idx / E), e = (int)(idx % E);
-    const float* wrow = wr + (size_t)e * H;
-    const float* xrow = x + (size_t)t * H;
+    if (idx >= (long)a.T * a.Ew) return;
+    const int t = (int)(idx / a.Ew), e = (int)(idx % a.Ew);
+    const float* wrow = a.w + (size_t)e * a.H;
+    const float* xrow = a.x + (size_t)t * a.H;
     float s = 0.0f;
-    for (int h = 0; h < H; ++h) s = __fadd_rn(s, __fmul_rn(wrow[h], xrow[h]));
-    if (bias) s = __fadd_rn(s, bias[e]);
-    logits[idx] = s;
+    for (int h = 0; h < a.H; ++h) s = __fadd_rn(s, __fmul_rn(wrow[h], xrow[h]));
+    if (a.bias && e < a.E) s = __fadd_rn(s, a.bias[e]);
+    a.logits[idx] = s;
 }
 
-__global__ void topk_kernel(const float* __restrict__ logits, int T, int E, int k,
-                            float min_weight, int32_t* ids, float* weights, uint32_t* err) {
+__global__ void route_rows_kernel(const RouterArgs a) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= T) return;
-    topk_row(logits + (size_t)warp * E, E, k, min_weight, ids + (size_t)warp * k,
-             weights + (size_t)warp * k, lane, err);
+    if (warp >= a.T) return;
+    route_row(a, warp, lane);
 }
 
 // One warp selects the top-k of a row of E logits (E <= 1024): k rounds of a
@@ -264,35 +275,128 @@ __device__ void topk_row(const float* row, int E, int k, float min_weight, int32
     }
 }
 
-int launch_router(const RouterArgs& a, cudaStream_t s) {
-    if (a.order == 1) {
-        const long n = (long)a.T * a.E;
-        router_sequential_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
-            a.x, a.w, a.bias, a.T, a.H, a.E, a.logits);
-        topk_kernel<<<(a.T * 32 + 255) / 256, 256, 0, s>>>(a.logits, a.T, a.E, a.k,
-                                                           a.min_weight, a.ids, a.weights, a.err);
-        return 0;
+// Ling's grouped sigmoid routing for one row, one warp (E <= 256: element
+// lane + 32i of the row in sel[i]). Keys are total_cmp keys made unsigned
+// (key ^ 0x80000000), so an unsigned compare is the f32 total order; 0 stands
+// for "no element" in the top-2 merges (every group has >= 2 elements).
+__device__ void grouped_row(const float* row, const RouterArgs& a, int32_t* ids, float* weights,
+                            int lane) {
+    constexpr int kPL = kGroupedMaxExperts / 32;
+    const int E = a.E, k = a.k, width = E / a.groups;
+    uint32_t key[kPL];
+    bool finite = true;
+#pragma unroll
+    for (int i = 0; i < kPL; ++i) {
+        const int e = lane + 32 * i;
+        key[i] = 0u;
+        if (e < E) {
+            const float l = __ldcg(row + e);
+            if (!isfinite(l)) finite = false;
+            // selected = score + bias (moe.rs:165-168)
+            const float sel = __fadd_rn(sigmoid_ref(l), a.sel_bias[e]);
+            key[i] = (uint32_t)total_key(sel) ^ 0x80000000u;
+        }
     }
+    if (__any_sync(0xffffffffu, !finite) && lane == 0) atomicOr(a.err, kErrNonFinite);
+
+    // group score = the sum of the group's two largest selected values
+    // (moe.rs:170-187); lane g keeps group g's
+    uint32_t my_gkey = 0u;
+    for (int g = 0; g < a.groups; ++g) {
+        uint32_t f = 0u, s2 = 0u;
+#pragma unroll
+        for (int i = 0; i < kPL; ++i) {
+            const int e = lane + 32 * i;
+            if (e < E && e / width == g) {
+                const uint32_t v = key[i];
+                if (v > f) { s2 = f; f = v; }
+                else if (v > s2) s2 = v;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const uint32_t of = __shfl_xor_sync(0xffffffffu, f, off);
+            const uint32_t os = __shfl_xor_sync(0xffffffffu, s2, off);
+            s2 = max(min(f, of), max(s2, os));
+            f = max(f, of);
+        }
+        const float gs = __fadd_rn(key_value((int32_t)(f ^ 0x80000000u)),
+                                   key_value((int32_t)(s2 ^ 0x80000000u)));
+        if (lane == g) my_gkey = (uint32_t)total_key(gs) ^ 0x80000000u;
+    }
+    // the top_groups groups of (score desc, index asc) (moe.rs:188-198)
+    int rank = 0;
+    for (int h = 0; h < a.groups; ++h) {
+        const uint32_t hk = __shfl_sync(0xffffffffu, my_gkey, h);
+        if (hk > my_gkey || (hk == my_gkey && h < lane)) ++rank;
+    }
+    const uint32_t enabled = __ballot_sync(0xffffffffu, lane < a.groups && rank < a.top_groups);
+
+    // the first k of (selected desc, id asc) among the enabled groups' experts
+    // (moe.rs:199-210)
+    uint32_t taken = 0;
+    int my_id = 0;
+    for (int r = 0; r < k; ++r) {
+        unsigned long long best = 0ull;
+#pragma unroll
+        for (int i = 0; i < kPL; ++i) {
+            const int e = lane + 32 * i;
+            if (e >= E || ((taken >> i) & 1u) || !((enabled >> (e / width)) & 1u)) continue;
+            const unsigned long long v =
+                ((unsigned long long)key[i] << 32) | (0xFFFFFFFFu - (uint32_t)e);
+            if (v > best) best = v;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+            if (o > best) best = o;
+        }
+        const int win = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+        if ((win & 31) == lane) taken |= 1u << (win >> 5);
+        if (lane == r) my_id = win;
+    }
+    // weights from the unbiased sigmoid, summed in chosen order (moe.rs:211-221)
+    const float score = lane < k ? sigmoid_ref(__ldcg(row + my_id)) : 0.0f;
+    float sum = -0.0f;
+    for (int r = 0; r < k; ++r) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, score, r));
+    sum = __fadd_rn(sum, 1e-20f);
+    if (lane < k) {
+        const float w = k > 1 ? __fdiv_rn(score, sum) : score;
+        ids[lane] = my_id;
+        weights[lane] = __fmul_rn(w, a.scale);
+    }
+}
+
+template <bool TF32>
+static int launch_router_t(const RouterArgs& a, cudaStream_t s) {
     if (a.T < 16) {
         const size_t smem = sizeof(float) * ((size_t)kDecEB * (a.H + 16) + a.H);
         if (smem > 200 * 1024) return -1;
-        cudaFuncSetAttribute(router_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(router_decode_kernel<TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem);
-        dim3 grid(a.T, (a.E + kDecEB - 1) / kDecEB);
-        router_decode_kernel<<<grid, 128, smem, s>>>(a.x, a.w, a.bias, a.T, a.H, a.E, a.logits,
-                                                     a.counters, a.k, a.min_weight, a.ids,
-                                                     a.weights, a.err);
+        dim3 grid(a.T, (a.Ew + kDecEB - 1) / kDecEB);
+        router_decode_kernel<TF32><<<grid, 128, smem, s>>>(a);
         return 0;
     }
     constexpr int TT = 16, EB = 32;
     const size_t smem = sizeof(float) * 4 * (EB * (128 + 16) + TT * 128);
-    cudaFuncSetAttribute(router_tile_kernel<TT, EB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    dim3 grid((a.T + TT - 1) / TT, (a.E + EB - 1) / EB);
-    router_tile_kernel<TT, EB><<<grid, kRouterThreads, smem, s>>>(
-        a.x, a.w, a.bias, a.T, a.H, a.E, a.logits, a.counters, a.k, a.min_weight, a.ids,
-        a.weights, a.err);
+    cudaFuncSetAttribute(router_tile_kernel<TT, EB, TF32>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dim3 grid((a.T + TT - 1) / TT, (a.Ew + EB - 1) / EB);
+    router_tile_kernel<TT, EB, TF32><<<grid, kRouterThreads, smem, s>>>(a);
     return 0;
+}
+
+int launch_router(const RouterArgs& args, cudaStream_t s) {
+    RouterArgs a = args;
+    if (a.Ew <= 0) a.Ew = a.E;
+    if (a.order == kOrderSequential) {
+        const long n = (long)a.T * a.Ew;
+        router_sequential_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(a);
+        route_rows_kernel<<<(a.T * 32 + 255) / 256, 256, 0, s>>>(a);
+        return 0;
+    }
+    return a.order == kOrderTf32 ? launch_router_t<true>(a, s) : launch_router_t<false>(a, s);
 }
 
 }  // namespace moe

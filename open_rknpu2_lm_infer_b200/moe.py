@@ -205,21 +205,60 @@ class Backend:
         return cfg
 
     def router(self, weight: np.ndarray, top: int, bias: np.ndarray | None = None,
-               order: int = L.ROUTER_NEON16, min_weight: float = 0.0) -> "Router":
-        """Router over weight [experts][hidden] f32 (src/model/qwen35/moe.rs:215-241)."""
+               order: int = L.ROUTER_NEON16, min_weight: float = 0.0, *,
+               rule: int = L.ROUTE_SOFTMAX, groups: int = 1, top_groups: int = 1,
+               routing_scale: float = 1.0, expert_bias: np.ndarray | None = None,
+               shared_gate: np.ndarray | None = None) -> "Router":
+        """Router over weight [experts][hidden] f32: Qwen's softmax top-k
+        (src/model/qwen35/moe.rs:215-241), or with rule=ROUTE_GROUPED_SIGMOID
+        Ling's grouped sigmoid routing (src/model/ling3tiny/moe.rs:146-223).
+        shared_gate [hidden] gates the shared expert by sigmoid(gate . x)
+        (src/model/qwen35/moe.rs:334-347)."""
         weight = np.ascontiguousarray(weight, dtype=np.float32)
         e, h = weight.shape
         if not (np.isfinite(min_weight) and 0.0 <= min_weight <= 1.0):
             raise ValueError("expert minimum weight must be finite and between 0 and 1")
         if not (0 < top <= e):
             raise ValueError("invalid router top-k")
+        if rule == L.ROUTE_GROUPED_SIGMOID:
+            if not (groups > 0 and e % groups == 0 and e // groups >= 2 and
+                    0 < top_groups <= groups and top <= top_groups * (e // groups) and
+                    routing_scale > 0):
+                raise ValueError("invalid Ling layer/router dimensions")
+            if expert_bias is None:
+                raise ValueError("grouped sigmoid routing needs the expert bias")
         cfg = self._config(h, 32, e, False, top, 0)
-        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
-        raw = self.lib.moe_b200_router_create(C.byref(cfg), _ptr(weight), _ptr(b), order,
-                                              C.c_float(min_weight))
+        keep = []
+
+        def arr(a, n):
+            if a is None:
+                return None
+            a = np.ascontiguousarray(a, dtype=np.float32)
+            if a.size != n:
+                raise ValueError("router vector has the wrong length")
+            keep.append(a)
+            return _ptr(a)
+
+        opt = L.RouterOptions()
+        self.lib.moe_b200_router_options_init(C.byref(opt))
+        opt.order, opt.rule, opt.min_weight = order, rule, min_weight
+        opt.bias = arr(bias, e)
+        opt.groups, opt.top_groups, opt.routing_scale = groups, top_groups, routing_scale
+        opt.expert_bias = arr(expert_bias, e)
+        opt.shared_gate = arr(shared_gate, h)
+        raw = self.lib.moe_b200_router_create_ex(C.byref(cfg), _ptr(weight), C.byref(opt))
         if not raw:
             raise MoeError("cannot create router", L.ERR_INVALID)
-        return Router(_Handle(raw, self.lib.moe_b200_router_free), h, e, top)
+        return Router(_Handle(raw, self.lib.moe_b200_router_free), h, e, top,
+                      shared_gate is not None)
+
+    def router_for(self, layer, **kw) -> "Router":
+        """The router a synthetic.Layer specifies (rule, order, biases, gate)."""
+        spec = layer.spec
+        return self.router(layer.router, spec.top, layer.bias, spec.router_order,
+                           spec.min_weight, rule=spec.route_rule, groups=spec.groups,
+                           top_groups=spec.top_groups, routing_scale=spec.routing_scale,
+                           expert_bias=layer.expert_bias, shared_gate=layer.shared_gate, **kw)
 
     def close(self):
         for w in self._work.values():
@@ -233,6 +272,11 @@ class Router:
     hidden: int
     experts: int
     top: int
+    gated: bool = False   # logits carry the shared-gate column (experts + 1 wide)
+
+    @property
+    def logit_columns(self) -> int:
+        return self.experts + (1 if self.gated else 0)
 
     @property
     def raw(self):

@@ -11,6 +11,11 @@ Configurations (shapes only; token counts are parameters):
   c3  H=2048 E=256 k=8 I=512  W4 group-32 + shared W8 per-channel I_s=2048,
       router logits + seeded Zipf(s=1.1) per-expert bias (T=498/2110)
   c5  the c3 layer with routed W4 group-32 ("c5_w4") or W8 per-channel ("c5_w8")
+  ling  H=1536 E=128 k=8 I=512 W4 per-channel + joint shared W8 I_s=512, TF32
+        router, grouped sigmoid routing (8 groups, top 4, scale 2.5) with a
+        seeded N(0, 0.1) expert bias (the Ling 2.5 mini shapes)
+  q35g  the c3 layer with a dense shared expert I_s=512 behind a sigmoid gate
+        (the Qwen3.5 MoE shared-expert arrangement)
 """
 from __future__ import annotations
 
@@ -21,7 +26,8 @@ import numpy as np
 
 from .moe import QuantMatrix
 
-ROUTER_NEON16 = 0
+ROUTER_NEON16, ROUTER_TF32 = 0, 2
+ROUTE_SOFTMAX, ROUTE_GROUPED_SIGMOID = 0, 1
 
 
 @dataclass(frozen=True)
@@ -38,6 +44,12 @@ class LayerSpec:
     zipf_scale: float = 2.0        # bias of the rank-1 expert, in logit units
     router_order: int = ROUTER_NEON16
     min_weight: float = 0.0
+    route_rule: int = ROUTE_SOFTMAX
+    groups: int = 1
+    top_groups: int = 1
+    routing_scale: float = 1.0
+    expert_bias_std: float = 0.0   # grouped sigmoid: selection bias ~ N(0, std)
+    shared_gate: bool = False      # sigmoid-gated shared expert
 
 
 CONFIGS: dict[str, LayerSpec] = {
@@ -46,14 +58,21 @@ CONFIGS: dict[str, LayerSpec] = {
     "c3": LayerSpec("c3", 2048, 512, 256, 8, shared_inter=2048, zipf_s=1.1),
     "c5_w4": LayerSpec("c5_w4", 2048, 512, 256, 8, shared_inter=2048, zipf_s=1.1),
     "c5_w8": LayerSpec("c5_w8", 2048, 512, 256, 8, routed="w8pc", shared_inter=2048, zipf_s=1.1),
+    "ling": LayerSpec("ling", 1536, 512, 128, 8, routed="w4pc", shared_inter=512,
+                      router_order=ROUTER_TF32, route_rule=ROUTE_GROUPED_SIGMOID, groups=8,
+                      top_groups=4, routing_scale=2.5, expert_bias_std=0.1),
+    "q35g": LayerSpec("q35g", 2048, 512, 256, 8, shared_inter=512, zipf_s=1.1,
+                      shared_gate=True),
 }
 
 TOKENS = {"c1": (32,), "c2": (1, 512, 4096), "c3": (498, 2110),
-          "c5_w4": (1, 8, 32, 128, 256), "c5_w8": (1, 8, 32, 128, 256)}
+          "c5_w4": (1, 8, 32, 128, 256), "c5_w8": (1, 8, 32, 128, 256), "ling": (1, 512),
+          "q35g": (1, 512)}
 
 # tensor ids of the per-tensor streams
 _ROUTER, _BIAS, _PERM, _X, _RES, _NORM = 1, 2, 3, 4, 5, 6
 _GATE, _DOWN, _SGATE, _SDOWN = 100, 200, 300, 400
+_EBIAS, _SHGATE = 7, 8
 
 
 def rng(seed: int, tensor: int, index: int = 0) -> np.random.Generator:
@@ -97,6 +116,8 @@ class Layer:
     gate: list[QuantMatrix]       # [E] k=H, n=2I (gate columns first)
     down: list[QuantMatrix]       # [E] k=I, n=H
     shared: tuple[QuantMatrix, QuantMatrix] | None
+    expert_bias: np.ndarray | None = None   # [E] f32 selection bias (grouped sigmoid)
+    shared_gate: np.ndarray | None = None   # [H] f32 shared-expert gate row
 
 
 def _expert(spec: LayerSpec, seed: int, e: int) -> tuple[QuantMatrix, QuantMatrix]:
@@ -124,7 +145,15 @@ def make_layer(spec: LayerSpec | str, seed: int = 0, threads: int = 8) -> Layer:
         wg = rng(seed, _SGATE).standard_normal((H, 2 * Is), dtype=np.float32) * np.float32(0.02)
         wd = rng(seed, _SDOWN).standard_normal((Is, H), dtype=np.float32) * np.float32(0.02)
         shared = (quantize_pc(wg, spec.shared_bits), quantize_pc(wd, spec.shared_bits))
-    return Layer(spec, router, bias, [p[0] for p in pairs], [p[1] for p in pairs], shared)
+    expert_bias = None
+    if spec.route_rule == ROUTE_GROUPED_SIGMOID:
+        expert_bias = (rng(seed, _EBIAS).standard_normal(E, dtype=np.float32)
+                       * np.float32(spec.expert_bias_std))
+    shared_gate = None
+    if spec.shared_gate:
+        shared_gate = rng(seed, _SHGATE).standard_normal(H, dtype=np.float32) * np.float32(0.02)
+    return Layer(spec, router, bias, [p[0] for p in pairs], [p[1] for p in pairs], shared,
+                 expert_bias, shared_gate)
 
 
 def make_input(spec: LayerSpec | str, tokens: int, seed: int = 0, stream: int = _X) -> np.ndarray:

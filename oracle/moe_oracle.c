@@ -87,11 +87,29 @@ static float router_dot(const float *w, const float *x, int H, int order) {
         }
         sum = (v[0] + v[1]) + (v[2] + v[3]);
     }
+    if (order == ORACLE_ROUTER_TF32) {
+        /* Tf32Linear (src/npu/tf32.rs:142-170): both operands narrowed to TF32
+         * by dropping the low 13 mantissa bits; the reference's own check
+         * (src/npu/tf32.rs:212-224) is the f64 sum of those products within
+         * 5e-5, which is what this computes (rounded once to f32). */
+        double acc = 0.0;
+        for (; i < H; ++i)
+            acc += (double)u2f(f2u(w[i]) & ~0x1fffu) * (double)u2f(f2u(x[i]) & ~0x1fffu);
+        return (float)acc;
+    }
     for (; i < H; ++i) {
         float p = w[i] * x[i];
         sum = sum + p;
     }
     return sum;
+}
+
+/* sigmoid (src/ops/activation.rs:7-14): the two branches keep exp's argument
+ * non-positive. */
+float oracle_sigmoid(float x) {
+    if (x >= 0.0f) return 1.0f / (1.0f + expf(-x));
+    float e = expf(x);
+    return e / (1.0f + e);
 }
 
 /* Cpu::dense_head_batch (src/model/cpu.rs:302-316): every output keeps the
@@ -140,6 +158,88 @@ int oracle_routes(const float *logits, int T, int E, int k, float min_weight,
                 if (w[r] < min_weight) w[r] = 0.0f;
     }
     return 0;
+}
+
+/* Ling's grouped sigmoid routing, RoutingScratch::routes
+ * (src/model/ling3tiny/moe.rs:146-223): score = sigmoid(logit), selected =
+ * score + bias; a group's score is the sum of its two largest selected values
+ * (total_cmp); the top_groups groups by (score desc, index asc) are enabled;
+ * the k largest selected values among their experts, (selected desc, id asc),
+ * in that order, are chosen; weight = score / (sum of chosen scores in chosen
+ * order + 1e-20) for k > 1, else score, times routing_scale. Returns 0, or -1
+ * for a geometry the reference's config check rejects
+ * (src/model/ling3tiny/config.rs:113-124). */
+int oracle_ling_routes(const float *logits, const float *bias, int T, int E, int groups,
+                       int top_groups, int k, float routing_scale, int32_t *ids,
+                       float *weights) {
+    if (groups <= 0 || E % groups != 0 || E / groups < 2 || top_groups <= 0 ||
+        top_groups > groups || k <= 0 || k > top_groups * (E / groups) || !(routing_scale > 0.0f))
+        return -1;
+    const int width = E / groups;
+    int bad = 0;
+#pragma omp parallel for schedule(static) reduction(| : bad)
+    for (int t = 0; t < T; ++t) {
+        const float *l = logits + (long)t * E;
+        int32_t *id = ids + (long)t * k;
+        float *w = weights + (long)t * k;
+        float *score = (float *)malloc(sizeof(float) * (size_t)E);
+        float *sel = (float *)malloc(sizeof(float) * (size_t)E);
+        float *gscore = (float *)malloc(sizeof(float) * (size_t)groups);
+        char *enabled = (char *)calloc((size_t)groups, 1);
+        if (!score || !sel || !gscore || !enabled) { bad = 1; }
+        else {
+            for (int e = 0; e < E; ++e) {
+                score[e] = oracle_sigmoid(l[e]);
+                sel[e] = score[e] + bias[e];
+            }
+            for (int g = 0; g < groups; ++g) {
+                const float *v = sel + (long)g * width;
+                float first = v[0], second = v[1];
+                if (oracle_total_key(second) > oracle_total_key(first)) {
+                    float tmp = first; first = second; second = tmp;
+                }
+                for (int j = 2; j < width; ++j) {
+                    if (oracle_total_key(v[j]) > oracle_total_key(first)) {
+                        second = first;
+                        first = v[j];
+                    } else if (oracle_total_key(v[j]) > oracle_total_key(second)) {
+                        second = v[j];
+                    }
+                }
+                gscore[g] = first + second;
+            }
+            /* the top_groups groups of the order (score desc, index asc) */
+            for (int r = 0; r < top_groups; ++r) {
+                int best = -1;
+                for (int g = 0; g < groups; ++g) {
+                    if (enabled[g]) continue;
+                    if (best < 0 || oracle_total_key(gscore[g]) > oracle_total_key(gscore[best]))
+                        best = g;
+                }
+                enabled[best] = 1;
+            }
+            /* the first k of the order (selected desc, id asc) among enabled experts */
+            for (int r = 0; r < k; ++r) {
+                int best = -1;
+                for (int e = 0; e < E; ++e) {
+                    if (!enabled[e / width]) continue;
+                    int taken = 0;
+                    for (int q = 0; q < r; ++q) taken |= (id[q] == e);
+                    if (taken) continue;
+                    if (best < 0 || oracle_total_key(sel[e]) > oracle_total_key(sel[best]))
+                        best = e;
+                }
+                id[r] = best;
+            }
+            float sum = -0.0f;
+            for (int r = 0; r < k; ++r) sum = sum + score[id[r]];
+            sum = sum + 1e-20f;
+            for (int r = 0; r < k; ++r)
+                w[r] = (k > 1 ? score[id[r]] / sum : score[id[r]]) * routing_scale;
+        }
+        free(score); free(sel); free(gscore); free(enabled);
+    }
+    return bad ? -1 : 0;
 }
 
 /* Grouping of assignments a = t*k + r by expert, ascending a inside a group;
@@ -456,7 +556,24 @@ int oracle_moe_run(const oracle_layer *L, int T, const float *x, const int32_t *
             expert_ffn(qs + (long)r0 * H, ss + r0, nr, L->shared_gate_up, L->shared_down, rule,
                        smid + (long)r0 * Is, sqm + (long)r0 * Is, ssm + r0, sh + (long)r0 * H);
         }
-        for (long i = 0; i < (long)T * H; ++i) out[i] = out[i] + sh[i];
+        if (L->shared_gate) {
+            /* the gate merge of src/model/qwen35/moe.rs:334-347: gate = dense_head
+             * of the [1][hidden] gate row (the router's dot order), scale =
+             * 1 / (1 + exp(-gate)), projected += scale * attended */
+#pragma omp parallel for schedule(static)
+            for (int t = 0; t < T; ++t) {
+                float g = router_dot(L->shared_gate, x + (long)t * H, H, L->router_order);
+                float scale = 1.0f / (1.0f + expf(-g));
+                if (dump && dump->shared_scale) dump->shared_scale[t] = scale;
+                for (int c = 0; c < H; ++c) {
+                    long i = (long)t * H + c;
+                    float p = scale * sh[i];
+                    out[i] = out[i] + p;
+                }
+            }
+        } else {
+            for (long i = 0; i < (long)T * H; ++i) out[i] = out[i] + sh[i];
+        }
         if (dump && dump->shared) memcpy(dump->shared, sh, sizeof(float) * (size_t)T * H);
         if (qs != qx) { free(qs); free(ss); }
         free(smid); free(sqm); free(ssm); free(sh);
@@ -480,7 +597,9 @@ int oracle_moe_run(const oracle_layer *L, int T, const float *x, const int32_t *
 
 /* Routed::forward + the decoder residual (src/model/qwen35/moe.rs:188-226,
  * src/model/qwen35/decoder.rs:215-217): router -> routes -> run ->
- * out = residual + projected (residual may be NULL). */
+ * out = residual + projected (residual may be NULL). With the grouped sigmoid
+ * rule the routes are Ling's (FeedForward::run, src/model/ling3tiny/
+ * moe.rs:354-394: router projection, routes per row, bank run, + shared). */
 int oracle_moe_forward(const oracle_layer *L, int T, const float *x, const float *residual,
                        float *out, oracle_dump *dump) {
     const int E = L->experts, k = L->top, H = L->hidden;
@@ -488,7 +607,10 @@ int oracle_moe_forward(const oracle_layer *L, int T, const float *x, const float
     int32_t *ids = (int32_t *)malloc(sizeof(int32_t) * (size_t)T * k + 4);
     float *w = (float *)malloc(sizeof(float) * (size_t)T * k + 4);
     oracle_router_logits(x, L->router, L->router_bias, T, H, E, L->router_order, logits);
-    int rc = oracle_routes(logits, T, E, k, L->min_weight, ids, w);
+    int rc = L->route_rule == ORACLE_ROUTE_GROUPED_SIGMOID
+                 ? oracle_ling_routes(logits, L->expert_bias, T, E, L->groups, L->top_groups, k,
+                                      L->routing_scale, ids, w)
+                 : oracle_routes(logits, T, E, k, L->min_weight, ids, w);
     if (rc == 0) rc = oracle_moe_run(L, T, x, ids, w, out, dump);
     if (rc == 0 && residual)
         for (long i = 0; i < (long)T * H; ++i) out[i] = residual[i] + out[i];

@@ -22,8 +22,12 @@
 extern "C" {
 #endif
 
-/* Router accumulation orders of src/model/cpu.rs:96-153 (dense_dot). */
-enum { ORACLE_ROUTER_NEON16 = 0, ORACLE_ROUTER_SEQUENTIAL = 1 };
+/* Router accumulation orders: dense_dot of src/model/cpu.rs:96-153 (NEON16,
+ * SEQUENTIAL), and the TF32 NPU linear of src/npu/tf32.rs (TF32). */
+enum { ORACLE_ROUTER_NEON16 = 0, ORACLE_ROUTER_SEQUENTIAL = 1, ORACLE_ROUTER_TF32 = 2 };
+/* Routing rules: softmax top-k (src/model/qwen35/moe.rs:51-67) and Ling's
+ * grouped sigmoid top-k (src/model/ling3tiny/moe.rs:146-223). */
+enum { ORACLE_ROUTE_SOFTMAX = 0, ORACLE_ROUTE_GROUPED_SIGMOID = 1 };
 /* Activation quantisation rules. */
 enum { ORACLE_QUANT_MOE = 0, ORACLE_QUANT_DENSE = 1 };
 /* Shared expert modes. */
@@ -53,6 +57,14 @@ typedef struct {
     const oracle_qmat *down;     /* [experts]: k=inter,  n=hidden */
     const oracle_qmat *shared_gate_up; /* k=hidden, n=2*shared_inter */
     const oracle_qmat *shared_down;    /* k=shared_inter, n=hidden */
+    /* grouped sigmoid routing (route_rule = ORACLE_ROUTE_GROUPED_SIGMOID) */
+    int route_rule;
+    int groups, top_groups;
+    float routing_scale;
+    const float *expert_bias; /* [experts] selection bias */
+    /* shared-expert gate [hidden] f32 (src/model/qwen35/moe.rs:334-347), or
+     * NULL: the shared output is added as sigmoid(gate . x) * shared */
+    const float *shared_gate;
 } oracle_layer;
 
 /* Optional stage dumps; any pointer may be NULL. Sizes for T tokens, A = number
@@ -72,6 +84,7 @@ typedef struct {
     float *routed;     /* [T][H] weighted combine of routed experts */
     float *shared;     /* [T][H] shared expert output */
     int32_t n_assign;  /* out: A */
+    float *shared_scale; /* [T] sigmoid of the shared gate (when the layer has one) */
 } oracle_dump;
 
 /* Total-order key of Rust's f32::total_cmp, as a signed integer. */
@@ -81,6 +94,10 @@ void oracle_router_logits(const float *x, const float *router, const float *bias
                           int H, int E, int order, float *logits);
 int oracle_routes(const float *logits, int T, int E, int k, float min_weight,
                   int32_t *ids, float *weights);
+int oracle_ling_routes(const float *logits, const float *bias, int T, int E, int groups,
+                       int top_groups, int k, float routing_scale, int32_t *ids,
+                       float *weights);
+float oracle_sigmoid(float x);
 int oracle_permute(const int32_t *ids, const float *weights, int T, int k, int E,
                    int32_t *perm, int32_t *offsets);
 void oracle_quantize(const float *x, int rows, int cols, int rule, int8_t *q, float *s);

@@ -15,7 +15,8 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libmoe_oracle.so"
 
-ROUTER_NEON16, ROUTER_SEQUENTIAL = 0, 1
+ROUTER_NEON16, ROUTER_SEQUENTIAL, ROUTER_TF32 = 0, 1, 2
+ROUTE_SOFTMAX, ROUTE_GROUPED_SIGMOID = 0, 1
 QUANT_MOE, QUANT_DENSE = 0, 1
 SHARED_JOINT, SHARED_DENSE = 0, 1
 
@@ -30,13 +31,16 @@ class LayerS(C.Structure):
                 ("shared_inter", C.c_int), ("shared_mode", C.c_int), ("router_order", C.c_int),
                 ("min_weight", C.c_float), ("router", C.c_void_p), ("router_bias", C.c_void_p),
                 ("gate_up", C.POINTER(QMat)), ("down", C.POINTER(QMat)),
-                ("shared_gate_up", C.POINTER(QMat)), ("shared_down", C.POINTER(QMat))]
+                ("shared_gate_up", C.POINTER(QMat)), ("shared_down", C.POINTER(QMat)),
+                ("route_rule", C.c_int), ("groups", C.c_int), ("top_groups", C.c_int),
+                ("routing_scale", C.c_float), ("expert_bias", C.c_void_p),
+                ("shared_gate", C.c_void_p)]
 
 
 class Dump(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in (
         "logits", "ids", "weights", "perm", "offsets", "qx", "sx", "middle", "qm", "sm", "y",
-        "routed", "shared")] + [("n_assign", C.c_int32)]
+        "routed", "shared")] + [("n_assign", C.c_int32), ("shared_scale", C.c_void_p)]
 
 
 _lib = None
@@ -60,6 +64,11 @@ def lib() -> C.CDLL:
         L.oracle_router_logits.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, P]
         L.oracle_routes.restype = C.c_int
         L.oracle_routes.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_float, P, P]
+        L.oracle_ling_routes.restype = C.c_int
+        L.oracle_ling_routes.argtypes = [P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                         C.c_float, P, P]
+        L.oracle_sigmoid.restype = C.c_float
+        L.oracle_sigmoid.argtypes = [C.c_float]
         L.oracle_permute.restype = C.c_int
         L.oracle_permute.argtypes = [P, P, C.c_int, C.c_int, C.c_int, P, P]
         L.oracle_quantize.argtypes = [P, C.c_int, C.c_int, C.c_int, P, P]
@@ -111,6 +120,24 @@ def routes(logits, k, min_weight=0.0):
     if rc != 0:
         raise ValueError("invalid router top-k")
     return ids, w
+
+
+def ling_routes(logits, bias, groups, top_groups, k, routing_scale):
+    """Ling's grouped sigmoid routing (src/model/ling3tiny/moe.rs:146-223)."""
+    logits = _c(np.atleast_2d(logits), np.float32)
+    bias = _c(bias, np.float32)
+    T, E = logits.shape
+    ids = np.empty((T, max(k, 1)), np.int32)
+    w = np.empty((T, max(k, 1)), np.float32)
+    rc = lib().oracle_ling_routes(_p(logits), _p(bias), T, E, groups, top_groups, k,
+                                  routing_scale, _p(ids), _p(w))
+    if rc != 0:
+        raise ValueError("invalid grouped routing geometry")
+    return ids, w
+
+
+def sigmoid(x: float) -> float:
+    return lib().oracle_sigmoid(x)
 
 
 def permute(ids, weights, E):
@@ -210,6 +237,14 @@ class OracleLayer:
             s.shared_mode = shared_mode
             s.shared_gate_up = C.pointer(self.sg.s)
             s.shared_down = C.pointer(self.sd.s)
+        s.route_rule = getattr(spec, "route_rule", ROUTE_SOFTMAX)
+        s.groups = getattr(spec, "groups", 1)
+        s.top_groups = getattr(spec, "top_groups", 1)
+        s.routing_scale = getattr(spec, "routing_scale", 1.0)
+        eb, sgate = getattr(layer, "expert_bias", None), getattr(layer, "shared_gate", None)
+        self.expert_bias = None if eb is None else _c(eb, np.float32)
+        self.shared_gate = None if sgate is None else _c(sgate, np.float32)
+        s.expert_bias, s.shared_gate = _p(self.expert_bias), _p(self.shared_gate)
 
     def _dump(self, T, A, want):
         if not want:
@@ -221,7 +256,7 @@ class OracleLayer:
                     sx=np.empty(T, np.float32), middle=np.empty((A, I), np.float32),
                     qm=np.empty((A, I), np.int8), sm=np.empty(A, np.float32),
                     y=np.empty((A, H), np.float32), routed=np.empty((T, H), np.float32),
-                    shared=np.empty((T, H), np.float32))
+                    shared=np.empty((T, H), np.float32), shared_scale=np.empty(T, np.float32))
         d = Dump(**{n: _p(a) for n, a in bufs.items()})
         return d, bufs
 

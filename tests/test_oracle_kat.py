@@ -35,6 +35,63 @@ def test_routes_ties_prefer_lower_id_and_total_order():
     assert O.total_key(0.0) > O.total_key(-0.0) > O.total_key(-1e-30)
 
 
+# ---- Ling grouped routing: src/model/ling3tiny/moe.rs:404-493 ----------------
+def test_ling_selection_matches_sorted_oracle_with_ties():
+    from kat_vectors import (LING_GEOMETRIES, LING_SCALE, LING_STEPS, ling_sorted_oracle,
+                             ling_step)
+    for experts, groups, top_groups, top in LING_GEOMETRIES:
+        for step in range(LING_STEPS):
+            logits, bias = ling_step(experts, step)
+            ref_ids, ref_w = ling_sorted_oracle(logits, bias, groups, top_groups, top,
+                                                LING_SCALE, O.sigmoid)
+            ids, w = O.ling_routes(logits, bias, groups, top_groups, top, LING_SCALE)
+            assert ids[0].tolist() == ref_ids.tolist(), (experts, step)
+            assert np.array_equal(w[0], ref_w), (experts, step)  # assert_eq! on f32
+
+
+def test_ling_group_bias_selects_but_weights_use_original_sigmoid():
+    from kat_vectors import LING_BIAS_CASE as K, LING_SCALE
+    experts, groups, top_groups, top = K["geometry"]
+    ids, w = O.ling_routes(K["logits"], K["bias"], groups, top_groups, top, LING_SCALE)
+    assert ids[0].tolist() == K["ids"]
+    total = sum(O.sigmoid(v) for v in K["weight_logits"])
+    for got, v in zip(w[0], K["weight_logits"]):
+        assert abs(got - O.sigmoid(v) / total * 2.5) < 1e-6
+    assert abs(float(w[0].sum()) - 2.5) < 1e-6
+
+
+def test_ling_geometry_is_validated():
+    z = np.zeros((1, 8), np.float32)
+    for g, tg, k in [(3, 1, 1), (8, 1, 1), (4, 5, 1), (4, 2, 5), (4, 2, 0)]:
+        with pytest.raises(ValueError):
+            O.ling_routes(z, np.zeros(8, np.float32), g, tg, k, 2.5)
+
+
+def test_sigmoid_branches():
+    # x >= 0: 1 / (1 + exp(-x)); x < 0: e / (1 + e) with e = exp(x)
+    for x in (0.0, 0.5, 3.5, 20.0, 100.0):
+        assert O.sigmoid(x) == np.float32(1.0) / (np.float32(1.0) + np.exp(np.float32(-x)))
+    assert O.sigmoid(-100.0) > 0.0 and O.sigmoid(-1000.0) == 0.0
+    assert O.sigmoid(0.0) == 0.5
+
+
+def test_tf32_router_is_the_truncated_f64_dot():
+    # src/npu/tf32.rs:190-224: both operands lose their low 13 mantissa bits
+    k, n, rows = 1536, 128, 3
+    i = np.arange(k * n)
+    w = ((i * 13 % 71).astype(np.float32) - 35.0) * np.float32(0.001)
+    w = (w.view(np.uint32) + 0x7FFF + ((w.view(np.uint32) >> 16) & 1)).astype(np.uint32)
+    w = (w & 0xFFFF0000).view(np.float32).reshape(n, k)  # bf16-rounded weights, [N][K]
+    x = (((np.arange(rows * k) * 7 % 83).astype(np.float32) - 41.0) * np.float32(0.01317))
+    x = x.reshape(rows, k)
+    got = O.router_logits(x, w, order=O.ROUTER_TF32)
+    tr = lambda a: (a.view(np.uint32) & ~np.uint32(0x1FFF)).view(np.float32).astype(np.float64)
+    expected = tr(x) @ tr(w).T
+    assert np.abs(got.astype(np.float64) - expected).max() < 5e-5
+    assert (got.view(np.uint32) & 0x1FFF).any()  # FP32 output, not narrowed
+    assert not O.router_logits(x, np.zeros_like(w), order=O.ROUTER_TF32).any()
+
+
 # ---- pruning::apply: src/model/experts/pruning.rs:64-84 --------------------
 def test_threshold_keeps_boundary_and_best_without_renormalizing():
     # logits whose softmax weights are ~[0.5, 0.25, 0.125, 0.125]
@@ -168,3 +225,37 @@ def test_half_conversion_round_trips():
         h = O.lib().oracle_float_to_half(v)
         assert h == int(np.array(v, np.float16).view(np.uint16))
         assert O.lib().oracle_half_to_float(h) == float(np.float16(v))
+
+
+# ---- shared-expert gate merge: src/model/qwen35/moe.rs:334-347 --------------
+def test_shared_gate_merge_is_projected_plus_scaled_shared():
+    from open_rknpu2_lm_infer_b200 import synthetic as S
+    spec = S.small_spec("q35g", hidden=256, inter=64, experts=8, top=2, shared_inter=64)
+    layer = S.make_layer(spec, seed=9)
+    x = S.make_input(spec, 6, seed=1)
+    res = S.make_input(spec, 6, seed=2, stream=5)
+    ol = O.OracleLayer(layer, shared_mode=O.SHARED_DENSE)
+    out, d = ol.forward(x, res, dump=True)
+    g = O.router_logits(x, layer.shared_gate[None, :])[:, 0]
+    one = np.float32(1.0)
+    # the reference's scale: 1 / (1 + exp(-gate)) in f32 (glibc expf via the oracle)
+    scale = np.array([one / (one + np.float32(np.exp(np.float64(-v)))) for v in g], np.float32)
+    assert np.allclose(d["shared_scale"], scale, rtol=1e-6, atol=0)
+    merged = (d["routed"] + (d["shared_scale"][:, None] * d["shared"]).astype(np.float32))
+    assert np.array_equal(out, (res + merged.astype(np.float32)).astype(np.float32))
+
+
+def test_ling_layer_routes_through_grouped_rule():
+    from open_rknpu2_lm_infer_b200 import synthetic as S
+    spec = S.small_spec("ling", hidden=256, inter=64, experts=16, top=4, groups=4, top_groups=2,
+                        shared_inter=64)
+    layer = S.make_layer(spec, seed=3)
+    x = S.make_input(spec, 5, seed=4)
+    out, d = O.OracleLayer(layer).forward(x, None, dump=True)
+    logits = O.router_logits(x, layer.router, None, O.ROUTER_TF32)
+    assert np.array_equal(d["logits"], logits)
+    ids, w = O.ling_routes(logits, layer.expert_bias, 4, 2, 4, 2.5)
+    assert np.array_equal(d["ids"], ids) and np.array_equal(d["weights"], w)
+    assert np.allclose(w.sum(axis=1), 2.5, rtol=1e-6)
+    # the chosen experts lie in at most top_groups groups
+    assert all(len(set((row // 4).tolist())) <= 2 for row in ids)
