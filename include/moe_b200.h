@@ -141,6 +141,34 @@ void moe_b200_weights_free(moe_b200_weights *w);
 /* Replaces rk_npu_moe_w8_weights_device_bytes. */
 uint64_t moe_b200_weights_device_bytes(const moe_b200_weights *w);
 
+/* ---- expert slot bank (replaces rk_npu_moe_quant_slots_create,
+ * _expert_blob_bytes, _export_expert, _import_expert and _swap_slots, used by
+ * Moe::import_bank / promote / export / import at src/npu/moe.rs:243-320).
+ * A blob is one routed expert's packed device image: a 64-byte header (magic
+ * "MB2XBLOB", MOE_B200_BLOB_VERSION, format, hidden, intermediate, four
+ * region sizes) followed by the bank's own gate|up and down regions, so
+ * export and import are plain copies. Blobs are specific to this library's
+ * packing and to the bank's format and geometry; a mismatch is
+ * MOE_B200_ERR_INVALID. ------------------------------------------------- */
+#define MOE_B200_BLOB_VERSION 1
+uint32_t moe_b200_blob_version(void);
+/* An empty routed bank of cfg->weights.routed_experts slots in routed_format
+ * (MOE_B200_W4_*, MOE_B200_W8_*); zero weights; no shared expert. */
+moe_b200_weights *moe_b200_slots_create(const moe_b200_config *cfg, int32_t routed_format);
+uint64_t moe_b200_expert_blob_bytes(const moe_b200_weights *w);
+/* Synchronous device -> host copy of expert `expert`; bytes must equal the blob size. */
+int moe_b200_export_expert(const moe_b200_weights *w, int32_t expert, void *data, uint64_t bytes);
+/* Synchronous host -> device copy into slot `slot`. */
+int moe_b200_import_expert(moe_b200_weights *w, int32_t slot, const void *data, uint64_t bytes);
+/* The same, stream-ordered (page-locked data overlaps with other streams; the
+ * host buffer must stay valid until the copy completes). */
+int moe_b200_import_expert_async(moe_b200_weights *w, int32_t slot, const void *data,
+                                 uint64_t bytes, void *stream);
+/* Exchanges bank slot `slot` with staging slot `staged` on the device
+ * (stream-ordered). Both banks: same device, format and geometry. */
+int moe_b200_swap_slots(moe_b200_weights *bank, int32_t slot, moe_b200_weights *staging,
+                        int32_t staged, void *stream);
+
 /* Replaces rk_npu_moe_quant_workspace_create / rk_npu_moe_w4_workspace_create
  * (src/npu/moe.rs:200-206). One workspace per stream; reusable by every
  * bank of the same geometry. */

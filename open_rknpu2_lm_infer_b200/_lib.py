@@ -86,6 +86,14 @@ SIGNATURES = [
      [C.POINTER(Config), C.POINTER(Expert), C.POINTER(Format)]),
     ("moe_b200_weights_free", None, [C.c_void_p]),
     ("moe_b200_weights_device_bytes", C.c_uint64, [C.c_void_p]),
+    ("moe_b200_blob_version", C.c_uint32, []),
+    ("moe_b200_slots_create", C.c_void_p, [C.POINTER(Config), C.c_int32]),
+    ("moe_b200_expert_blob_bytes", C.c_uint64, [C.c_void_p]),
+    ("moe_b200_export_expert", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_uint64]),
+    ("moe_b200_import_expert", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_uint64]),
+    ("moe_b200_import_expert_async", C.c_int,
+     [C.c_void_p, C.c_int32, C.c_void_p, C.c_uint64, C.c_void_p]),
+    ("moe_b200_swap_slots", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32, C.c_void_p]),
     ("moe_b200_workspace_create", C.c_void_p, [C.POINTER(Config)]),
     ("moe_b200_workspace_free", None, [C.c_void_p]),
     ("moe_b200_workspace_device_bytes", C.c_uint64, [C.c_void_p]),

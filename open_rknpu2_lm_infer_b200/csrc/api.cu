@@ -667,6 +667,175 @@ void moe_b200_weights_free(moe_b200_weights* w) {
 
 uint64_t moe_b200_weights_device_bytes(const moe_b200_weights* w) { return w ? w->bytes : 0; }
 
+// ---- expert slot bank -------------------------------------------------------
+// A blob is one routed expert's packed device image: a 64-byte header, then
+// the gate|up weights, their scales, the down weights and their scales, each
+// exactly as they sit in the bank (tile-major, swizzled), so import and export
+// are plain copies.
+
+namespace {
+
+constexpr char kBlobMagic[8] = {'M', 'B', '2', 'X', 'B', 'L', 'O', 'B'};
+
+struct BlobHeader {
+    char magic[8];
+    uint32_t version, format, hidden, intermediate;
+    uint64_t sizes[4];  // gate|up weights, gate|up scales, down weights, down scales
+    uint8_t pad[8];
+};
+static_assert(sizeof(BlobHeader) == 64, "blob header is 64 bytes");
+
+struct Region {
+    uint8_t* dev;
+    uint64_t bytes;
+};
+
+// The four device regions of expert e (weights of group-32 banks carry their
+// scales inside; their scale regions hold the unused per-channel slots).
+void expert_regions(const moe_b200_weights* w, int e, Region r[4]) {
+    r[0] = {w->gu.w + w->gu.w_expert_stride * e, w->gu.w_expert_stride};
+    r[1] = {static_cast<uint8_t*>(w->gu.s) + w->gu.s_expert_stride * e, w->gu.s_expert_stride};
+    r[2] = {w->dn.w + w->dn.w_expert_stride * e, w->dn.w_expert_stride};
+    r[3] = {static_cast<uint8_t*>(w->dn.s) + w->dn.s_expert_stride * e, w->dn.s_expert_stride};
+}
+
+uint32_t public_format(const moe_b200_weights* w) {
+    if (w->gu.fmt == kFmtW4G32)
+        return w->exact_down ? MOE_B200_W4_G32_FP16_EXACT : MOE_B200_W4_G32_FP16;
+    return (uint32_t)w->gu.fmt;  // kFmtW4PC / kFmtW8PC match the public values
+}
+
+BlobHeader blob_header(const moe_b200_weights* w) {
+    BlobHeader h{};
+    std::memcpy(h.magic, kBlobMagic, 8);
+    h.version = MOE_B200_BLOB_VERSION;
+    h.format = public_format(w);
+    h.hidden = (uint32_t)w->H;
+    h.intermediate = (uint32_t)w->I;
+    Region r[4];
+    expert_regions(w, 0, r);
+    for (int i = 0; i < 4; ++i) h.sizes[i] = r[i].bytes;
+    return h;
+}
+
+uint64_t blob_size(const moe_b200_weights* w) {
+    const BlobHeader h = blob_header(w);
+    return sizeof(BlobHeader) + h.sizes[0] + h.sizes[1] + h.sizes[2] + h.sizes[3];
+}
+
+int check_blob(const moe_b200_weights* w, const void* data, uint64_t bytes) {
+    if (!data || bytes != blob_size(w)) return MOE_B200_ERR_INVALID;
+    BlobHeader got;
+    std::memcpy(&got, data, sizeof(got));
+    const BlobHeader want = blob_header(w);
+    if (std::memcmp(got.magic, want.magic, 8) || got.version != want.version ||
+        got.format != want.format || got.hidden != want.hidden ||
+        got.intermediate != want.intermediate || std::memcmp(got.sizes, want.sizes, sizeof(got.sizes)))
+        return MOE_B200_ERR_INVALID;
+    return MOE_B200_OK;
+}
+
+}  // namespace
+
+uint32_t moe_b200_blob_version(void) { return MOE_B200_BLOB_VERSION; }
+
+moe_b200_weights* moe_b200_slots_create(const moe_b200_config* cfg, int32_t routed_format) {
+    if (validate_config(cfg) || cfg->weights.shared_expert) return nullptr;
+    if (routed_format < 0 || routed_format > MOE_B200_W4_G32_FP16_EXACT) return nullptr;
+    if (check_device(cfg->device, nullptr)) return nullptr;
+    DeviceGuard guard(cfg->device);
+    const bool exact_down = routed_format == MOE_B200_W4_G32_FP16_EXACT;
+    const int f = exact_down ? MOE_B200_W4_G32_FP16 : routed_format;
+    auto* w = new moe_b200_weights();
+    w->device = cfg->device;
+    w->H = cfg->weights.hidden;
+    w->I = cfg->weights.intermediate;
+    w->E = cfg->weights.routed_experts;
+    w->top = cfg->top;
+    w->Is = w->I;
+    w->exact_down = exact_down;
+    setup_mat(w->gu, f, w->E, w->H, w->I, true);
+    setup_mat(w->dn, f, w->E, w->I, w->H, false);
+    for (PackedMat* m : {&w->gu, &w->dn}) {
+        const size_t wb = m->w_expert_stride * w->E, sb = m->s_expert_stride * w->E;
+        void *dw = nullptr, *ds = nullptr;
+        if (dev_alloc(&dw, wb) != cudaSuccess || dev_alloc(&ds, sb) != cudaSuccess ||
+            cudaMemset(dw, 0, wb) != cudaSuccess || cudaMemset(ds, 0, sb) != cudaSuccess) {
+            if (dw) cudaFree(dw);
+            if (ds) cudaFree(ds);
+            moe_b200_weights_free(w);
+            return nullptr;
+        }
+        m->w = static_cast<uint8_t*>(dw);
+        m->s = ds;
+        w->bytes += wb + sb;
+    }
+    return w;
+}
+
+uint64_t moe_b200_expert_blob_bytes(const moe_b200_weights* w) { return w ? blob_size(w) : 0; }
+
+int moe_b200_export_expert(const moe_b200_weights* w, int32_t expert, void* data, uint64_t bytes) {
+    if (!w || !data || bytes != blob_size(w)) return MOE_B200_ERR_INVALID;
+    if (expert < 0 || expert >= w->E) return MOE_B200_ERR_BAD_EXPERT;
+    DeviceGuard guard(w->device);
+    const BlobHeader h = blob_header(w);
+    std::memcpy(data, &h, sizeof(h));
+    uint8_t* dst = static_cast<uint8_t*>(data) + sizeof(h);
+    Region r[4];
+    expert_regions(w, expert, r);
+    for (const Region& g : r) {
+        const cudaError_t e = cudaMemcpy(dst, g.dev, g.bytes, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) return cuda_rc(e);
+        dst += g.bytes;
+    }
+    return MOE_B200_OK;
+}
+
+int moe_b200_import_expert_async(moe_b200_weights* w, int32_t slot, const void* data,
+                                 uint64_t bytes, void* stream) {
+    if (!w) return MOE_B200_ERR_INVALID;
+    int rc = check_blob(w, data, bytes);
+    if (rc) return rc;
+    if (slot < 0 || slot >= w->E) return MOE_B200_ERR_BAD_EXPERT;
+    DeviceGuard guard(w->device);
+    const uint8_t* src = static_cast<const uint8_t*>(data) + sizeof(BlobHeader);
+    Region r[4];
+    expert_regions(w, slot, r);
+    for (const Region& g : r) {
+        const cudaError_t e = cudaMemcpyAsync(g.dev, src, g.bytes, cudaMemcpyHostToDevice,
+                                              static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_rc(e);
+        src += g.bytes;
+    }
+    return MOE_B200_OK;
+}
+
+int moe_b200_import_expert(moe_b200_weights* w, int32_t slot, const void* data, uint64_t bytes) {
+    int rc = moe_b200_import_expert_async(w, slot, data, bytes, nullptr);
+    if (rc) return rc;
+    DeviceGuard guard(w->device);
+    return cuda_rc(cudaStreamSynchronize(nullptr));
+}
+
+int moe_b200_swap_slots(moe_b200_weights* bank, int32_t slot, moe_b200_weights* staging,
+                        int32_t staged, void* stream) {
+    if (!bank || !staging || bank->device != staging->device) return MOE_B200_ERR_INVALID;
+    if (blob_size(bank) != blob_size(staging) || public_format(bank) != public_format(staging) ||
+        bank->H != staging->H || bank->I != staging->I)
+        return MOE_B200_ERR_INVALID;
+    if (slot < 0 || slot >= bank->E || staged < 0 || staged >= staging->E)
+        return MOE_B200_ERR_BAD_EXPERT;
+    if (bank == staging && slot == staged) return MOE_B200_OK;
+    DeviceGuard guard(bank->device);
+    Region a[4], b[4];
+    expert_regions(bank, slot, a);
+    expert_regions(staging, staged, b);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (int i = 0; i < 4; ++i) launch_swap_bytes(a[i].dev, b[i].dev, a[i].bytes, s);
+    return cuda_rc(cudaPeekAtLastError());
+}
+
 moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     if (validate_config(cfg)) return nullptr;
     int sms = 0;

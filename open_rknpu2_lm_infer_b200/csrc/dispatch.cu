@@ -18,6 +18,8 @@
 //                (src/model/qwen35/decoder.rs:215-217)
 #include <float.h>
 
+#include <algorithm>
+
 #include "kernels.cuh"
 
 namespace moe {
@@ -449,6 +451,22 @@ void launch_requant(const float* gate_up, const int32_t* count, int max_rows, in
     else if (v <= 8) RQ(8);
     else RQ(16);
 #undef RQ
+}
+
+__global__ void swap_bytes_kernel(uint4* __restrict__ a, uint4* __restrict__ b, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const uint4 x = a[i];
+        a[i] = b[i];
+        b[i] = x;
+    }
+}
+
+void launch_swap_bytes(void* a, void* b, size_t bytes, cudaStream_t s) {
+    const size_t n = bytes / 16;
+    if (n == 0) return;
+    const unsigned blocks = (unsigned)std::min<size_t>((n + 255) / 256, 148 * 8);
+    swap_bytes_kernel<<<blocks, 256, 0, s>>>(static_cast<uint4*>(a), static_cast<uint4*>(b), n);
 }
 
 void launch_combine(const float* y, const int32_t* pos, const float* routes, const float* shared,

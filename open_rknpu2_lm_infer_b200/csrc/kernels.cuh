@@ -108,6 +108,9 @@ void launch_combine(const float* y, const int32_t* pos, const float* routes, con
                     const float* residual, int T, int H, int k, float* out, cudaStream_t s,
                     const float* gate = nullptr, int gate_ld = 0);
 
+// Exchanges two device byte ranges (16-byte aligned, bytes % 16 == 0).
+void launch_swap_bytes(void* a, void* b, size_t bytes, cudaStream_t s);
+
 constexpr int kRouteChunk = 512;  // assignments per route_count / route_scatter CTA
 
 // K-blocks (128 bytes of K each) per GEMM load stage: one bulk copy brings the

@@ -195,7 +195,28 @@ class Backend:
                 raise MoeError("cannot allocate grouped MoE workspace", L.ERR_NOMEM)
             self._work[key] = _Handle(ws, self.lib.moe_b200_workspace_free)
         self.weight_bytes += self.lib.moe_b200_weights_device_bytes(raw)
-        return Moe(self, weights, key, cfg)
+        return Moe(self, weights, key, cfg, routed)
+
+    def moe_packed(self, h: int, f: int, slots: int, top: int,
+                   fmt: int = L.W4_PER_CHANNEL) -> "Moe":
+        """An empty bank of `slots` expert slots to import blobs into
+        (Backend::moe_packed / moe_slots, src/npu/moe.rs:145-175)."""
+        if not (h > 0 and f > 0 and 0 < top <= slots):
+            raise ValueError("invalid MoE slot bank geometry")
+        cfg = self._config(h, f, slots, False, top, 0)
+        raw = self.lib.moe_b200_slots_create(C.byref(cfg), fmt)
+        if not raw:
+            raise MoeError("cannot allocate expert slot bank", L.ERR_NOMEM)
+        weights = _Handle(raw, self.lib.moe_b200_weights_free)
+        key = (h, f, slots, top, False, 0)
+        if key not in self._work:
+            ws = self.lib.moe_b200_workspace_create(C.byref(cfg))
+            if not ws:
+                weights.close()
+                raise MoeError("cannot allocate grouped MoE workspace", L.ERR_NOMEM)
+            self._work[key] = _Handle(ws, self.lib.moe_b200_workspace_free)
+        self.weight_bytes += self.lib.moe_b200_weights_device_bytes(raw)
+        return Moe(self, weights, key, cfg, fmt)
 
     def _config(self, h, f, e, shared, top, shared_inter) -> L.Config:
         cfg = L.Config()
@@ -286,14 +307,39 @@ class Router:
         self.handle.close()
 
 
+@dataclass
+class ImportBank:
+    """A staging bank (npu::ImportBank): slots filled off the critical path,
+    then swapped into a live bank with Moe.promote."""
+    owner: "Backend"
+    weights: "_Handle"
+    slots: int
+
+    def import_(self, slot: int, data) -> None:
+        if not 0 <= slot < self.slots:
+            raise ValueError("staging slot out of range")
+        mv = memoryview(data).cast("B")
+        buf = (C.c_uint8 * len(mv)).from_buffer_copy(mv)
+        check(self.owner.lib.moe_b200_import_expert(self.weights.raw, slot, buf, len(mv)),
+              "import staged expert")
+
+    def weight_bytes(self) -> int:
+        return self.owner.lib.moe_b200_weights_device_bytes(self.weights.raw)
+
+    def close(self):
+        self.weights.close()
+
+
 class Moe:
     """npu::Moe (src/npu/moe.rs:10-14, 242-388)."""
 
-    def __init__(self, owner: Backend, weights: _Handle, key: tuple, cfg: L.Config):
+    def __init__(self, owner: Backend, weights: _Handle, key: tuple, cfg: L.Config,
+                 fmt: int = L.W4_PER_CHANNEL):
         self.owner = owner
         self.weights = weights
         self.key = key
         self.cfg = cfg
+        self.fmt = fmt  # routed MOE_B200_W* format
 
     @property
     def workspace(self) -> int:
@@ -309,6 +355,52 @@ class Moe:
 
     def max_rows(self) -> int:
         return self.owner.lib.moe_b200_max_rows(self.workspace)
+
+    # ---- slot bank (src/npu/moe.rs:243-320) ----
+    @staticmethod
+    def blob_version() -> int:
+        return L.load().moe_b200_blob_version()
+
+    def blob_bytes(self) -> int:
+        return self.owner.lib.moe_b200_expert_blob_bytes(self.weights.raw)
+
+    def export(self, expert: int) -> bytes:
+        """The packed device image of one expert (Moe::export)."""
+        if not 0 <= expert < self.key[2]:
+            raise ValueError("expert index out of range")
+        buf = (C.c_uint8 * self.blob_bytes())()
+        check(self.owner.lib.moe_b200_export_expert(self.weights.raw, expert, buf, len(buf)),
+              "export packed expert")
+        return bytes(buf)
+
+    def import_(self, slot: int, data) -> None:
+        """Loads a blob into a slot (Moe::import)."""
+        if not 0 <= slot < self.key[2]:
+            raise ValueError("expert slot out of range")
+        mv = memoryview(data).cast("B")
+        buf = (C.c_uint8 * len(mv)).from_buffer_copy(mv) if mv.readonly else \
+            (C.c_uint8 * len(mv)).from_buffer(mv)
+        check(self.owner.lib.moe_b200_import_expert(self.weights.raw, slot, buf, len(mv)),
+              "import packed expert")
+
+    def import_device(self, slot: int, ptr: int, nbytes: int, stream: int = 0) -> None:
+        """Stream-ordered import from host memory at `ptr` (page-locked for overlap)."""
+        check(self.owner.lib.moe_b200_import_expert_async(self.weights.raw, slot, ptr, nbytes,
+                                                          stream), "import packed expert")
+
+    def import_bank(self, slots: int) -> "ImportBank":
+        """A staging bank of the same geometry and format (Moe::import_bank)."""
+        cfg = self.owner._config(self.key[0], self.key[1], slots, False, min(self.key[3], slots), 0)
+        raw = self.owner.lib.moe_b200_slots_create(C.byref(cfg), self.fmt)
+        if not raw:
+            raise MoeError("cannot allocate expert staging bank", L.ERR_NOMEM)
+        self.owner.weight_bytes += self.owner.lib.moe_b200_weights_device_bytes(raw)
+        return ImportBank(self.owner, _Handle(raw, self.owner.lib.moe_b200_weights_free), slots)
+
+    def promote(self, slot: int, bank: "ImportBank", staged: int, stream: int = 0) -> None:
+        """Exchanges this bank's slot with a staged expert (Moe::promote)."""
+        check(self.owner.lib.moe_b200_swap_slots(self.weights.raw, slot, bank.weights.raw, staged,
+                                                 stream), "promote staged expert")
 
     def weight_bytes(self) -> int:
         return self.owner.lib.moe_b200_weights_device_bytes(self.weights.raw)
