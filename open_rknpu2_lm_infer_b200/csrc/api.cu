@@ -307,6 +307,7 @@ struct moe_b200_workspace {
     float* s_x = nullptr;
     int32_t *hist = nullptr, *offsets = nullptr, *perm = nullptr, *pos = nullptr;
     int32_t *shared_offsets = nullptr, *counters = nullptr;
+    int32_t* gv_counters = nullptr;  // small-batch path: last-arrival counters
     int8_t* a_perm = nullptr;
     __half *q_m_h = nullptr, *sq_m_h = nullptr;  // fp16 copies of the middle codes (group-32 down)
     float* s_perm = nullptr;
@@ -433,6 +434,73 @@ cudaEvent_t* prof_slot(moe_b200_workspace* ws, int flags) {
 
 // The whole routed (+ shared) pipeline on device pointers. ev != null records
 // stage events for run_profiled-style timings.
+// Small batches of group-32 banks without a shared expert run the GEMV path
+// (csrc/gemv.cu): 3 launches, every weight stage in flight at once.
+constexpr int kGemvMaxRows = 4;
+
+bool use_gemv(const moe_b200_workspace* ws, const moe_b200_weights* w, int rows) {
+    return rows <= kGemvMaxRows && w->gu.fmt == kFmtW4G32 && w->dn.fmt == kFmtW4G32 &&
+           !w->shared && (int)(gemv_smem_bytes((int)(w->gu.kblocks / kKPS))) <= (int)kGemvMaxSmem &&
+           gemv_smem_bytes((int)(w->dn.kblocks / kKPS)) <= kGemvMaxSmem && ws->k <= 32;
+}
+
+int run_small(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
+              const int32_t* d_ids, const float* d_routes, const float* d_res, float* d_out,
+              cudaStream_t s, cudaEvent_t* evs, cudaEvent_t res_ready) {
+    auto mark = [&](int i) {
+        if (evs) cudaEventRecord(evs[i], s);
+    };
+    ws->launches += 3;
+    mark(1);
+    mark(2);
+    launch_quant_gather(d_x, rows, ws->H, ws->Kh, kQuantMoe, 1, nullptr, ws->q_x, ws->s_x,
+                        nullptr, nullptr, nullptr, nullptr, ws->err, s);
+    mark(3);
+    GemvArgs a{};
+    a.ids = d_ids;
+    a.routes = d_routes;
+    a.T = rows;
+    a.k = ws->k;
+    a.E = ws->E;
+    a.H = ws->H;
+    a.I = ws->I;
+    a.q_x = ws->q_x;
+    a.s_x = ws->s_x;
+    a.ld_qx = ws->Kh;
+    a.gu_w = w->gu.w;
+    a.gu_expert_stride = w->gu.w_expert_stride;
+    a.gu_tile_stride = w->gu.w_tile_stride;
+    a.gu_stage_stride = w->gu.w_stage_stride;
+    a.gu_stages = w->gu.kblocks / kKPS;
+    a.dn_w = w->dn.w;
+    a.dn_expert_stride = w->dn.w_expert_stride;
+    a.dn_tile_stride = w->dn.w_tile_stride;
+    a.dn_stage_stride = w->dn.w_stage_stride;
+    a.dn_stages = w->dn.kblocks / kKPS;
+    a.middle = ws->gate_up;
+    a.q_m = ws->q_m;
+    a.s_m = ws->s_m;
+    a.ld_qm = ws->Ki;
+    a.y = ws->y;
+    a.residual = d_res;
+    a.out = d_out;
+    a.counters = ws->gv_counters;
+    a.dn_counter_base = (int)ws->n_max;
+    a.err = ws->err;
+    if (launch_gemv(a, 0, s)) return MOE_B200_ERR_UNSUPPORTED;
+    mark(4);
+    mark(5);
+    if (res_ready) cudaStreamWaitEvent(s, res_ready, 0);
+    if (launch_gemv(a, 1, s)) return MOE_B200_ERR_UNSUPPORTED;
+    mark(6);
+    mark(7);
+    mark(8);
+    ws->last_rows = 0;  // no permuted accumulators to dump for this call
+    ws->last_w = w;
+    ws->last_stream = s;
+    return cuda_rc(cudaPeekAtLastError());
+}
+
 // The shared-gate logits of a gated router: column E of the workspace logits.
 struct GateRef {
     const float* logits = nullptr;
@@ -443,6 +511,8 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
                  const int32_t* d_ids, const float* d_routes, const float* d_res, float* d_out,
                  cudaStream_t s, cudaEvent_t* evs, cudaEvent_t res_ready = nullptr,
                  GateRef gate = {}) {
+    if (use_gemv(ws, w, rows))
+        return run_small(ws, w, rows, d_x, d_ids, d_routes, d_res, d_out, s, evs, res_ready);
     const int E = ws->E, k = ws->k, H = ws->H, I = ws->I;
     const long n = (long)rows * k;
     auto mark = [&](int i) {
@@ -873,6 +943,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     rc |= ws_alloc(ws, &ws->pos, n);
     rc |= ws_alloc(ws, &ws->shared_offsets, 2);
     rc |= ws_alloc(ws, &ws->counters, T);
+    rc |= ws_alloc(ws, &ws->gv_counters, n + T * ((ws->H + 127) / 128));
     rc |= ws_alloc(ws, &ws->a_perm, (n + pad_rows) * ws->Kh);
     rc |= ws_alloc(ws, &ws->q_m_h, (n + pad_rows) * ws->Ki);
     rc |= ws_alloc(ws, &ws->s_perm, n);
@@ -896,6 +967,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
         return nullptr;
     }
     cudaMemset(ws->counters, 0, sizeof(int) * T);
+    cudaMemset(ws->gv_counters, 0, sizeof(int) * (size_t)(n + T * ((ws->H + 127) / 128)));
     cudaMemset(ws->err, 0, sizeof(uint32_t));
     cudaMemset(ws->a_perm, 0, (size_t)(n + pad_rows) * ws->Kh);
     cudaMemset(ws->q_m, 0, (size_t)(n + pad_rows) * ws->Ki);

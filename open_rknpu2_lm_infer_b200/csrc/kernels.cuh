@@ -108,6 +108,37 @@ void launch_combine(const float* y, const int32_t* pos, const float* routes, con
                     const float* residual, int T, int H, int k, float* out, cudaStream_t s,
                     const float* gate = nullptr, int gate_ld = 0);
 
+// gemv.cu: the small-batch path of group-32 int4 banks (no shared expert).
+struct GemvArgs {
+    const int32_t* ids;       // [T][k]
+    const float* routes;      // [T][k]
+    int T, k, E, H, I;
+    const int8_t* q_x;        // [T][ld_qx] MoE A8 codes of the tokens
+    const float* s_x;         // [T]
+    int ld_qx;
+    const uint8_t* gu_w;      // packed gate|up bank
+    size_t gu_expert_stride, gu_tile_stride, gu_stage_stride;
+    int gu_stages;            // 256-k stages of the gate/up K (= H padded)
+    const uint8_t* dn_w;      // packed down bank
+    size_t dn_expert_stride, dn_tile_stride, dn_stage_stride;
+    int dn_stages;
+    float* middle;            // [T*k][I]
+    int8_t* q_m;              // [T*k][ld_qm]
+    float* s_m;               // [T*k]
+    int ld_qm;
+    float* y;                 // [T*k][H]
+    const float* residual;    // [T][H] or null
+    float* out;               // [T][H]
+    int* counters;            // [T*k] gate/up, then [T][H/128] down (zeroed)
+    int dn_counter_base;
+    uint32_t* err;
+};
+// part 0: gate/up (+ SwiGLU + requant), part 1: down (+ combine + residual).
+// -1 when the stage set does not fit shared memory (kGemvMaxSmem).
+constexpr size_t kGemvMaxSmem = 220 * 1024;
+int launch_gemv(const GemvArgs& a, int part, cudaStream_t s);
+size_t gemv_smem_bytes(int stages);
+
 // Exchanges two device byte ranges (16-byte aligned, bytes % 16 == 0).
 void launch_swap_bytes(void* a, void* b, size_t bytes, cudaStream_t s);
 

@@ -229,10 +229,66 @@ __global__ void route_rows_kernel(const RouterArgs a) {
     route_row(a, warp, lane);
 }
 
+// Rows of up to 256 logits: the row is read once into registers (one L2 round
+// trip instead of one per round), then the same selection as topk_row.
+__device__ __forceinline__ void topk_row_regs(const float* row, int E, int k, float min_weight,
+                                              int32_t* ids, float* weights, int lane,
+                                              uint32_t* err) {
+    constexpr int kPL = 8;
+    uint32_t key[kPL];
+    float val[kPL];
+    bool finite = true;
+#pragma unroll
+    for (int i = 0; i < kPL; ++i) {
+        const int e = lane + 32 * i;
+        val[i] = e < E ? __ldcg(row + e) : 0.0f;
+        if (e < E && !isfinite(val[i])) finite = false;
+        key[i] = (uint32_t)total_key(val[i]) ^ 0x80000000u;
+    }
+    if (__any_sync(0xffffffffu, !finite) && lane == 0) atomicOr(err, kErrNonFinite);
+    uint32_t taken = 0;
+    int my_id = -1;
+    float my_val = 0.0f, top_val = 0.0f;
+    for (int r = 0; r < k; ++r) {
+        unsigned long long best = 0ull;
+#pragma unroll
+        for (int i = 0; i < kPL; ++i) {
+            const int e = lane + 32 * i;
+            if (e >= E || ((taken >> i) & 1u)) continue;
+            const unsigned long long v = ((unsigned long long)key[i] << 32) | (0xFFFFFFFFu - (uint32_t)e);
+            if (v > best) best = v;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+            if (o > best) best = o;
+        }
+        const int win = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+        const float wv = key_value((int32_t)((uint32_t)(best >> 32) ^ 0x80000000u));
+        if ((win & 31) == lane) taken |= 1u << (win >> 5);
+        if (lane == r) { my_id = win; my_val = wv; }
+        if (r == 0) top_val = wv;
+    }
+    float w = 0.0f;
+    if (lane < k) w = expf(__fsub_rn(my_val, top_val));
+    float sum = -0.0f;
+    for (int r = 0; r < k; ++r) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, w, r));
+    if (lane < k) {
+        w = __fdiv_rn(w, sum);
+        if (min_weight != 0.0f && lane >= 1 && w < min_weight) w = 0.0f;
+        ids[lane] = my_id;
+        weights[lane] = w;
+    }
+}
+
 // One warp selects the top-k of a row of E logits (E <= 1024): k rounds of a
 // warp arg-max over (total_cmp key, -id), then softmax over the selected.
 __device__ void topk_row(const float* row, int E, int k, float min_weight, int32_t* ids,
                          float* weights, int lane, uint32_t* err) {
+    if (E <= 256) {
+        topk_row_regs(row, E, k, min_weight, ids, weights, lane, err);
+        return;
+    }
     uint32_t taken = 0;  // bit i: element lane + 32*i already selected
     const int per_lane = (E + 31) / 32;
     int my_id = -1;

@@ -277,8 +277,8 @@ def test_invalid_inputs_are_rejected(cuda):
     # the device path flags an out-of-range id through the status word
     import torch
     dx, dout = torch.from_numpy(x).cuda(), torch.empty((8, spec.hidden), device="cuda")
-    moe.run_device(dx.data_ptr(), torch.from_numpy(bad).cuda().data_ptr(),
-                   torch.from_numpy(routes).cuda().data_ptr(), dout.data_ptr(), 8,
+    d_ids, d_w = torch.from_numpy(bad).cuda(), torch.from_numpy(routes).cuda()  # kept alive
+    moe.run_device(dx.data_ptr(), d_ids.data_ptr(), d_w.data_ptr(), dout.data_ptr(), 8,
                    torch.cuda.current_stream().cuda_stream)
     with pytest.raises(MoeError) as e:
         moe.status()
