@@ -233,13 +233,8 @@ def run_ours(args):
     stage_avg = {k: statistics.mean(s[k] for s in stages) for k in stages[0]} if stages else {}
 
     # routing statistics of the last call: experts hit, kept assignments
-    offs_ptr, _ = moe.buffer("offsets")
-    offs = np.empty(spec.experts + 1, np.int32)
-    import ctypes as C
     torch.cuda.synchronize()
-    cudart_copy(offs, offs_ptr)
-    U = int(np.count_nonzero(np.diff(offs)))
-    A = int(offs[-1])
+    U, A = routing_stats(moe, spec, T)
 
     pk, pk_kind = peaks()
     hbm_peak = pk["hbm_gbs"]
@@ -437,6 +432,17 @@ def run_ep(args):
         print(json.dumps(result), flush=True)
 
 
+def routing_stats(moe, spec, T):
+    """(distinct experts hit, kept assignments) of the last routed call, from
+    the workspace's ids and routing weights (valid for every execution path)."""
+    ids = np.empty((T, spec.top), np.int32)
+    w = np.empty((T, spec.top), np.float32)
+    cudart_copy(ids, moe.buffer("ids")[0])
+    cudart_copy(w, moe.buffer("routes")[0])
+    kept = w > 0
+    return int(np.unique(ids[kept]).size), int(kept.sum())
+
+
 def cudart_copy(dst: np.ndarray, src_ptr: int):
     import torch
 
@@ -517,10 +523,7 @@ def run_extra(args, moe, router, spec, lib, wsp, hbm_peak):
                 st.append(tm.as_dict())
         lib.moe_b200_workspace_profile(wsp, 0)
         avg = {k: statistics.mean(s[k] for s in st) for k in st[0]} if st else {}
-        offs_ptr, _ = moe.buffer("offsets")
-        offs = np.empty(spec.experts + 1, np.int32)
-        cudart_copy(offs, offs_ptr)
-        U, A = int(np.count_nonzero(np.diff(offs))), int(offs[-1])
+        U, A = routing_stats(moe, spec, T)
         lb = layer_bytes(spec, T, U, A)
         ops = 2 * A * 3 * spec.hidden * spec.inter
         gb = gate_up_bytes(spec, U, A)

@@ -435,7 +435,7 @@ cudaEvent_t* prof_slot(moe_b200_workspace* ws, int flags) {
 // The whole routed (+ shared) pipeline on device pointers. ev != null records
 // stage events for run_profiled-style timings.
 // Small batches of group-32 banks without a shared expert run the GEMV path
-// (csrc/gemv.cu): 3 launches, every weight stage in flight at once.
+// (csrc/gemv.cu): 2 launches after the router, every weight stage in flight.
 constexpr int kGemvMaxRows = 4;
 
 bool use_gemv(const moe_b200_workspace* ws, const moe_b200_weights* w, int rows) {
@@ -450,11 +450,9 @@ int run_small(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const
     auto mark = [&](int i) {
         if (evs) cudaEventRecord(evs[i], s);
     };
-    ws->launches += 3;
+    ws->launches += 2;
     mark(1);
     mark(2);
-    launch_quant_gather(d_x, rows, ws->H, ws->Kh, kQuantMoe, 1, nullptr, ws->q_x, ws->s_x,
-                        nullptr, nullptr, nullptr, nullptr, ws->err, s);
     mark(3);
     GemvArgs a{};
     a.ids = d_ids;
@@ -464,9 +462,7 @@ int run_small(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const
     a.E = ws->E;
     a.H = ws->H;
     a.I = ws->I;
-    a.q_x = ws->q_x;
-    a.s_x = ws->s_x;
-    a.ld_qx = ws->Kh;
+    a.x = d_x;
     a.gu_w = w->gu.w;
     a.gu_expert_stride = w->gu.w_expert_stride;
     a.gu_tile_stride = w->gu.w_tile_stride;
@@ -1467,8 +1463,10 @@ int moe_b200_forward_f32(moe_b200_workspace* ws, const moe_b200_weights* w,
 int moe_b200_workspace_status(moe_b200_workspace* ws) {
     if (!ws) return MOE_B200_ERR_INVALID;
     DeviceGuard guard(ws->device);
-    cudaStream_t s = ws->last_stream ? ws->last_stream : ws->own_stream;
-    cudaError_t e = cudaStreamSynchronize(s);
+    // the last launching stream (a null handle is the legacy default stream,
+    // which the non-blocking own stream does not order against), then our own
+    cudaError_t e = cudaStreamSynchronize(ws->last_stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ws->own_stream);
     if (e != cudaSuccess) return cuda_rc(e);
     return read_status(ws, ws->own_stream);
 }

@@ -21,13 +21,12 @@
 //                        group with a TMEM read-back per k-block is bound by
 //                        that round trip (measured ~3.5x slower).
 //   W4 group-32 (exact)  kind::i8, one MMA (K = 32 = one group) per TMEM
-//                        buffer; the four buffers of a k-block form a slot.
-//                        Every buffer holds the bits of 12582912.0f before its
-//                        MMA, which adds the int32 sum to them, so the result
-//                        read back as a float is exactly 12582912 + 16*acc
-//                        (|16*acc| < 2^22). The epilogue re-arms the buffers
-//                        right after loading them and computes
-//                        f = fma(D - 12582912, s/16, f) two values per
+//                        buffer, overwriting it; the four buffers of a k-block
+//                        form a slot. The epilogue adds the bits of
+//                        12582912.0f to each int32 sum D = 16*acc (an integer
+//                        add), which reads back as the float 12582912 + 16*acc
+//                        exactly (|16*acc| < 2^22), and computes
+//                        f = fma(that - 12582912, s/16, f) two values per
 //                        instruction (f32x2), equal to fma((float)acc, s, f) bit
 //                        for bit. Used where the result is requantised (the
 //                        gate/up GEMM: a rounding difference there flips int8
@@ -271,13 +270,6 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     // lane quadrant of this warp's TMEM accesses
     const int quad = warp & 3;
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-    if (C::kGroup && warp >= C::kEpiWarp0) {
-        // every group buffer starts as the float 12582912.0
-        const int half = (warp - C::kEpiWarp0) >> 2;
-        for (int b = 0; b < C::kNSlot * 4; ++b)
-            tmem_fill<C::kHalf>(acc_base + lane_addr + b * NT + half * C::kHalf, kMagicBits);
-        tmem_wait_st();
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -364,12 +356,12 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
                                 const uint64_t db = smem_desc_k_sw128(abk + 32 * j);
-                                // exact group path: each buffer adds one group's sum to the
-                                // magic float; per-channel: accumulate over K
+                                // exact group path: each buffer receives one group's sum
+                                // (overwritten); per-channel: accumulate over K
                                 const uint32_t d = C::kGroup ? acc_base + slot * C::kSlotCols + j * NT
                                                              : acc_base + dcol;
                                 const uint32_t acc =
-                                    C::kGroup ? 1u : ((st > 0 || jk > 0 || j > 0) ? 1u : 0u);
+                                    C::kGroup ? 0u : ((st > 0 || jk > 0 || j > 0) ? 1u : 0u);
                                 if (C::kW4)
                                     mma_i8_ts(d, a_tmem + jk * 32 + 8 * j, db, idesc, acc);
                                 else
@@ -582,19 +574,13 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                         // (the group order per column stays 0..3)
                         constexpr int kRound = C::kHalf < 8 ? C::kHalf : 8;
 #pragma unroll
-                        for (int r0 = 0; r0 < C::kHalf; r0 += kRound) {
+                        for (int r0 = 0; r0 < C::kHalf && active; r0 += kRound) {
                             uint32_t v[4][kRound];
-                            if (active) {
 #pragma unroll
-                                for (int j = 0; j < 4; ++j) tmem_ld<kRound>(sbase + j * NT + r0, v[j]);
-                                tmem_wait_ld();
+                            for (int j = 0; j < 4; ++j) tmem_ld<kRound>(sbase + j * NT + r0, v[j]);
+                            tmem_wait_ld();
 #pragma unroll
-                                for (int j = 0; j < 4; ++j) tmem_ld_pin(v[j]);
-                            }
-                            // columns of an idle warp are re-armed too: the MMA adds to them
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) tmem_fill<kRound>(sbase + j * NT + r0, kMagicBits);
-                            if (!active) continue;
+                            for (int j = 0; j < 4; ++j) tmem_ld_pin(v[j]);
                             if (EPI == kEpiAcc) {
 #pragma unroll
                                 for (int j = 0; j < 4; ++j)
@@ -602,8 +588,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                                     for (int q = 0; q < kRound; ++q)
                                         if (c0 + r0 + q < nvalid && col_ok)
                                             a.acc_out[((size_t)(row0 + c0 + r0 + q) * (a.kblocks * 4) + kb * 4 +
-                                                       j) * a.acc_ld + ocol] = (int)(v[j][q] - kMagicBits) >> 4;
+                                                       j) * a.acc_ld + ocol] = (int)v[j][q] >> 4;
                             } else {
+                                // int32 -> f32 exactly: the bits of 12582912.0f plus the
+                                // sum are the float 12582912 + sum (|sum| < 2^22)
                                 const float2 nm = make_float2(-kMagic, -kMagic);
 #pragma unroll
                                 for (int j = 0; j < 4; ++j) {
@@ -613,14 +601,14 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
 #pragma unroll
                                     for (int q = 0; q < kRound / 2; ++q) {
                                         const float2 d = __fadd2_rn(
-                                            make_float2(__uint_as_float(v[j][2 * q]), __uint_as_float(v[j][2 * q + 1])),
+                                            make_float2(__uint_as_float(v[j][2 * q] + kMagicBits),
+                                                        __uint_as_float(v[j][2 * q + 1] + kMagicBits)),
                                             nm);
                                         facc[r0 / 2 + q] = __ffma2_rn(d, s2, facc[r0 / 2 + q]);
                                     }
                                 }
                             }
                         }
-                        tmem_wait_st();
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&tempty[slot]);

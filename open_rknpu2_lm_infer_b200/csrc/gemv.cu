@@ -3,24 +3,27 @@
 //
 // At a few tokens per layer each routed expert row is used by one token, so
 // the tensor-core GEMM's per-k-block TMEM round trip of the exact group path
-// is pure latency. Here every CTA streams whole 18 KB weight stages (the
-// bank's own packed layout: 128 rows x 256 codes + 128 x 8 fp16 group scales)
-// with one bulk copy each, all stages in flight at once, and reduces them with
-// dp4a: a group's int32 sum is exact (sum over its 32 codes of code * q_x),
-// then f = fma((float)acc_g, s_g, f) over ascending groups and * s_x, the
-// restatement's order — the same values as the exact tensor-core path.
+// is pure latency. Here every CTA streams one 128-row tile of one assignment
+// as whole 18 KB stages (the bank's own packed layout: 128 rows x 256 codes +
+// 128 x 8 fp16 group scales), one bulk copy each, all stages in flight at
+// once. Sixteen warps split the (stage, 4-row) items and write every group's
+// exact int32 sum (sum over its 32 codes of code * activation code) to shared
+// memory; then one thread per row folds them in ascending group order,
+// f = fma((float)acc_g, s_g, f), and scales by the activation scale: the
+// restatement's order, the same values as the exact tensor-core path.
 //
-//   gemv_gateup_kernel : grid (T*k assignments, I/64 tiles). One CTA = one
-//     128-row gate|up tile (64 gate + 64 up channels) of one assignment ->
-//     SwiGLU middle values; the last CTA of an assignment requantises its
-//     middle row (A8, the MoE rule) for the down projection.
+//   gemv_gateup_kernel : grid (T*k assignments, I/64 tiles). Quantises its
+//     token's activation row itself (the MoE A8 rule), computes the 64 gate and
+//     64 up channels of its tile -> SwiGLU middle values; the last CTA of an
+//     assignment requantises the middle row (A8) for the down projection.
 //   gemv_down_kernel   : grid (T*k assignments, H/128 tiles) -> expert rows
 //     y; the last CTA of a (token, tile) combines the token's kept ranks in
 //     rank order (fma), adds the residual and writes the output tile.
 //
 // The "last CTA" hand-offs are counter increments after a __threadfence: no
 // CTA ever waits for another, so nothing can hang. Reference semantics: the
-// expert FFN of src/npu/moe.rs:324-333 (native), the SwiGLU of
+// expert FFN of src/npu/moe.rs:324-333 (native), the activation quantiser of
+// llm_generated_docs/MOE_CPU_FUSION_20261023.md:13, the SwiGLU of
 // native/cpu_kernels/swiglu.cpp:23-25, the combine of
 // src/model/experts/paged.rs:495-506 and the residual of
 // src/model/qwen35/decoder.rs:215-217.
@@ -32,7 +35,8 @@ namespace moe {
 
 namespace {
 
-constexpr int kGvThreads = 128;
+constexpr int kGvThreads = 512;
+constexpr int kGvWarps = kGvThreads / 32;
 constexpr int kGvStage = 128 * 128 + 128 * 16;  // bytes of one packed group-32 stage
 constexpr int kGvStageW = 128 * 128;
 
@@ -44,71 +48,111 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
     return d;
 }
 
-// Activation row -> shared memory in the packed word order: a weight word
-// holds (low nibbles) codes j = 0,4,1,5 and (high nibbles) j = 2,6,3,7 of its
-// 8 k, so the activations of each 8-k word are stored as x0 x4 x1 x5 | x2 x6
-// x3 x7. Also the per-group sums of the codes (for the offset-binary
-// correction: sum((b - 8) * x) = sum(b * x) - 8 * sum(x)).
-__device__ __forceinline__ void stage_activation(const int8_t* __restrict__ q, int K,
-                                                 uint32_t* xp, int* gsum) {
-    for (int wd = threadIdx.x; wd < K / 8; wd += blockDim.x) {
-        const uint2 v = reinterpret_cast<const uint2*>(q)[wd];
-        const uint32_t lo = v.x, hi = v.y;  // bytes x0..x3, x4..x7
-        // A = x0 x4 x1 x5, B = x2 x6 x3 x7
-        xp[2 * wd] = __byte_perm(lo, hi, 0x5140);
-        xp[2 * wd + 1] = __byte_perm(lo, hi, 0x7362);
-    }
-    for (int g = threadIdx.x; g < K / 32; g += blockDim.x) {
-        const int8_t* p = q + g * 32;
-        int s = 0;
-        for (int i = 0; i < 32; ++i) s += p[i];
-        gsum[g] = s;
-    }
+__device__ __forceinline__ int byte_sum(uint32_t w) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(w), "r"(0x01010101), "r"(0));
+    return d;
 }
 
-// One step: 4 rows x 8 groups of one stage, lane = (row rs = lane >> 3,
-// logical group gl = lane & 7). Returns this lane's exact group sum.
-__device__ __forceinline__ int group_dot(const uint8_t* stg, int lr, int gl, const uint32_t (&A)[4],
-                                         const uint32_t (&B)[4], int gs) {
-    const uint4 wv = *reinterpret_cast<const uint4*>(stg + lr * 128 + ((gl ^ (lr & 7)) * 16));
-    const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
-    int acc = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        acc = dp4a_us(wd[i] & 0x0F0F0F0Fu, A[i], acc);
-        acc = dp4a_us((wd[i] >> 4) & 0x0F0F0F0Fu, B[i], acc);
-    }
-    return acc - 8 * gs;
+// Shared-memory layout of both kernels (S stages, Kp = 256 S activation codes,
+// G = 8 S groups per row).
+struct GvSmem {
+    uint8_t* st;     // [S][kGvStage]
+    uint32_t* xp;    // [Kp / 4] activation codes in the packed word order
+    int* gsum;       // [G] per-group sums of the activation codes
+    int* acc;        // [128][G + 8] exact group sums
+    float* val;      // [128] dequantised row values
+    uint64_t* bars;  // [S]
+    int G, ld;
+};
+
+__device__ __forceinline__ GvSmem gv_smem(uint8_t* sm, int S) {
+    GvSmem m;
+    const int Kp = S * 256;
+    m.G = S * 8;
+    m.ld = m.G + 8;  // rows 8 banks apart: the 4 rows of a step store conflict-free
+    m.st = sm;
+    m.xp = reinterpret_cast<uint32_t*>(sm + (size_t)S * kGvStage);
+    m.gsum = reinterpret_cast<int*>(m.xp + Kp / 4);
+    m.acc = m.gsum + m.G;
+    m.val = reinterpret_cast<float*>(m.acc + 128 * m.ld);
+    m.bars = reinterpret_cast<uint64_t*>(m.val + 128);
+    return m;
 }
 
-// The row leader (gl == 0) folds the 8 group sums of its row in ascending
-// group order: f = fma((float)acc_g, s_g, f).
-__device__ __forceinline__ float fold_groups(float f, int acc, const uint8_t* stg, int lr, int lane) {
-    const __half* sc = reinterpret_cast<const __half*>(stg + kGvStageW + lr * 16);
-#pragma unroll
-    for (int g = 0; g < 8; ++g) {
-        const int a = __shfl_sync(0xffffffffu, acc, (lane & ~7) | g);
-        f = __fmaf_rn((float)a, __half2float(sc[g]), f);
-    }
-    return f;
+// The 8 codes of one 8-k word -> the packed word order: a weight word holds
+// (low nibbles) codes j = 0,4,1,5 and (high nibbles) j = 2,6,3,7, so the
+// activations are stored as x0 x4 x1 x5 | x2 x6 x3 x7. The group sums feed
+// the offset-binary correction sum((b - 8) x) = sum(b x) - 8 sum(x). Called
+// by whole warps with wd = thread index (4 consecutive words = one group).
+__device__ __forceinline__ void put_word(const GvSmem& m, int wd, uint32_t lo, uint32_t hi) {
+    m.xp[2 * wd] = __byte_perm(lo, hi, 0x5140);
+    m.xp[2 * wd + 1] = __byte_perm(lo, hi, 0x7362);
+    int s = byte_sum(lo) + byte_sum(hi);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if ((wd & 3) == 0) m.gsum[wd >> 2] = s;
 }
 
-__device__ __forceinline__ void load_stage_regs(const uint32_t* xp, const int* gsum, int s, int gl,
-                                                uint32_t (&A)[4], uint32_t (&B)[4], int& gs) {
-    const uint4* p = reinterpret_cast<const uint4*>(xp + (s * 8 + gl) * 8);
-    const uint4 u0 = p[0], u1 = p[1];
-    A[0] = u0.x; B[0] = u0.y; A[1] = u0.z; B[1] = u0.w;
-    A[2] = u1.x; B[2] = u1.y; A[3] = u1.z; B[3] = u1.w;
-    gs = gsum[s * 8 + gl];
-}
-
-// Issue every stage of one packed tile: one bulk copy and one barrier each.
-__device__ __forceinline__ void issue_stages(uint8_t* st, uint64_t* bars, const uint8_t* tile,
+// Every stage of one packed tile: one bulk copy and one barrier each.
+__device__ __forceinline__ void issue_stages(const GvSmem& m, const uint8_t* tile,
                                              size_t stage_stride, int S) {
     for (int s = 0; s < S; ++s) {
-        mbar_arrive_expect_tx(&bars[s], kGvStage);
-        bulk_g2s(st + (size_t)s * kGvStage, tile + (size_t)s * stage_stride, kGvStage, &bars[s]);
+        mbar_arrive_expect_tx(&m.bars[s], kGvStage);
+        bulk_g2s(m.st + (size_t)s * kGvStage, tile + (size_t)s * stage_stride, kGvStage,
+                 &m.bars[s]);
     }
+}
+
+// Phase A: items (stage s, rows 4q..4q+3), lane = (row rs = lane >> 3, logical
+// group gl = lane & 7); every group's exact sum goes to acc[row][8 s + gl].
+// Returns false when a stage never arrived (flagged).
+__device__ __forceinline__ bool group_sums(const GvSmem& m, int S, int* abort_flag,
+                                           uint32_t* err) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gl = lane & 7, rs = lane >> 3;
+    int waited = -1;
+    for (int it = warp; it < S * 32; it += kGvWarps) {
+        const int s = it >> 5, lr = (it & 31) * 4 + rs;
+        if (s != waited) {
+            // every lane waits (acquire); the warp decides together
+            if (!__all_sync(0xffffffffu, mbar_wait(&m.bars[s], 0, abort_flag, err))) return false;
+            waited = s;
+        }
+        const uint4* xq = reinterpret_cast<const uint4*>(m.xp + (s * 8 + gl) * 8);
+        const uint4 u0 = xq[0], u1 = xq[1];
+        const uint32_t A[4] = {u0.x, u0.z, u1.x, u1.z}, B[4] = {u0.y, u0.w, u1.y, u1.w};
+        const uint8_t* stg = m.st + (size_t)s * kGvStage;
+        const uint4 wv = *reinterpret_cast<const uint4*>(stg + lr * 128 + ((gl ^ (lr & 7)) * 16));
+        const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+        int acc = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            acc = dp4a_us(wd[i] & 0x0F0F0F0Fu, A[i], acc);
+            acc = dp4a_us((wd[i] >> 4) & 0x0F0F0F0Fu, B[i], acc);
+        }
+        m.acc[lr * m.ld + s * 8 + gl] = acc - 8 * m.gsum[s * 8 + gl];
+    }
+    return true;
+}
+
+// Phase B (one thread per row): f = fma((float)acc_g, s_g, f) over ascending
+// groups.
+__device__ __forceinline__ float fold_row(const GvSmem& m, int S, int r) {
+    float f = 0.0f;
+    for (int s = 0; s < S; ++s) {
+        const uint4 hs =
+            *reinterpret_cast<const uint4*>(m.st + (size_t)s * kGvStage + kGvStageW + r * 16);
+        const int4 a0 = *reinterpret_cast<const int4*>(m.acc + r * m.ld + s * 8);
+        const int4 a1 = *reinterpret_cast<const int4*>(m.acc + r * m.ld + s * 8 + 4);
+        const __half2* h = reinterpret_cast<const __half2*>(&hs);
+        const int av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            const __half hg = (g & 1) ? __high2half(h[g >> 1]) : __low2half(h[g >> 1]);
+            f = __fmaf_rn((float)av[g], __half2float(hg), f);
+        }
+    }
+    return f;
 }
 
 __device__ __forceinline__ bool last_arrival(int* counter, int expected) {
@@ -125,16 +169,31 @@ __device__ __forceinline__ bool last_arrival(int* counter, int expected) {
     return is_last;
 }
 
+// Block-wide max of non-negative values.
+__device__ __forceinline__ float gv_block_max(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = red[0];
+    for (int i = 1; i < kGvWarps; ++i) r = fmaxf(r, red[i]);
+    __syncthreads();
+    return r;
+}
+
+__device__ __forceinline__ int quant_moe(float x, float s) {
+    const int q = __float2int_rn(__fdiv_rn(x, s));
+    return q > 127 ? 127 : (q < -127 ? -127 : q);
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(kGvThreads) gemv_gateup_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
-    const int S = a.gu_stages, Kp = S * 256;
-    uint8_t* st = sm;
-    uint32_t* xp = reinterpret_cast<uint32_t*>(sm + (size_t)S * kGvStage);
-    int* gsum = reinterpret_cast<int*>(xp + Kp / 4);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(gsum + Kp / 32);
     __shared__ int abort_flag;
+    __shared__ float red[kGvWarps];
+    const int S = a.gu_stages, Kp = S * 256;
+    const GvSmem m = gv_smem(sm, S);
     const int asg = blockIdx.x, rt = blockIdx.y, t = asg / a.k;
     const float w = a.routes[asg];
     const int e = a.ids[asg];
@@ -146,134 +205,98 @@ __global__ void __launch_bounds__(kGvThreads) gemv_gateup_kernel(const GemvArgs 
     }
     if (threadIdx.x == 0) {
         abort_flag = 0;
-        for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+        for (int s = 0; s < S; ++s) mbar_init(&m.bars[s], 1);
         fence_barrier_init();
     }
     __syncthreads();
     if (threadIdx.x == 0)
-        issue_stages(st, bars, a.gu_w + (size_t)e * a.gu_expert_stride + (size_t)rt * a.gu_tile_stride,
+        issue_stages(m, a.gu_w + (size_t)e * a.gu_expert_stride + (size_t)rt * a.gu_tile_stride,
                      a.gu_stage_stride, S);
-    stage_activation(a.q_x + (size_t)t * a.ld_qx, Kp, xp, gsum);
-    __syncthreads();
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gl = lane & 7, rs = lane >> 3;
-    // warp w: gate channels 16w + 4j + rs (rows), up rows 64 + the same
-    float f[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) f[j] = 0.0f;
-    bool ok = true;
-    for (int s = 0; s < S && ok; ++s) {
-        // every lane waits (acquire), the warp decides together (shuffles follow)
-        ok = __all_sync(0xffffffffu, mbar_wait(&bars[s], 0, &abort_flag, a.err));
-        if (!ok) break;
-        const uint8_t* stg = st + (size_t)s * kGvStage;
-        uint32_t A[4], B[4];
-        int gs;
-        load_stage_regs(xp, gsum, s, gl, A, B, gs);
+    // the token's activation row -> MoE A8 codes (s = max|x| / 127, 0 -> 1,
+    // q = rne(x / s)), computed by every CTA of the token from the f32 row
+    const float* xr = a.x + (size_t)t * a.H;
+    float mx = 0.0f;
+    for (int i = threadIdx.x; i < a.H; i += kGvThreads) mx = fmaxf(mx, fabsf(xr[i]));
+    mx = gv_block_max(mx, red);
+    const float sx = mx == 0.0f ? 1.0f : __fdiv_rn(mx, 127.0f);
+    if (!isfinite(sx) && rt == 0 && threadIdx.x == 0) atomicOr(a.err, kErrNonFinite);
+    // Kp / 8 is a multiple of 32: whole warps take words or stop together
+    for (int wd = threadIdx.x; wd < Kp / 8; wd += kGvThreads) {
+        uint32_t lo = 0, hi = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int lr = (j < 4 ? 0 : 64) + 16 * warp + 4 * (j & 3) + rs;
-            const int acc = group_dot(stg, lr, gl, A, B, gs);
-            f[j] = fold_groups(f[j], acc, stg, lr, lane);
+            const int k = wd * 8 + j;
+            const uint32_t q = k < a.H ? (uint32_t)(quant_moe(xr[k], sx) & 0xFF) : 0u;
+            if (j < 4) lo |= q << (8 * j);
+            else hi |= q << (8 * (j - 4));
         }
+        put_word(m, wd, lo, hi);
     }
+    __syncthreads();
+    const bool ok = group_sums(m, S, &abort_flag, a.err);
+    __syncthreads();
+    if (threadIdx.x < 128) m.val[threadIdx.x] = __fmul_rn(fold_row(m, S, threadIdx.x), sx);
+    __syncthreads();
     // a stalled copy (flagged above) still arrives, so the counters stay consistent
-    if (ok && gl == 0) {
-        const float sx = a.s_x[t];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int c = rt * 64 + 16 * warp + 4 * j + rs;
-            if (c < a.I) {
-                const float g = __fmul_rn(f[j], sx), u = __fmul_rn(f[4 + j], sx);
-                const float d = __fadd_rn(1.0f, expf(-g));
-                a.middle[(size_t)asg * a.I + c] = __fmul_rn(__fdiv_rn(g, d), u);
-            }
+    if (ok && threadIdx.x < 64) {
+        const int c = rt * 64 + threadIdx.x;
+        if (c < a.I) {
+            const float g = m.val[threadIdx.x], u = m.val[64 + threadIdx.x];
+            const float d = __fadd_rn(1.0f, expf(-g));
+            a.middle[(size_t)asg * a.I + c] = __fmul_rn(__fdiv_rn(g, d), u);
         }
     }
     if (!last_arrival(&a.counters[asg], gridDim.y)) return;
-    // requantise the assignment's middle row (MoE A8: s = max|x| / 127, q = rne(x / s))
-    __shared__ float red[kGvThreads / 32];
+    // requantise the assignment's middle row (MoE A8)
     const float* mrow = a.middle + (size_t)asg * a.I;
-    float m = 0.0f;
-    for (int c = threadIdx.x; c < a.I; c += blockDim.x) m = fmaxf(m, fabsf(__ldcg(mrow + c)));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[warp] = m;
-    __syncthreads();
-    m = red[0];
-    for (int i = 1; i < kGvThreads / 32; ++i) m = fmaxf(m, red[i]);
-    const float sc = m == 0.0f ? 1.0f : __fdiv_rn(m, 127.0f);
+    float mm = 0.0f;
+    for (int c = threadIdx.x; c < a.I; c += kGvThreads) mm = fmaxf(mm, fabsf(__ldcg(mrow + c)));
+    mm = gv_block_max(mm, red);
+    const float sc = mm == 0.0f ? 1.0f : __fdiv_rn(mm, 127.0f);
     if (threadIdx.x == 0) a.s_m[asg] = sc;
     int8_t* qrow = a.q_m + (size_t)asg * a.ld_qm;
-    for (int c = threadIdx.x; c < a.ld_qm; c += blockDim.x) {
-        int q = 0;
-        if (c < a.I) {
-            q = __float2int_rn(__fdiv_rn(__ldcg(mrow + c), sc));
-            q = q > 127 ? 127 : (q < -127 ? -127 : q);
-        }
-        qrow[c] = (int8_t)q;
-    }
+    for (int c = threadIdx.x; c < a.ld_qm; c += kGvThreads)
+        qrow[c] = (int8_t)(c < a.I ? quant_moe(__ldcg(mrow + c), sc) : 0);
 }
 
 __global__ void __launch_bounds__(kGvThreads) gemv_down_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
-    const int S = a.dn_stages, Kp = S * 256;
-    uint8_t* st = sm;
-    uint32_t* xp = reinterpret_cast<uint32_t*>(sm + (size_t)S * kGvStage);
-    int* gsum = reinterpret_cast<int*>(xp + Kp / 4);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(gsum + Kp / 32);
     __shared__ int abort_flag;
+    const int S = a.dn_stages, Kp = S * 256;
+    const GvSmem m = gv_smem(sm, S);
     const int asg = blockIdx.x, dt = blockIdx.y, t = asg / a.k;
     const float w = a.routes[asg];
     const int e = a.ids[asg];
     const bool valid = e >= 0 && e < a.E;
     const bool kept = w > 0.0f && valid;
     if (w > 0.0f && !valid && threadIdx.x == 0) atomicOr(a.err, kErrBadExpert);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gl = lane & 7, rs = lane >> 3;
     if (kept) {
         if (threadIdx.x == 0) {
             abort_flag = 0;
-            for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+            for (int s = 0; s < S; ++s) mbar_init(&m.bars[s], 1);
             fence_barrier_init();
         }
         __syncthreads();
         if (threadIdx.x == 0)
-            issue_stages(st, bars,
-                         a.dn_w + (size_t)e * a.dn_expert_stride + (size_t)dt * a.dn_tile_stride,
+            issue_stages(m, a.dn_w + (size_t)e * a.dn_expert_stride + (size_t)dt * a.dn_tile_stride,
                          a.dn_stage_stride, S);
-        stage_activation(a.q_m + (size_t)asg * a.ld_qm, Kp, xp, gsum);
-        __syncthreads();
-        // warp w: output rows 32w + 4j + rs of the tile
-        float f[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) f[j] = 0.0f;
-        bool ok = true;
-        for (int s = 0; s < S && ok; ++s) {
-            ok = __all_sync(0xffffffffu, mbar_wait(&bars[s], 0, &abort_flag, a.err));
-            if (!ok) break;
-            const uint8_t* stg = st + (size_t)s * kGvStage;
-            uint32_t A[4], B[4];
-            int gs;
-            load_stage_regs(xp, gsum, s, gl, A, B, gs);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int lr = 32 * warp + 4 * j + rs;
-                const int acc = group_dot(stg, lr, gl, A, B, gs);
-                f[j] = fold_groups(f[j], acc, stg, lr, lane);
-            }
+        const uint2* qr = reinterpret_cast<const uint2*>(a.q_m + (size_t)asg * a.ld_qm);
+        for (int wd = threadIdx.x; wd < Kp / 8; wd += kGvThreads) {
+            const uint2 v = __ldcg(qr + wd);
+            put_word(m, wd, v.x, v.y);
         }
-        if (ok && gl == 0) {
-            const float sm_ = a.s_m[asg];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int c = dt * 128 + 32 * warp + 4 * j + rs;
-                if (c < a.H) a.y[(size_t)asg * a.H + c] = __fmul_rn(f[j], sm_);
-            }
+        __syncthreads();
+        const bool ok = group_sums(m, S, &abort_flag, a.err);
+        __syncthreads();
+        if (ok && threadIdx.x < 128) {
+            const int c = dt * 128 + threadIdx.x;
+            const float f = fold_row(m, S, threadIdx.x);
+            if (c < a.H) a.y[(size_t)asg * a.H + c] = __fmul_rn(f, a.s_m[asg]);
         }
     }
     if (!last_arrival(&a.counters[a.dn_counter_base + t * gridDim.y + dt], a.k)) return;
     // combine the token's kept ranks in rank order, then the residual
-    for (int c = dt * 128 + threadIdx.x; c < min(a.H, dt * 128 + 128); c += blockDim.x) {
+    for (int c = dt * 128 + threadIdx.x; c < min(a.H, dt * 128 + 128); c += kGvThreads) {
         float acc = 0.0f;
         for (int r = 0; r < a.k; ++r) {
             const int as = t * a.k + r;
@@ -288,8 +311,8 @@ __global__ void __launch_bounds__(kGvThreads) gemv_down_kernel(const GemvArgs a)
 }
 
 size_t gemv_smem_bytes(int S) {
-    const size_t Kp = (size_t)S * 256;
-    return (size_t)S * kGvStage + Kp + (Kp / 32) * 4 + (size_t)S * 8;
+    const size_t Kp = (size_t)S * 256, G = (size_t)S * 8;
+    return (size_t)S * kGvStage + Kp + G * 4 + 128 * (G + 8) * 4 + 128 * 4 + (size_t)S * 8;
 }
 
 int launch_gemv(const GemvArgs& a, int part, cudaStream_t s) {

@@ -113,9 +113,7 @@ struct GemvArgs {
     const int32_t* ids;       // [T][k]
     const float* routes;      // [T][k]
     int T, k, E, H, I;
-    const int8_t* q_x;        // [T][ld_qx] MoE A8 codes of the tokens
-    const float* s_x;         // [T]
-    int ld_qx;
+    const float* x;           // [T][H] activations (quantised in the gate/up kernel)
     const uint8_t* gu_w;      // packed gate|up bank
     size_t gu_expert_stride, gu_tile_stride, gu_stage_stride;
     int gu_stages;            // 256-k stages of the gate/up K (= H padded)

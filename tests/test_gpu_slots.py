@@ -68,7 +68,9 @@ def test_pager_matches_resident_layer(cuda, tmp_path, slots_n, T):
     spec = S.small_spec("c2", experts=32)
     layer = S.make_layer(spec, seed=31)
     be = Backend(device=0, max_rows=T * spec.top)
-    moe = be.load_moe(layer.gate, layer.down, spec.top)
+    # exact group sums in both GEMMs: the resident small-batch path and the
+    # pager's expert rows then compute the same values whatever the row count
+    moe = be.load_moe(layer.gate, layer.down, spec.top, exact=True)
     router = be.router(layer.router, spec.top, layer.bias)
     g = Geometry(native_version=moe.blob_version(), layers=1, experts=spec.experts,
                  hidden=spec.hidden, intermediate=spec.inter, down_bits=4)
@@ -77,7 +79,7 @@ def test_pager_matches_resident_layer(cuda, tmp_path, slots_n, T):
         w.write(0, e, moe.export(e))
     w.finish()
     store = Store(tmp_path, g, [])
-    pager = Pager(be, store, 0, slots_n, spec.top, L.W4_G32_FP16, max_rows=T)
+    pager = Pager(be, store, 0, slots_n, spec.top, L.W4_G32_FP16_EXACT, max_rows=T)
     for step in range(3):
         x = S.make_input(spec, T, seed=40 + step)
         res = S.make_input(spec, T, seed=50 + step, stream=5)
