@@ -90,6 +90,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     }
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while its predecessor still runs. pdl_wait() blocks
+// until the predecessor grid has completed with its memory visible (it returns
+// at once when there is no such predecessor); pdl_trigger() lets this grid's
+// own dependents begin to launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Generic-proxy smem writes -> visible to the async proxy (tensor core reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -106,18 +106,18 @@ __device__ __forceinline__ void issue_stages(const GvSmem& m, const uint8_t* til
 
 // Phase A: items (stage s, rows 4q..4q+3), lane = (row rs = lane >> 3, logical
 // group gl = lane & 7); every group's exact sum goes to acc[row][8 s + gl].
-// Returns false when a stage never arrived (flagged).
+// The stages land together, so every lane first waits for all of them
+// (acquire) and the warp decides together; the item loop then runs without
+// waits. Returns false when a stage never arrived (flagged).
 __device__ __forceinline__ bool group_sums(const GvSmem& m, int S, int* abort_flag,
                                            uint32_t* err) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gl = lane & 7, rs = lane >> 3;
-    int waited = -1;
+    bool arrived = true;
+    for (int s = 0; s < S; ++s) arrived = mbar_wait(&m.bars[s], 0, abort_flag, err) && arrived;
+    if (!__all_sync(0xffffffffu, arrived)) return false;
+#pragma unroll 4
     for (int it = warp; it < S * 32; it += kGvWarps) {
         const int s = it >> 5, lr = (it & 31) * 4 + rs;
-        if (s != waited) {
-            // every lane waits (acquire); the warp decides together
-            if (!__all_sync(0xffffffffu, mbar_wait(&m.bars[s], 0, abort_flag, err))) return false;
-            waited = s;
-        }
         const uint4* xq = reinterpret_cast<const uint4*>(m.xp + (s * 8 + gl) * 8);
         const uint4 u0 = xq[0], u1 = xq[1];
         const uint32_t A[4] = {u0.x, u0.z, u1.x, u1.z}, B[4] = {u0.y, u0.w, u1.y, u1.w};
@@ -195,23 +195,12 @@ __global__ void __launch_bounds__(kGvThreads) gemv_gateup_kernel(const GemvArgs 
     const int S = a.gu_stages, Kp = S * 256;
     const GvSmem m = gv_smem(sm, S);
     const int asg = blockIdx.x, rt = blockIdx.y, t = asg / a.k;
-    const float w = a.routes[asg];
-    const int e = a.ids[asg];
-    if (!(w >= 0.0f) && rt == 0 && threadIdx.x == 0) atomicOr(a.err, kErrBadRoute);  // < 0 or NaN
-    if (!(w > 0.0f)) return;  // skipped route: its middle row is never read
-    if (e < 0 || e >= a.E) {
-        if (threadIdx.x == 0) atomicOr(a.err, kErrBadExpert);
-        return;
-    }
+    // prologue, independent of the routing: barriers and the activation codes
     if (threadIdx.x == 0) {
         abort_flag = 0;
         for (int s = 0; s < S; ++s) mbar_init(&m.bars[s], 1);
         fence_barrier_init();
     }
-    __syncthreads();
-    if (threadIdx.x == 0)
-        issue_stages(m, a.gu_w + (size_t)e * a.gu_expert_stride + (size_t)rt * a.gu_tile_stride,
-                     a.gu_stage_stride, S);
     // the token's activation row -> MoE A8 codes (s = max|x| / 127, 0 -> 1,
     // q = rne(x / s)), computed by every CTA of the token from the f32 row
     const float* xr = a.x + (size_t)t * a.H;
@@ -232,7 +221,23 @@ __global__ void __launch_bounds__(kGvThreads) gemv_gateup_kernel(const GemvArgs 
         }
         put_word(m, wd, lo, hi);
     }
-    __syncthreads();
+    // the routing comes from the preceding grid (the router, when this kernel
+    // is its programmatic dependent); once it is visible, the down kernel may
+    // launch and read it too
+    pdl_wait();
+    pdl_trigger();
+    const float w = a.routes[asg];
+    const int e = a.ids[asg];
+    if (!(w >= 0.0f) && rt == 0 && threadIdx.x == 0) atomicOr(a.err, kErrBadRoute);  // < 0 or NaN
+    if (!(w > 0.0f)) return;  // skipped route: its middle row is never read
+    if (e < 0 || e >= a.E) {
+        if (threadIdx.x == 0) atomicOr(a.err, kErrBadExpert);
+        return;
+    }
+    __syncthreads();  // barriers initialised, activation codes staged
+    if (threadIdx.x == 0)
+        issue_stages(m, a.gu_w + (size_t)e * a.gu_expert_stride + (size_t)rt * a.gu_tile_stride,
+                     a.gu_stage_stride, S);
     const bool ok = group_sums(m, S, &abort_flag, a.err);
     __syncthreads();
     if (threadIdx.x < 128) m.val[threadIdx.x] = __fmul_rn(fold_row(m, S, threadIdx.x), sx);
@@ -270,16 +275,19 @@ __global__ void __launch_bounds__(kGvThreads) gemv_down_kernel(const GemvArgs a)
     const bool valid = e >= 0 && e < a.E;
     const bool kept = w > 0.0f && valid;
     if (w > 0.0f && !valid && threadIdx.x == 0) atomicOr(a.err, kErrBadExpert);
+    // the routing was visible before the gate/up grid let this grid launch, so
+    // the weights stream in while the gate/up kernel still runs; its outputs
+    // (middle codes and scales) are read only after pdl_wait
+    if (kept && threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < S; ++s) mbar_init(&m.bars[s], 1);
+        fence_barrier_init();
+        issue_stages(m, a.dn_w + (size_t)e * a.dn_expert_stride + (size_t)dt * a.dn_tile_stride,
+                     a.dn_stage_stride, S);
+    }
+    pdl_wait();
     if (kept) {
-        if (threadIdx.x == 0) {
-            abort_flag = 0;
-            for (int s = 0; s < S; ++s) mbar_init(&m.bars[s], 1);
-            fence_barrier_init();
-        }
         __syncthreads();
-        if (threadIdx.x == 0)
-            issue_stages(m, a.dn_w + (size_t)e * a.dn_expert_stride + (size_t)dt * a.dn_tile_stride,
-                         a.dn_stage_stride, S);
         const uint2* qr = reinterpret_cast<const uint2*>(a.q_m + (size_t)asg * a.ld_qm);
         for (int wd = threadIdx.x; wd < Kp / 8; wd += kGvThreads) {
             const uint2 v = __ldcg(qr + wd);
@@ -315,22 +323,26 @@ size_t gemv_smem_bytes(int S) {
     return (size_t)S * kGvStage + Kp + G * 4 + 128 * (G + 8) * 4 + 128 * 4 + (size_t)S * 8;
 }
 
+// Both kernels launch as programmatic dependents of the kernel before them
+// (their prologues overlap its tail); each waits (pdl_wait) before reading
+// what that kernel wrote.
 int launch_gemv(const GemvArgs& a, int part, cudaStream_t s) {
     const int n = a.T * a.k;
-    if (part == 0) {
-        const size_t smg = gemv_smem_bytes(a.gu_stages);
-        if (smg > kGemvMaxSmem) return -1;
-        cudaFuncSetAttribute(gemv_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smg);
-        gemv_gateup_kernel<<<dim3(n, (a.I + 63) / 64), kGvThreads, smg, s>>>(a);
-    } else {
-        const size_t smd = gemv_smem_bytes(a.dn_stages);
-        if (smd > kGemvMaxSmem) return -1;
-        cudaFuncSetAttribute(gemv_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smd);
-        gemv_down_kernel<<<dim3(n, (a.H + 127) / 128), kGvThreads, smd, s>>>(a);
-    }
-    return 0;
+    const size_t smem = gemv_smem_bytes(part == 0 ? a.gu_stages : a.dn_stages);
+    if (smem > kGemvMaxSmem) return -1;
+    void (*kern)(const GemvArgs) = part == 0 ? gemv_gateup_kernel : gemv_down_kernel;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = part == 0 ? dim3(n, (a.I + 63) / 64) : dim3(n, (a.H + 127) / 128);
+    cfg.blockDim = dim3(kGvThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a) == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace moe

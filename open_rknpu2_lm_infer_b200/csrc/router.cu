@@ -83,6 +83,10 @@ constexpr int kDecEB = 8;
 template <bool TF32>
 __global__ void __launch_bounds__(128) router_decode_kernel(const RouterArgs a) {
     extern __shared__ __align__(16) float rsm[];
+    // a small-batch layer launches its gate/up kernel as a programmatic
+    // dependent: it may start its own prologue now (it waits for this grid
+    // before reading the routing)
+    pdl_trigger();
     const int H = a.H;
     const int stride = H + 16;  // padded rows: the two rows of a warp use different banks
     float* w_s = rsm;                     // [8][stride]
