@@ -1210,7 +1210,9 @@ static int route_impl(moe_b200_workspace* ws, const moe_b200_router* r, int rows
     a.weights = d_routes;
     a.err = ws->err;
     launch_router(a, s);
-    ws->launches += r->order == MOE_B200_ROUTER_SEQUENTIAL ? 2 : 1;
+    // the decode-sized router routes in its last CTA; the others launch a
+    // separate routing kernel
+    ws->launches += (r->order == MOE_B200_ROUTER_SEQUENTIAL || rows >= 16) ? 2 : 1;
     return cuda_rc(cudaPeekAtLastError());
 }
 

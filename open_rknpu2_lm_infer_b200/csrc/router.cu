@@ -22,8 +22,6 @@
 
 namespace moe {
 
-constexpr int kRouterThreads = 256;
-
 // The 16 lanes of one (token, expert) dot live in 16 consecutive threads
 // (j = tid & 15); reduce them with the fixed tree of vaddq/vaddvq:
 // (l[j]+l[j+4]) + (l[j+8]+l[j+12]), then (v0+v1)+(v2+v3). Result in lane j=0.
@@ -127,73 +125,88 @@ __global__ void __launch_bounds__(128) router_decode_kernel(const RouterArgs a) 
     finish_tile(a, t, t, 1);
 }
 
-// Prefill-sized router: TT tokens x EB weight rows per CTA (grid (ceil(T/TT),
-// ceil(Ew/EB))), 256 threads = 16 lanes x 16 groups; a group owns EB/16 rows
-// for all TT tokens. Hidden dimension streamed in chunks of kCh through a
-// kStg-deep cp.async ring.
-template <int TT, int EB, bool TF32>
-__global__ void __launch_bounds__(kRouterThreads) router_tile_kernel(const RouterArgs a) {
-    constexpr int EPG = EB / 16;
-    constexpr int kCh = 128, kStg = 4, kWS = kCh + 16;
-    constexpr int kStageF = EB * kWS + TT * kCh;
+// Prefill-sized router (logits only; the routing runs in route_rows_kernel).
+// A thread owns TT tokens x 4 weight rows x 4 NEON lanes (j = 4q + c): one
+// 16-byte shared-memory read per token and per row covers the 4 lanes' next
+// element, and the 64 (or 32) chains per thread are independent. A warp =
+// 4 lane groups q x 8 row groups s (rows s, s + 8, s + 16, s + 24 of the
+// warp's 32); a CTA = WY x WX warps = WY*TT tokens x WX*32 rows. The hidden
+// dimension streams in chunks of KCH through an STG-deep cp.async ring; row
+// strides of KCH + 4 floats keep the 16-byte reads conflict-free. The fixed
+// reduction tree of the reference's lanes, (l[c] + l[c+4]) + (l[c+8] +
+// l[c+12]) then (v0 + v1) + (v2 + v3), pairs lane groups q ^ 1, then q ^ 2.
+template <int TT, int WY, int WX, int KCH, int STG, bool TF32>
+__global__ void __launch_bounds__(32 * WY * WX) router_tile4_kernel(const RouterArgs a) {
+    constexpr int TTc = TT * WY, EBc = 32 * WX;
+    constexpr int WS = KCH + 4, XS = KCH + 4;
+    constexpr int kStageF = EBc * WS + TTc * XS;
+    constexpr int NTH = 32 * WY * WX;
     extern __shared__ __align__(16) float rsm[];
     const int H = a.H;
-    const int tid = threadIdx.x, j = tid & 15, g = tid >> 4;
-    const int t0 = blockIdx.x * TT, e0 = blockIdx.y * EB;
-    const int ne = min(EB, a.Ew - e0), nt = min(TT, a.T - t0);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int q = lane >> 3, sg = lane & 7;
+    const int wy = warp / WX, wx = warp % WX;
+    const int t0 = blockIdx.x * TTc, e0 = blockIdx.y * EBc;
+    const int ne = min(EBc, a.Ew - e0), nt = min(TTc, a.T - t0);
     const int H16 = (H / 16) * 16;
-    const int nchunks = (H16 + kCh - 1) / kCh;
-    const bool vec = (H & 3) == 0;
+    const int nchunks = (H16 + KCH - 1) / KCH;
 
     auto load_chunk = [&](int c) {
-        float* w_s = rsm + (c % kStg) * kStageF;
-        float* x_s = w_s + EB * kWS;
-        const int h0 = c * kCh;
-        const int q4 = min(kCh, H16 - h0) / 4;
-        for (int idx = tid; idx < (EB + TT) * (kCh / 4); idx += kRouterThreads) {
-            const int r = idx / (kCh / 4), q = idx % (kCh / 4);
-            if (q >= q4) continue;
-            const bool isw = r < EB;
-            if (isw ? r >= ne : (r - EB) >= nt) continue;
-            const float* src = isw ? a.w + (size_t)(e0 + r) * H + h0 + 4 * q
-                                   : a.x + (size_t)(t0 + r - EB) * H + h0 + 4 * q;
-            float* dst = isw ? w_s + r * kWS + 4 * q : x_s + (r - EB) * kCh + 4 * q;
-            if (vec) {
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src));
-            } else {
-                for (int c2 = 0; c2 < 4; ++c2) dst[c2] = src[c2];
-            }
+        float* w_s = rsm + (c % STG) * kStageF;
+        float* x_s = w_s + EBc * WS;
+        const int h0 = c * KCH;
+        const int q4 = min(KCH, H16 - h0) / 4;
+        for (int idx = tid; idx < (EBc + TTc) * (KCH / 4); idx += NTH) {
+            const int r = idx / (KCH / 4), qq = idx % (KCH / 4);
+            if (qq >= q4) continue;
+            const bool isw = r < EBc;
+            if (isw ? r >= ne : (r - EBc) >= nt) continue;
+            const float* src = isw ? a.w + (size_t)(e0 + r) * H + h0 + 4 * qq
+                                   : a.x + (size_t)(t0 + r - EBc) * H + h0 + 4 * qq;
+            float* dst = isw ? w_s + r * WS + 4 * qq : x_s + (r - EBc) * XS + 4 * qq;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src));
         }
     };
 
-    float acc[TT][EPG];
+    float acc[TT][4][4];
 #pragma unroll
     for (int t = 0; t < TT; ++t)
 #pragma unroll
-        for (int m = 0; m < EPG; ++m) acc[t][m] = 0.0f;
+        for (int m = 0; m < 4; ++m)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[t][m][c] = 0.0f;
 
-    for (int c = 0; c < kStg - 1; ++c) {
+    for (int c = 0; c < STG - 1; ++c) {
         if (c < nchunks) load_chunk(c);
         asm volatile("cp.async.commit_group;" ::: "memory");
     }
     for (int c = 0; c < nchunks; ++c) {
-        asm volatile("cp.async.wait_group %0;" ::"n"(kStg - 2) : "memory");
+        asm volatile("cp.async.wait_group %0;" ::"n"(STG - 2) : "memory");
         __syncthreads();
-        if (c + kStg - 1 < nchunks) load_chunk(c + kStg - 1);
+        if (c + STG - 1 < nchunks) load_chunk(c + STG - 1);
         asm volatile("cp.async.commit_group;" ::: "memory");
-        const float* w_s = rsm + (c % kStg) * kStageF;
-        const float* x_s = w_s + EB * kWS;
-        const int steps = min(kCh, H16 - c * kCh) / 16;
-#pragma unroll 2
+        const float* w_s = rsm + (c % STG) * kStageF + (wx * 32 + sg) * WS + 4 * q;
+        const float* x_s = rsm + (c % STG) * kStageF + EBc * WS + (wy * TT) * XS + 4 * q;
+        const int steps = min(KCH, H16 - c * KCH) / 16;
+#pragma unroll 1
         for (int i = 0; i < steps; ++i) {
-            float wv[EPG];
-#pragma unroll
-            for (int m = 0; m < EPG; ++m) wv[m] = w_s[(g + 16 * m) * kWS + 16 * i + j];
+            float4 xv[TT];
 #pragma unroll
             for (int t = 0; t < TT; ++t) {
-                const float xv = xval<TF32>(x_s[t * kCh + 16 * i + j]);
+                xv[t] = *reinterpret_cast<const float4*>(x_s + t * XS + 16 * i);
+                xv[t] = make_float4(xval<TF32>(xv[t].x), xval<TF32>(xv[t].y), xval<TF32>(xv[t].z),
+                                    xval<TF32>(xv[t].w));
+            }
 #pragma unroll
-                for (int m = 0; m < EPG; ++m) acc[t][m] = __fmaf_rn(wv[m], xv, acc[t][m]);
+            for (int m = 0; m < 4; ++m) {
+                const float4 wv = *reinterpret_cast<const float4*>(w_s + (8 * m) * WS + 16 * i);
+#pragma unroll
+                for (int t = 0; t < TT; ++t) {
+                    acc[t][m][0] = __fmaf_rn(wv.x, xv[t].x, acc[t][m][0]);
+                    acc[t][m][1] = __fmaf_rn(wv.y, xv[t].y, acc[t][m][1]);
+                    acc[t][m][2] = __fmaf_rn(wv.z, xv[t].z, acc[t][m][2]);
+                    acc[t][m][3] = __fmaf_rn(wv.w, xv[t].w, acc[t][m][3]);
+                }
             }
         }
     }
@@ -201,16 +214,21 @@ __global__ void __launch_bounds__(kRouterThreads) router_tile_kernel(const Route
 #pragma unroll
     for (int t = 0; t < TT; ++t) {
 #pragma unroll
-        for (int m = 0; m < EPG; ++m) {
-            const float q = neon16_tree(acc[t][m]);
-            const int e = g + 16 * m;
-            if (j == 0 && t < nt && e < ne)
-                a.logits[(size_t)(t0 + t) * a.Ew + e0 + e] = neon16_finish<TF32>(
-                    q, a.w + (size_t)(e0 + e) * H, a.x + (size_t)(t0 + t) * H, H16, H, a.bias,
-                    e0 + e, a.E);
+        for (int m = 0; m < 4; ++m) {
+            float v[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float s1 = __fadd_rn(acc[t][m][c], __shfl_xor_sync(0xffffffffu, acc[t][m][c], 8));
+                v[c] = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, 16));
+            }
+            const float tot = __fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3]));
+            const int tl = wy * TT + t, el = wx * 32 + sg + 8 * m;
+            if (q == 0 && tl < nt && el < ne)
+                a.logits[(size_t)(t0 + tl) * a.Ew + e0 + el] = neon16_finish<TF32>(
+                    tot, a.w + (size_t)(e0 + el) * H, a.x + (size_t)(t0 + tl) * H, H16, H, a.bias,
+                    e0 + el, a.E);
         }
     }
-    finish_tile(a, blockIdx.x, t0, nt);
 }
 
 // x86 order: one thread per (token, row), sequential sum += w*x with a
@@ -427,6 +445,16 @@ __device__ void grouped_row(const float* row, const RouterArgs& a, int32_t* ids,
     }
 }
 
+template <int TT, int WY, int WX, int KCH, int STG, bool TF32>
+static void launch_tile4(const RouterArgs& a, cudaStream_t s) {
+    constexpr int TTc = TT * WY, EBc = 32 * WX;
+    const size_t smem = sizeof(float) * STG * (EBc * (KCH + 4) + TTc * (KCH + 4));
+    auto k = router_tile4_kernel<TT, WY, WX, KCH, STG, TF32>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dim3 grid((a.T + TTc - 1) / TTc, (a.Ew + EBc - 1) / EBc);
+    k<<<grid, 32 * WY * WX, smem, s>>>(a);
+}
+
 template <bool TF32>
 static int launch_router_t(const RouterArgs& a, cudaStream_t s) {
     if (a.T < 16) {
@@ -438,12 +466,13 @@ static int launch_router_t(const RouterArgs& a, cudaStream_t s) {
         router_decode_kernel<TF32><<<grid, 128, smem, s>>>(a);
         return 0;
     }
-    constexpr int TT = 16, EB = 32;
-    const size_t smem = sizeof(float) * 4 * (EB * (128 + 16) + TT * 128);
-    cudaFuncSetAttribute(router_tile_kernel<TT, EB, TF32>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    dim3 grid((a.T + TT - 1) / TT, (a.Ew + EB - 1) / EB);
-    router_tile_kernel<TT, EB, TF32><<<grid, kRouterThreads, smem, s>>>(a);
+    // logits, then one warp per token for the routing (a separate launch: the
+    // routing tail of a fused last-CTA step cost more than the launch)
+    if (a.T <= 1024)
+        launch_tile4<2, 4, 2, 64, 4, TF32>(a, s);
+    else
+        launch_tile4<4, 4, 1, 64, 4, TF32>(a, s);
+    route_rows_kernel<<<(a.T * 32 + 255) / 256, 256, 0, s>>>(a);
     return 0;
 }
 
