@@ -332,6 +332,36 @@ int moe_b200_ep_expert_rows(moe_b200_workspace *ws, const moe_b200_weights *w, i
                             const int8_t *d_q, const float *d_scale, const int32_t *d_expert,
                             float *d_y, void *stream);
 
+/* Device-initiated exchange over NVLink peer memory (replaces the caller's
+ * NCCL all-to-alls and their host-side split sizes). Each rank creates one
+ * exchange (up to cap rows from any one source, rows of row_bytes =
+ * moe_b200_workspace_row_bytes of the token-side workspace, hidden H),
+ * shares its MOE_B200_EP_HANDLE_BYTES handle with the other ranks (any host
+ * transport), connects with all world handles in rank order, and then per
+ * layer step calls moe_b200_ep_exchange_step after moe_b200_ep_pack: the
+ * packed rows go straight into their owners' memory, the owner runs its
+ * experts (ws / w: the expert-side workspace with max_rows * top >= world *
+ * cap, and the rank's bank), and the expert rows come back into this rank's
+ * y_back at the packed positions, ready for moe_b200_ep_combine. No host
+ * synchronisation; every wait for a peer gives up after about 2 s with
+ * MOE_B200_ERR_DEVICE_TIMEOUT (moe_b200_ep_exchange_status). Every rank
+ * must call step the same number of times. */
+#define MOE_B200_EP_HANDLE_BYTES 64
+typedef struct moe_b200_ep_exchange moe_b200_ep_exchange;
+moe_b200_ep_exchange *moe_b200_ep_exchange_create(int32_t device, int32_t world, int32_t rank,
+                                                  int32_t cap, int64_t row_bytes, int32_t hidden);
+int moe_b200_ep_exchange_handle(const moe_b200_ep_exchange *ex, void *handle);
+int moe_b200_ep_exchange_connect(moe_b200_ep_exchange *ex, const void *handles);
+int moe_b200_ep_exchange_step(moe_b200_ep_exchange *ex, moe_b200_workspace *ws,
+                              const moe_b200_weights *w, const int8_t *d_send_q,
+                              const float *d_send_scale, const int32_t *d_send_expert,
+                              const int32_t *d_send_counts, void *stream);
+/* [cap][hidden] f32: the returned expert rows at this rank's packed positions. */
+const float *moe_b200_ep_exchange_y_back(const moe_b200_ep_exchange *ex);
+/* Synchronises the device, reads and clears the exchange's status word. */
+int moe_b200_ep_exchange_status(moe_b200_ep_exchange *ex);
+void moe_b200_ep_exchange_free(moe_b200_ep_exchange *ex);
+
 /* Token owner, step 3: out[t] = (residual[t] +) sum over ranks r ascending of
  * fma(y_back[pos[t*k+r]], routes[t,r]) for kept assignments, the order of the
  * single-device combine. */

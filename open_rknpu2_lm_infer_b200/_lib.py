@@ -34,6 +34,7 @@ ROUTER_SEQUENTIAL = 1
 ROUTER_TF32 = 2
 ROUTE_SOFTMAX = 0
 ROUTE_GROUPED_SIGMOID = 1
+EP_HANDLE_BYTES = 64
 SHARED_JOINT = 0
 SHARED_DENSE = 1
 
@@ -128,6 +129,16 @@ SIGNATURES = [
     ("moe_b200_workspace_profile_read", C.c_int, [C.c_void_p, C.c_int32, C.POINTER(Timings)]),
     ("moe_b200_workspace_launches", C.c_int64, [C.c_void_p]),
     ("moe_b200_workspace_row_bytes", C.c_int64, [C.c_void_p]),
+    ("moe_b200_ep_exchange_create", C.c_void_p,
+     [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int64, C.c_int32]),
+    ("moe_b200_ep_exchange_handle", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("moe_b200_ep_exchange_connect", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("moe_b200_ep_exchange_step", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+      C.c_void_p]),
+    ("moe_b200_ep_exchange_y_back", C.c_void_p, [C.c_void_p]),
+    ("moe_b200_ep_exchange_status", C.c_int, [C.c_void_p]),
+    ("moe_b200_ep_exchange_free", None, [C.c_void_p]),
     ("moe_b200_graph_create", C.c_void_p,
      [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("moe_b200_graph_launch", C.c_int, [C.c_void_p, C.c_void_p]),

@@ -16,6 +16,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/moe_b200.h"
@@ -1350,19 +1351,12 @@ int moe_b200_ep_pack(moe_b200_workspace* ws, int32_t rows, const float* d_x, con
     return cuda_rc(cudaPeekAtLastError());
 }
 
-int moe_b200_ep_expert_rows(moe_b200_workspace* ws, const moe_b200_weights* w, int32_t n,
-                            const int8_t* d_q, const float* d_scale, const int32_t* d_expert,
-                            float* d_y, void* stream) {
-    int rc = compatible(ws, w);
-    if (rc) return rc;
-    if (w->shared) return MOE_B200_ERR_UNSUPPORTED;  // the owner computes the shared expert
-    if (n < 0) return MOE_B200_ERR_INVALID;
-    if (n > ws->n_max) return MOE_B200_ERR_CAPACITY;
-    if (n == 0) return MOE_B200_OK;
-    if (!d_q || !d_scale || !d_expert || !d_y || !aligned16(d_q) || !aligned16(d_y))
-        return MOE_B200_ERR_INVALID;
-    DeviceGuard guard(ws->device);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
+// Expert side of the exchange on rows [n] (row stride ws->Kh): grouped by
+// local expert, gate/up, requant, down into d_y in the received order. mask
+// (may be null): rows with mask <= 0 are padding and skipped.
+static int ep_expert_rows_impl(moe_b200_workspace* ws, const moe_b200_weights* w, int n,
+                               const int8_t* d_q, const float* d_scale, const int32_t* d_expert,
+                               const float* d_mask, float* d_y, cudaStream_t s) {
     const int E = ws->E, H = ws->H, I = ws->I;
     ws->launches += 6;
     // stage events of the profiling ring: schedule+gather, gate/up, requant, down
@@ -1372,9 +1366,9 @@ int moe_b200_ep_expert_rows(moe_b200_workspace* ws, const moe_b200_weights* w, i
     };
     mark(0);
     mark(1);
-    // rows -> permuted order by local expert (every row kept, one expert each)
-    launch_route_count(d_expert, nullptr, n, E, ws->hist, ws->err, s);
-    launch_route_scatter(d_expert, nullptr, n, E, ws->hist, ws->offsets, ws->perm, ws->pos,
+    // rows -> permuted order by local expert (every kept row, one expert each)
+    launch_route_count(d_expert, d_mask, n, E, ws->hist, ws->err, s);
+    launch_route_scatter(d_expert, d_mask, n, E, ws->hist, ws->offsets, ws->perm, ws->pos,
                          nullptr, n, s);
     launch_ep_gather_rows(d_q, d_scale, ws->pos, n, ws->Kh, ws->a_perm, ws->s_perm, s);
     mark(2);
@@ -1401,6 +1395,194 @@ int moe_b200_ep_expert_rows(moe_b200_workspace* ws, const moe_b200_weights* w, i
     mark(7);
     mark(8);
     return cuda_rc(cudaPeekAtLastError());
+}
+
+int moe_b200_ep_expert_rows(moe_b200_workspace* ws, const moe_b200_weights* w, int32_t n,
+                            const int8_t* d_q, const float* d_scale, const int32_t* d_expert,
+                            float* d_y, void* stream) {
+    int rc = compatible(ws, w);
+    if (rc) return rc;
+    if (w->shared) return MOE_B200_ERR_UNSUPPORTED;  // the owner computes the shared expert
+    if (n < 0) return MOE_B200_ERR_INVALID;
+    if (n > ws->n_max) return MOE_B200_ERR_CAPACITY;
+    if (n == 0) return MOE_B200_OK;
+    if (!d_q || !d_scale || !d_expert || !d_y || !aligned16(d_q) || !aligned16(d_y))
+        return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ws->device);
+    return ep_expert_rows_impl(ws, w, n, d_q, d_scale, d_expert, nullptr, d_y,
+                               static_cast<cudaStream_t>(stream));
+}
+
+// ---- device-initiated exchange (peer memory) --------------------------------
+
+struct moe_b200_ep_exchange {
+    int device = 0, world = 0, rank = 0, cap = 0, H = 0;
+    size_t row_bytes = 0, region_bytes = 0;
+    uint8_t* region = nullptr;          // this rank's exchange region (exported)
+    std::vector<uint8_t*> peers;        // every rank's region in this address space
+    uint8_t** d_peers = nullptr;
+    uint64_t* step = nullptr;
+    int* done = nullptr;
+    uint32_t* err = nullptr;
+    float* mask = nullptr;              // [world * cap]
+    float* y = nullptr;                 // [world * cap][H] expert rows of the received rows
+    ExchangeArgs args{};
+    bool connected = false;
+};
+
+moe_b200_ep_exchange* moe_b200_ep_exchange_create(int32_t device, int32_t world, int32_t rank,
+                                                  int32_t cap, int64_t row_bytes, int32_t hidden) {
+    if (world <= 0 || world > 64 || rank < 0 || rank >= world || cap <= 0 || hidden <= 0 ||
+        hidden % 4 || row_bytes <= 0 || row_bytes % 16)
+        return nullptr;
+    if (check_device(device, nullptr)) return nullptr;
+    DeviceGuard guard(device);
+    auto* ex = new moe_b200_ep_exchange();
+    ex->device = device;
+    ex->world = world;
+    ex->rank = rank;
+    ex->cap = cap;
+    ex->H = hidden;
+    ex->row_bytes = (size_t)row_bytes;
+    auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+    ExchangeArgs& a = ex->args;
+    const size_t wc = (size_t)world * cap;
+    size_t off = 0;
+    a.off_q = off;           off += al(wc * ex->row_bytes);
+    a.off_scale = off;       off += al(wc * 4);
+    a.off_expert = off;      off += al(wc * 4);
+    a.off_cnt = off;         off += al((size_t)world * 4);
+    a.off_base = off;        off += al((size_t)world * 4);
+    a.off_y = off;           off += al((size_t)cap * hidden * 4);
+    a.off_flag_rows = off;   off += al((size_t)world * 8);
+    a.off_flag_y = off;      off += al((size_t)world * 8);
+    ex->region_bytes = off;
+    void* p = nullptr;
+    bool ok = dev_alloc(&p, ex->region_bytes) == cudaSuccess;
+    ex->region = static_cast<uint8_t*>(p);
+    if (ok) ok = cudaMemset(ex->region, 0, ex->region_bytes) == cudaSuccess;
+    auto get = [&](auto** dst, size_t bytes) {
+        void* q = nullptr;
+        if (!ok || dev_alloc(&q, bytes) != cudaSuccess || cudaMemset(q, 0, bytes) != cudaSuccess) {
+            ok = false;
+            return;
+        }
+        *dst = static_cast<std::remove_pointer_t<std::remove_reference_t<decltype(dst)>>>(q);
+    };
+    get(&ex->d_peers, sizeof(uint8_t*) * world);
+    get(&ex->step, sizeof(uint64_t));
+    get(&ex->done, sizeof(int));
+    get(&ex->err, sizeof(uint32_t));
+    get(&ex->mask, sizeof(float) * wc);
+    get(&ex->y, sizeof(float) * wc * hidden);
+    if (!ok) {
+        moe_b200_ep_exchange_free(ex);
+        return nullptr;
+    }
+    ex->peers.assign(world, nullptr);
+    ex->peers[rank] = ex->region;
+    a.peers = ex->d_peers;
+    a.row_bytes = ex->row_bytes;
+    a.world = world;
+    a.rank = rank;
+    a.cap = cap;
+    a.H = hidden;
+    a.blocks = 64;
+    a.step = ex->step;
+    a.done = ex->done;
+    a.err = ex->err;
+    return ex;
+}
+
+int moe_b200_ep_exchange_handle(const moe_b200_ep_exchange* ex, void* handle) {
+    if (!ex || !handle) return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ex->device);
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, ex->region);
+    if (e != cudaSuccess) return cuda_rc(e);
+    static_assert(sizeof(h) == MOE_B200_EP_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle, &h, sizeof(h));
+    return MOE_B200_OK;
+}
+
+int moe_b200_ep_exchange_connect(moe_b200_ep_exchange* ex, const void* handles) {
+    if (!ex || !handles || ex->connected) return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ex->device);
+    const uint8_t* hb = static_cast<const uint8_t*>(handles);
+    for (int r = 0; r < ex->world; ++r) {
+        if (r == ex->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hb + (size_t)r * MOE_B200_EP_HANDLE_BYTES, sizeof(h));
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return cuda_rc(e);
+        ex->peers[r] = static_cast<uint8_t*>(p);
+    }
+    const cudaError_t e = cudaMemcpy(ex->d_peers, ex->peers.data(), sizeof(uint8_t*) * ex->world,
+                                     cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_rc(e);
+    ex->connected = true;
+    return MOE_B200_OK;
+}
+
+int moe_b200_ep_exchange_step(moe_b200_ep_exchange* ex, moe_b200_workspace* ws,
+                              const moe_b200_weights* w, const int8_t* d_send_q,
+                              const float* d_send_scale, const int32_t* d_send_expert,
+                              const int32_t* d_send_counts, void* stream) {
+    if (!ex || !ex->connected) return MOE_B200_ERR_INVALID;
+    int rc = compatible(ws, w);
+    if (rc) return rc;
+    if (w->shared) return MOE_B200_ERR_UNSUPPORTED;
+    if (ws->device != ex->device || (size_t)ws->Kh != ex->row_bytes || ws->H != ex->H)
+        return MOE_B200_ERR_INVALID;
+    const long n = (long)ex->world * ex->cap;
+    if (n > ws->n_max) return MOE_B200_ERR_CAPACITY;
+    if (!d_send_q || !d_send_scale || !d_send_expert || !d_send_counts || !aligned16(d_send_q))
+        return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ex->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const ExchangeArgs& a = ex->args;
+    uint8_t* own = ex->region;
+    launch_ep_begin(ex->step, s);
+    launch_ep_dispatch(a, d_send_q, d_send_scale, d_send_expert, d_send_counts, s);
+    launch_ep_wait(a, 0, ex->mask, s);
+    rc = ep_expert_rows_impl(ws, w, (int)n, reinterpret_cast<const int8_t*>(own + a.off_q),
+                             reinterpret_cast<const float*>(own + a.off_scale),
+                             reinterpret_cast<const int32_t*>(own + a.off_expert), ex->mask, ex->y,
+                             s);
+    if (rc) return rc;
+    launch_ep_return(a, ex->y, s);
+    launch_ep_wait(a, 1, nullptr, s);
+    ws->launches += 5;
+    return cuda_rc(cudaPeekAtLastError());
+}
+
+const float* moe_b200_ep_exchange_y_back(const moe_b200_ep_exchange* ex) {
+    return ex ? reinterpret_cast<const float*>(ex->region + ex->args.off_y) : nullptr;
+}
+
+int moe_b200_ep_exchange_status(moe_b200_ep_exchange* ex) {
+    if (!ex) return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ex->device);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_rc(e);
+    uint32_t bits = 0;
+    e = cudaMemcpy(&bits, ex->err, sizeof(bits), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_rc(e);
+    if (bits) cudaMemset(ex->err, 0, sizeof(uint32_t));
+    return map_err_bits(bits);
+}
+
+void moe_b200_ep_exchange_free(moe_b200_ep_exchange* ex) {
+    if (!ex) return;
+    DeviceGuard guard(ex->device);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < (int)ex->peers.size(); ++r)
+        if (r != ex->rank && ex->peers[r]) cudaIpcCloseMemHandle(ex->peers[r]);
+    for (void* p : {(void*)ex->region, (void*)ex->d_peers, (void*)ex->step, (void*)ex->done,
+                    (void*)ex->err, (void*)ex->mask, (void*)ex->y})
+        if (p) cudaFree(p);
+    delete ex;
 }
 
 int moe_b200_ep_combine(moe_b200_workspace* ws, int32_t rows, const float* d_y_back,

@@ -137,6 +137,23 @@ constexpr size_t kGemvMaxSmem = 220 * 1024;
 int launch_gemv(const GemvArgs& a, int part, cudaStream_t s);
 size_t gemv_smem_bytes(int stages);
 
+// exchange.cu: device-initiated expert-parallel exchange (peer memory).
+struct ExchangeArgs {
+    uint8_t* const* peers;    // [world] exchange regions, this rank's at [rank]
+    size_t off_q, off_scale, off_expert, off_cnt, off_base, off_y, off_flag_rows, off_flag_y;
+    size_t row_bytes;
+    int world, rank, cap, H, blocks;
+    const uint64_t* step;     // this step's number (local)
+    int* done;                // last-CTA counter (local, zeroed)
+    uint32_t* err;            // status word (local)
+};
+void launch_ep_begin(uint64_t* step, cudaStream_t s);
+void launch_ep_dispatch(const ExchangeArgs& a, const int8_t* send_q, const float* send_scale,
+                        const int32_t* send_expert, const int32_t* counts, cudaStream_t s);
+// which = 0: rows (fills mask [world * cap] with 1 / 0), 1: returned y rows.
+void launch_ep_wait(const ExchangeArgs& a, int which, float* mask, cudaStream_t s);
+void launch_ep_return(const ExchangeArgs& a, const float* y, cudaStream_t s);
+
 // Exchanges two device byte ranges (16-byte aligned, bytes % 16 == 0).
 void launch_swap_bytes(void* a, void* b, size_t bytes, cudaStream_t s);
 

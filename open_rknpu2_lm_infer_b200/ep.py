@@ -29,7 +29,8 @@ import numpy as np
 from . import _lib as L
 from ._lib import MoeError, check
 
-__all__ = ["ExchangePlan", "ep_forward", "DeviceOps", "owner_of"]
+__all__ = ["ExchangePlan", "ep_forward", "DeviceOps", "DeviceExchange", "ep_forward_device",
+           "owner_of"]
 
 
 def owner_of(expert: np.ndarray, experts_per_rank: int) -> np.ndarray:
@@ -171,3 +172,68 @@ class DeviceOps:
         if self.ws:
             self.lib.moe_b200_workspace_free(self.ws)
             self.ws = None
+
+
+class DeviceExchange:
+    """The exchange of steps 3-5 done by the GPUs themselves over NVLink peer
+    memory (moe_b200_ep_exchange_*): the packed rows are written straight into
+    their owners' memory, the owners run their experts, and the expert rows
+    come back to the token owners, with the split sizes staying on the device
+    (no host synchronisation, so a whole step can be captured in a CUDA
+    graph). Setup shares one IPC handle per rank through `dist`
+    (all_gather_object); every rank then steps in lockstep."""
+
+    def __init__(self, ops: "DeviceOps", dist, group=None):
+        import torch
+        self.ops = ops
+        self.lib = ops.lib
+        rank = dist.get_rank(group) if dist is not None else 0
+        world = ops.world
+        cap = ops.send_q.shape[0]  # T * top: every packed row of one rank
+        raw = self.lib.moe_b200_ep_exchange_create(torch.cuda.current_device(), world, rank, cap,
+                                                   ops.row_bytes, ops.hidden)
+        if not raw:
+            raise MoeError("cannot create the expert-parallel exchange", L.ERR_NOMEM)
+        self.raw = raw
+        h = (C.c_uint8 * L.EP_HANDLE_BYTES)()
+        check(self.lib.moe_b200_ep_exchange_handle(raw, h), "exchange handle")
+        mine = bytes(h)
+        if world > 1:
+            allh = [None] * world
+            dist.all_gather_object(allh, mine, group=group)
+        else:
+            allh = [mine]
+        table = (C.c_uint8 * (L.EP_HANDLE_BYTES * world)).from_buffer_copy(b"".join(allh))
+        check(self.lib.moe_b200_ep_exchange_connect(raw, table), "exchange connect")
+        ptr = self.lib.moe_b200_ep_exchange_y_back(raw)
+        self.y_back = torch.as_tensor(_CAI(ptr, (cap, ops.hidden), "<f4"), device="cuda")
+
+    def step(self, send_q, send_scale, send_expert, counts):
+        check(self.lib.moe_b200_ep_exchange_step(
+            self.raw, self.ops.moe.workspace, self.ops.moe.weights.raw, send_q.data_ptr(),
+            send_scale.data_ptr(), send_expert.data_ptr(), counts.data_ptr(), self.ops._stream()),
+            "exchange step")
+        return self.y_back
+
+    def status(self):
+        check(self.lib.moe_b200_ep_exchange_status(self.raw), "exchange status")
+
+    def close(self):
+        if self.raw:
+            self.lib.moe_b200_ep_exchange_free(self.raw)
+            self.raw = None
+
+
+class _CAI:
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3}
+
+
+def ep_forward_device(ops: "DeviceOps", ex: DeviceExchange, x, residual=None):
+    """ep_forward with the device-initiated exchange: route, pack, exchange
+    step, combine; stream-ordered, no host synchronisation."""
+    ids, routes = ops.route(x)
+    send_q, send_scale, send_expert, counts, pos = ops.pack(x, ids, routes)
+    y_back = ex.step(send_q, send_scale, send_expert, counts)
+    return ops.combine(y_back, pos, routes, residual)
