@@ -9,7 +9,8 @@ one router-inclusive layer forward (router + top-k, dispatch, gate/up GEMM +
 SwiGLU, requant, down GEMM, combine + residual) on inputs resident in HBM.
 `e2e` times the same layer through the public host-pointer API with the
 input/residual copied from pinned host memory and the output read back.
-Decode (T=1) and 4096-token prefill are reported under "extra".
+Decode (T=1) and 4096-token prefill are reported under "extra"; `--suite`
+adds the other BASELINE configurations (3, 4 and 5) under "suite".
 
 With N > 1 (torchrun) the layer runs expert parallel: rank g owns experts
 [g*E/N, (g+1)*E/N) and routes its own 512 tokens, rows travel to the expert
@@ -282,6 +283,8 @@ def run_ours(args):
     }
     if args.extra and world == 1:
         result["extra"] = run_extra(args, moe, router, spec, lib, wsp, hbm_peak)
+    if args.suite and world == 1:
+        result["suite"] = run_suite(args, hbm_peak)
     if rank == 0 and world == 1 and args.cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(layer, spec, T, budget_s=args.cpu_seconds)
     moe.close()
@@ -578,6 +581,110 @@ def run_extra(args, moe, router, spec, lib, wsp, hbm_peak):
     return out
 
 
+def spec_bytes(spec, T, U):
+    """Algorithmic HBM bytes of one layer call, any config: the weights of the
+    U routed experts hit (int4 g32: codes + fp16 group scales; int8
+    per-channel: codes + f32 scales), the shared expert (int8 per-channel),
+    the f32 router, and x in, residual in, out."""
+    H, I, Is = spec.hidden, spec.inter, spec.shared_inter
+    if spec.routed == "w8pc":
+        per_expert = 3 * H * I + 4 * (2 * I + H)
+    elif spec.routed == "w4pc":
+        per_expert = 3 * H * I // 2 + 4 * (2 * I + H)
+    else:
+        per_expert = 3 * H * I // 2 + 3 * H * I // 32 * 2
+    shared = 3 * H * Is + 4 * (2 * Is + H) if Is else 0
+    return U * per_expert + shared + spec.experts * H * 4 + 3 * T * H * 4
+
+
+def run_suite(args, hbm_peak):
+    """The other BASELINE configurations, one GPU, CUDA-graph replays timed with
+    CUDA events (stack: eager launches): config 3 (routed W4 g32 + shared W8
+    expert, Zipf-skewed router) at 498 and 2110 tokens; config 5 (the config-3
+    layer with W4 g32 or W8 per-channel routed experts) at 1..256 tokens;
+    config 4 (48 layers of config 2, RMSNorm before each, residual after) at
+    4096 tokens, its 48 layers cycling over 4 distinct seeded banks (each bank,
+    ~340 MB, is far above the 126 MB L2, so every layer streams its weights
+    from HBM as 48 distinct banks would)."""
+    import torch
+    from open_rknpu2_lm_infer_b200 import synthetic as S
+    from open_rknpu2_lm_infer_b200.moe import Backend
+    from open_rknpu2_lm_infer_b200.stack import MoeStack
+    sp = torch.cuda.current_stream().cuda_stream
+    steps = max(3, min(args.steps, 20))
+    out = {}
+
+    def timed(fn, n):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    def layer_case(name, tokens):
+        spec = S.CONFIGS[name]
+        layer = S.make_layer(spec, seed=SEED)
+        be = Backend(max_rows=max(tokens))
+        if layer.shared is not None:
+            moe = be.load_moe_with_shared(layer.gate, layer.down, spec.top, layer.shared)
+        else:
+            moe = be.load_moe(layer.gate, layer.down, spec.top)
+        router = be.router(layer.router, spec.top, layer.bias)
+        res = {}
+        for T in tokens:
+            x = torch.from_numpy(S.make_input(spec, T, seed=SEED, stream=4)).cuda()
+            r = torch.from_numpy(S.make_input(spec, T, seed=SEED, stream=5)).cuda()
+            o = torch.empty_like(x)
+            g = moe.graph(router, T, x.data_ptr(), r.data_ptr(), o.data_ptr())
+            for _ in range(3):
+                g.launch(sp)
+            ms = timed(lambda: g.launch(sp), steps)
+            g.close()
+            moe.status()
+            U, A = routing_stats(moe, spec, T)
+            b = spec_bytes(spec, T, U)
+            res[f"t{T}"] = {"tokens": T, "ms_per_step": ms, "tokens_per_s": T / (ms * 1e-3),
+                            "experts_hit": U, "algorithmic_bytes": b,
+                            "hbm_gbs": b / (ms * 1e-3) / 1e9,
+                            "hbm_frac": b / (ms * 1e-3) / 1e9 / hbm_peak}
+        moe.close(); router.close(); be.close()
+        return res
+
+    out["c3"] = layer_case("c3", (498, 2110))
+    out["c5_w4"] = layer_case("c5_w4", (1, 8, 32, 128, 256))
+    out["c5_w8"] = layer_case("c5_w8", (1, 8, 32, 128, 256))
+
+    # config 4: the 48-layer stack at 4096 tokens
+    spec, T, n_layers, n_banks = S.CONFIGS["c2"], 4096, 48, 4
+    be = Backend(max_rows=T)
+    banks = []
+    for i in range(n_banks):
+        lay = S.make_layer(spec, seed=SEED + 100 + i)
+        banks.append((be.load_moe(lay.gate, lay.down, spec.top),
+                      be.router(lay.router, spec.top, lay.bias)))
+        del lay
+    rng = np.random.default_rng(SEED)
+    norms = [(1 + rng.standard_normal(spec.hidden) * 0.02).astype(np.float32)
+             for _ in range(n_layers)]
+    stack = MoeStack([banks[i % n_banks] for i in range(n_layers)], norms, eps=1e-6)
+    h = torch.from_numpy(S.make_input(spec, T, seed=SEED, stream=4)).cuda()
+    o = torch.empty_like(h)
+    stack.forward_tensor(h, out=o)
+    ms = timed(lambda: stack.forward_tensor(h, out=o), 3)
+    for moe, _ in banks:
+        moe.status()
+    out["c4_stack"] = {"layers": n_layers, "tokens": T, "distinct_banks": n_banks,
+                       "ms_per_step": ms, "tokens_per_s": T / (ms * 1e-3),
+                       "ms_per_layer": ms / n_layers, "n_gpus": 1}
+    for moe, r in banks:
+        moe.close(); r.close()
+    be.close()
+    return out
+
+
 # ---------------------------------------------------------------- CPU side
 def cpu_baseline(layer, spec, T, budget_s=10.0):
     """The CPU restatement (oracle/, all host threads) on a bounded sample of
@@ -655,6 +762,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=TOKENS)
     ap.add_argument("--no-extra", dest="extra", action="store_false")
+    ap.add_argument("--suite", action="store_true",
+                    help="also measure BASELINE configs 3, 4 (48-layer stack) and 5 (one GPU)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()

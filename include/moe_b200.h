@@ -369,6 +369,18 @@ int moe_b200_ep_combine(moe_b200_workspace *ws, int32_t rows, const float *d_y_b
                         const int32_t *d_pos, const float *d_routes, const float *d_residual,
                         float *d_out, void *stream);
 
+/* Pre-norm of a layer stack: RMSNorm (src/ops/norm.rs:81-106, the norm the
+ * decoder applies before each MoE layer, src/model/qwen35/decoder.rs:180-189)
+ * of `rows` device rows of `width` floats, on the current device and stream:
+ * out[r,i] = (x[r,i] * s_r) * w_i with s_r = 1 / sqrt(sum_i x[r,i]^2 / width +
+ * epsilon), the squares summed in column order as the reference's iterator
+ * sum, w_i replaced by 1 + w_i when zero_centered. Bit-exact with the
+ * reference's f32 arithmetic. d_x and d_out may be the same buffer.
+ * MOE_B200_ERR_INVALID for width <= 0 or an epsilon that is not finite and
+ * positive (the reference's own checks). */
+int moe_b200_rms_norm(const float *d_x, const float *d_weight, int32_t rows, int32_t width,
+                      float epsilon, int32_t zero_centered, float *d_out, void *stream);
+
 /* Router + top-k that allocates nothing (no counterpart in the reference; an
  * addition for callers that cannot call cudaMalloc, such as an engine whose
  * own pool owns all device memory, or a hot path that must not risk an

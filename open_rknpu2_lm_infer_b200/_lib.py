@@ -152,6 +152,8 @@ SIGNATURES = [
     ("moe_b200_ep_combine", C.c_int,
      [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
       C.c_void_p]),
+    ("moe_b200_rms_norm", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_float, C.c_int32, C.c_void_p, C.c_void_p]),
     ("moe_b200_route_noalloc", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
       C.c_float, C.c_void_p, C.c_void_p, C.c_void_p]),

@@ -19,7 +19,8 @@ BUILD = PKG / "_build"
 LIB = PKG / "libmoe_b200.so"
 INCLUDE = PKG.parent / "include"
 
-SOURCES = ["api.cu", "router.cu", "dispatch.cu", "gemm.cu", "gemv.cu", "exchange.cu", "noalloc.cu"]
+SOURCES = ["api.cu", "router.cu", "dispatch.cu", "gemm.cu", "gemv.cu", "exchange.cu", "noalloc.cu",
+           "norm.cu"]
 HEADERS = ["common.cuh", "kernels.cuh"]
 
 # -fmad=false: no implicit a*b+c contraction; every fused multiply-add in the

@@ -1601,6 +1601,18 @@ int moe_b200_ep_combine(moe_b200_workspace* ws, int32_t rows, const float* d_y_b
     return cuda_rc(cudaPeekAtLastError());
 }
 
+int moe_b200_rms_norm(const float* d_x, const float* d_weight, int32_t rows, int32_t width,
+                      float epsilon, int32_t zero_centered, float* d_out, void* stream) {
+    // the reference's checks (src/ops/norm.rs:88-95): width > 0, finite eps > 0
+    if (rows < 0 || width <= 0 || !(epsilon > 0.0f) || !std::isfinite(epsilon))
+        return MOE_B200_ERR_INVALID;
+    if (rows == 0) return MOE_B200_OK;
+    if (!d_x || !d_weight || !d_out) return MOE_B200_ERR_INVALID;
+    launch_rms_norm(d_x, d_weight, rows, width, epsilon, zero_centered != 0, d_out,
+                    static_cast<cudaStream_t>(stream));
+    return cuda_rc(cudaPeekAtLastError());
+}
+
 int moe_b200_forward_f32(moe_b200_workspace* ws, const moe_b200_weights* w,
                          const moe_b200_router* r, int32_t rows, const float* input,
                          const float* residual, float* output, int32_t* ids, float* routes,

@@ -156,6 +156,9 @@ void launch_ep_return(const ExchangeArgs& a, const float* y, cudaStream_t s);
 
 // Exchanges two device byte ranges (16-byte aligned, bytes % 16 == 0).
 void launch_swap_bytes(void* a, void* b, size_t bytes, cudaStream_t s);
+// RMSNorm rows (norm.cu); x and out may alias.
+void launch_rms_norm(const float* x, const float* w, int rows, int width, float eps,
+                     int zero_centered, float* out, cudaStream_t s);
 
 constexpr int kRouteChunk = 512;  // assignments per route_count / route_scatter CTA
 

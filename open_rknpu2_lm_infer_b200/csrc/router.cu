@@ -468,8 +468,10 @@ static int launch_router_t(const RouterArgs& a, cudaStream_t s) {
     }
     // logits, then one warp per token for the routing (a separate launch: the
     // routing tail of a fused last-CTA step cost more than the launch)
+    // T <= 1024: CTAs of 8 tokens x 32 rows (two CTAs per SM) over 128-wide
+    // chunks, measured ~2 us faster at T = 512 than 8 x 64 over 64-wide ones
     if (a.T <= 1024)
-        launch_tile4<2, 4, 2, 64, 4, TF32>(a, s);
+        launch_tile4<2, 4, 1, 128, 3, TF32>(a, s);
     else
         launch_tile4<4, 4, 1, 64, 4, TF32>(a, s);
     route_rows_kernel<<<(a.T * 32 + 255) / 256, 256, 0, s>>>(a);

@@ -259,3 +259,29 @@ def test_ling_layer_routes_through_grouped_rule():
     assert np.allclose(w.sum(axis=1), 2.5, rtol=1e-6)
     # the chosen experts lie in at most top_groups groups
     assert all(len(set((row // 4).tolist())) <= 2 for row in ids)
+
+
+def test_rms_norm_is_the_sequential_reference_sum():
+    """The restatement's RMSNorm against a scalar loop written from
+    src/ops/norm.rs:96-104: iterator sum of x*x (each product rounded, added in
+    column order from -0.0), scale = recip(sqrt(sum / width + eps)), y = (x *
+    scale) * w, w -> 1 + w when zero-centred; an all-zero row gives 0."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(7)
+    for rows, width, zc in ((3, 37, False), (4, 64, True)):
+        x = (rng.standard_normal((rows, width)) * 3).astype(np.float32)
+        x[1] = 0.0
+        w = (1 + rng.standard_normal(width) * 0.02).astype(np.float32)
+        eps = np.float32(1e-6)
+        ref = np.empty_like(x)
+        for r in range(rows):
+            s = np.float32(-0.0)
+            for i in range(width):
+                s = np.float32(s + np.float32(x[r, i] * x[r, i]))
+            scale = np.float32(1.0) / np.sqrt(np.float32(s / np.float32(width) + eps))
+            for i in range(width):
+                wv = np.float32(1.0 + w[i]) if zc else w[i]
+                ref[r, i] = np.float32(np.float32(x[r, i] * scale) * wv)
+        got = O.rms_norm(x, w, float(eps), zc)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+        assert not got[1].any()
