@@ -309,6 +309,10 @@ struct moe_b200_workspace {
     int32_t *hist = nullptr, *offsets = nullptr, *perm = nullptr, *pos = nullptr;
     int32_t *shared_offsets = nullptr, *counters = nullptr;
     int32_t* gv_counters = nullptr;  // small-batch path: last-arrival counters
+    // fused small-batch layer: the grid barrier's 64-bit counter, then
+    // [n_max] middle-row max bits
+    uint32_t* dec_state = nullptr;
+    bool coop = false;  // the device runs cooperative launches
     int8_t* a_perm = nullptr;
     __half *q_m_h = nullptr, *sq_m_h = nullptr;  // fp16 copies of the middle codes (group-32 down)
     float* s_perm = nullptr;
@@ -445,6 +449,10 @@ bool use_gemv(const moe_b200_workspace* ws, const moe_b200_weights* w, int rows)
            gemv_smem_bytes((int)(w->dn.kblocks / kKPS)) <= kGemvMaxSmem && ws->k <= 32;
 }
 
+GemvArgs gemv_args(const moe_b200_workspace* ws, const moe_b200_weights* w, int rows,
+                   const float* d_x, const int32_t* d_ids, const float* d_routes,
+                   const float* d_res, float* d_out);
+
 int run_small(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
               const int32_t* d_ids, const float* d_routes, const float* d_res, float* d_out,
               cudaStream_t s, cudaEvent_t* evs, cudaEvent_t res_ready) {
@@ -455,6 +463,24 @@ int run_small(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const
     mark(1);
     mark(2);
     mark(3);
+    const GemvArgs a = gemv_args(ws, w, rows, d_x, d_ids, d_routes, d_res, d_out);
+    if (launch_gemv(a, 0, s)) return MOE_B200_ERR_UNSUPPORTED;
+    mark(4);
+    mark(5);
+    if (res_ready) cudaStreamWaitEvent(s, res_ready, 0);
+    if (launch_gemv(a, 1, s)) return MOE_B200_ERR_UNSUPPORTED;
+    mark(6);
+    mark(7);
+    mark(8);
+    ws->last_rows = 0;  // no permuted accumulators to dump for this call
+    ws->last_w = w;
+    ws->last_stream = s;
+    return cuda_rc(cudaPeekAtLastError());
+}
+
+GemvArgs gemv_args(const moe_b200_workspace* ws, const moe_b200_weights* w, int rows,
+                   const float* d_x, const int32_t* d_ids, const float* d_routes,
+                   const float* d_res, float* d_out) {
     GemvArgs a{};
     a.ids = d_ids;
     a.routes = d_routes;
@@ -484,18 +510,7 @@ int run_small(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const
     a.counters = ws->gv_counters;
     a.dn_counter_base = (int)ws->n_max;
     a.err = ws->err;
-    if (launch_gemv(a, 0, s)) return MOE_B200_ERR_UNSUPPORTED;
-    mark(4);
-    mark(5);
-    if (res_ready) cudaStreamWaitEvent(s, res_ready, 0);
-    if (launch_gemv(a, 1, s)) return MOE_B200_ERR_UNSUPPORTED;
-    mark(6);
-    mark(7);
-    mark(8);
-    ws->last_rows = 0;  // no permuted accumulators to dump for this call
-    ws->last_w = w;
-    ws->last_stream = s;
-    return cuda_rc(cudaPeekAtLastError());
+    return a;
 }
 
 // The shared-gate logits of a gated router: column E of the workspace logits.
@@ -597,6 +612,8 @@ int read_status(moe_b200_workspace* ws, cudaStream_t s) {
     if (e != cudaSuccess) return cuda_rc(e);
     if (bits) {
         cudaMemsetAsync(ws->err, 0, sizeof(uint32_t), s);
+        // a grid barrier that gave up is left mid-count: rearm it
+        if (bits & kErrWaitTimeout) cudaMemsetAsync(ws->dec_state, 0, 2 * sizeof(uint32_t), s);
         cudaStreamSynchronize(s);
     }
     return map_err_bits(bits);
@@ -941,6 +958,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     rc |= ws_alloc(ws, &ws->shared_offsets, 2);
     rc |= ws_alloc(ws, &ws->counters, T);
     rc |= ws_alloc(ws, &ws->gv_counters, n + T * ((ws->H + 127) / 128));
+    rc |= ws_alloc(ws, &ws->dec_state, n + 2);
     rc |= ws_alloc(ws, &ws->a_perm, (n + pad_rows) * ws->Kh);
     rc |= ws_alloc(ws, &ws->q_m_h, (n + pad_rows) * ws->Ki);
     rc |= ws_alloc(ws, &ws->s_perm, n);
@@ -965,6 +983,12 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     }
     cudaMemset(ws->counters, 0, sizeof(int) * T);
     cudaMemset(ws->gv_counters, 0, sizeof(int) * (size_t)(n + T * ((ws->H + 127) / 128)));
+    cudaMemset(ws->dec_state, 0, sizeof(uint32_t) * (size_t)(n + 2));
+    {
+        int coop = 0;
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ws->device);
+        ws->coop = coop != 0;
+    }
     cudaMemset(ws->err, 0, sizeof(uint32_t));
     cudaMemset(ws->a_perm, 0, (size_t)(n + pad_rows) * ws->Kh);
     cudaMemset(ws->q_m, 0, (size_t)(n + pad_rows) * ws->Ki);
@@ -1186,8 +1210,8 @@ static GateRef router_gate(const moe_b200_workspace* ws, const moe_b200_router* 
     return g;
 }
 
-static int route_impl(moe_b200_workspace* ws, const moe_b200_router* r, int rows, const float* d_x,
-                      float* d_logits, int32_t* d_ids, float* d_routes, cudaStream_t s) {
+static RouterArgs router_args(moe_b200_workspace* ws, const moe_b200_router* r, int rows,
+                              const float* d_x, float* d_logits, int32_t* d_ids, float* d_routes) {
     RouterArgs a{};
     a.x = d_x;
     a.w = r->w;
@@ -1205,11 +1229,17 @@ static int route_impl(moe_b200_workspace* ws, const moe_b200_router* r, int rows
     a.top_groups = r->top_groups;
     a.scale = r->scale;
     a.logits = d_logits ? d_logits : ws->logits;
-    ws->last_logit_cols = r->rows();
     a.counters = ws->counters;
     a.ids = d_ids;
     a.weights = d_routes;
     a.err = ws->err;
+    return a;
+}
+
+static int route_impl(moe_b200_workspace* ws, const moe_b200_router* r, int rows, const float* d_x,
+                      float* d_logits, int32_t* d_ids, float* d_routes, cudaStream_t s) {
+    const RouterArgs a = router_args(ws, r, rows, d_x, d_logits, d_ids, d_routes);
+    ws->last_logit_cols = r->rows();
     launch_router(a, s);
     // the decode-sized router routes in its last CTA; the others launch a
     // separate routing kernel
@@ -1231,6 +1261,39 @@ int moe_b200_route_device(moe_b200_workspace* ws, const moe_b200_router* r, int3
     return route_impl(ws, r, rows, d_input, d_logits, d_ids, d_routes, s);
 }
 
+// The router-inclusive layer: one cooperative launch of the fused small-batch
+// kernel where it applies (group-32 bank without a shared expert, at most
+// kGemvMaxRows tokens, NEON16 or TF32 router without a gate row), else the
+// router followed by the pipeline. The fused kernel's time shows as the
+// gate/up stage of the profiling events.
+static int layer_impl(moe_b200_workspace* ws, const moe_b200_weights* w, const moe_b200_router* r,
+                      int rows, const float* d_x, const float* d_res, float* d_out, cudaStream_t s,
+                      cudaEvent_t* evs, cudaEvent_t res_ready) {
+    if (ws->coop && use_gemv(ws, w, rows) && r->order != MOE_B200_ROUTER_SEQUENTIAL && !r->gate) {
+        if (res_ready) cudaStreamWaitEvent(s, res_ready, 0);
+        DecodeArgs d{};
+        d.r = router_args(ws, r, rows, d_x, nullptr, ws->ids, ws->routes);
+        d.g = gemv_args(ws, w, rows, d_x, ws->ids, ws->routes, d_res, d_out);
+        d.bar = reinterpret_cast<unsigned long long*>(ws->dec_state);
+        d.mmax = ws->dec_state + 2;
+        for (int i = 1; evs && i <= 3; ++i) cudaEventRecord(evs[i], s);
+        if (launch_decode_layer(d, ws->num_sms, s) == 0) {
+            ws->launches += 1;
+            ws->last_logit_cols = r->rows();
+            for (int i = 4; evs && i <= 8; ++i) cudaEventRecord(evs[i], s);
+            ws->last_rows = 0;  // no permuted accumulators to dump for this call
+            ws->last_w = w;
+            ws->last_stream = s;
+            return cuda_rc(cudaPeekAtLastError());
+        }
+        cudaGetLastError();  // not launched: run the kernels one by one
+    }
+    const int rc = route_impl(ws, r, rows, d_x, nullptr, ws->ids, ws->routes, s);
+    if (rc) return rc;
+    return run_pipeline(ws, w, rows, d_x, ws->ids, ws->routes, d_res, d_out, s, evs, res_ready,
+                        router_gate(ws, r));
+}
+
 int moe_b200_forward_device(moe_b200_workspace* ws, const moe_b200_weights* w,
                             const moe_b200_router* r, int32_t rows, const float* d_input,
                             const float* d_residual, float* d_output, void* stream) {
@@ -1247,10 +1310,7 @@ int moe_b200_forward_device(moe_b200_workspace* ws, const moe_b200_weights* w,
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaEvent_t* evs = prof_slot(ws, 1 | (w->shared ? 2 : 0));
     if (evs) cudaEventRecord(evs[0], s);
-    rc = route_impl(ws, r, rows, d_input, nullptr, ws->ids, ws->routes, s);
-    if (rc) return rc;
-    return run_pipeline(ws, w, rows, d_input, ws->ids, ws->routes, d_residual, d_output, s, evs,
-                        nullptr, router_gate(ws, r));
+    return layer_impl(ws, w, r, rows, d_input, d_residual, d_output, s, evs, nullptr);
 }
 
 struct moe_b200_graph {
@@ -1280,10 +1340,7 @@ moe_b200_graph* moe_b200_graph_create(moe_b200_workspace* ws, const moe_b200_wei
         ws->profiling = prof;
         return nullptr;
     }
-    rc = route_impl(ws, r, rows, d_input, nullptr, ws->ids, ws->routes, s);
-    if (rc == MOE_B200_OK)
-        rc = run_pipeline(ws, w, rows, d_input, ws->ids, ws->routes, d_residual, d_output, s, nullptr,
-                          nullptr, router_gate(ws, r));
+    rc = layer_impl(ws, w, r, rows, d_input, d_residual, d_output, s, nullptr, nullptr);
     const cudaError_t e = cudaStreamEndCapture(s, &g);
     ws->profiling = prof;
     if (rc != MOE_B200_OK || e != cudaSuccess || !g) {
@@ -1635,11 +1692,8 @@ int moe_b200_forward_f32(moe_b200_workspace* ws, const moe_b200_weights* w,
         cudaEventRecord(ws->res_ready, ws->copy_stream);
     }
     if (timings) cudaEventRecord(ws->ev[0], s);
-    rc = route_impl(ws, r, rows, ws->x, nullptr, ws->ids, ws->routes, s);
-    if (rc) return rc;
-    rc = run_pipeline(ws, w, rows, ws->x, ws->ids, ws->routes, residual ? ws->res : nullptr,
-                      ws->out, s, timings ? ws->ev : nullptr, residual ? ws->res_ready : nullptr,
-                      router_gate(ws, r));
+    rc = layer_impl(ws, w, r, rows, ws->x, residual ? ws->res : nullptr, ws->out, s,
+                    timings ? ws->ev : nullptr, residual ? ws->res_ready : nullptr);
     if (rc) return rc;
     cudaMemcpyAsync(output, ws->out, xb, cudaMemcpyDeviceToHost, s);
     if (ids) cudaMemcpyAsync(ids, ws->ids, sizeof(int32_t) * nb, cudaMemcpyDeviceToHost, s);

@@ -30,6 +30,7 @@
 #include <float.h>
 
 #include "kernels.cuh"
+#include "route.cuh"
 
 namespace moe {
 
@@ -108,12 +109,15 @@ __device__ __forceinline__ void issue_stages(const GvSmem& m, const uint8_t* til
 // group gl = lane & 7); every group's exact sum goes to acc[row][8 s + gl].
 // The stages land together, so every lane first waits for all of them
 // (acquire) and the warp decides together; the item loop then runs without
-// waits. Returns false when a stage never arrived (flagged).
-__device__ __forceinline__ bool group_sums(const GvSmem& m, int S, int* abort_flag,
-                                           uint32_t* err) {
+// waits. Returns false when a stage never arrived (flagged). Bit s of
+// `phases` is the phase parity stage s's barrier is in (a CTA that reuses its
+// barriers passes the parities; one use per barrier: 0).
+__device__ __forceinline__ bool group_sums_p(const GvSmem& m, int S, uint32_t phases,
+                                             int* abort_flag, uint32_t* err) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gl = lane & 7, rs = lane >> 3;
     bool arrived = true;
-    for (int s = 0; s < S; ++s) arrived = mbar_wait(&m.bars[s], 0, abort_flag, err) && arrived;
+    for (int s = 0; s < S; ++s)
+        arrived = mbar_wait(&m.bars[s], (phases >> s) & 1u, abort_flag, err) && arrived;
     if (!__all_sync(0xffffffffu, arrived)) return false;
 #pragma unroll 4
     for (int it = warp; it < S * 32; it += kGvWarps) {
@@ -133,6 +137,11 @@ __device__ __forceinline__ bool group_sums(const GvSmem& m, int S, int* abort_fl
         m.acc[lr * m.ld + s * 8 + gl] = acc - 8 * m.gsum[s * 8 + gl];
     }
     return true;
+}
+
+__device__ __forceinline__ bool group_sums(const GvSmem& m, int S, int* abort_flag,
+                                           uint32_t* err) {
+    return group_sums_p(m, S, 0u, abort_flag, err);
 }
 
 // Phase B (one thread per row): f = fma((float)acc_g, s_g, f) over ascending
@@ -343,6 +352,436 @@ int launch_gemv(const GemvArgs& a, int part, cudaStream_t s) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, a) == cudaSuccess ? 0 : -1;
+}
+
+// ===================================================================== fused
+// The small-batch layer as one cooperative launch, one CTA per SM. Phases:
+//   R  router logits, item = (token, weight row) spread over all CTAs (the
+//      CTA's rows and the token rows staged in shared memory, the NEON16 /
+//      TF32 dot of the decode router, on warps 0-1), and at the same time the
+//      tokens' activation codes (MoE A8, warps 2-15).
+//   -- grid barrier --
+//   T  every CTA routes every token itself (the softmax top-k by the whole
+//      block, the grouped rule by one warp per token) from the logits; CTA 0
+//      writes ids and weights out.
+//   G  gate/up items = (assignment, 64-channel tile) as gemv_gateup_kernel,
+//      then SwiGLU -> middle values and each middle
+//      row's max |value| (atomic max of the float bits); then the CTA's first
+//      down item's weights are requested, so they stream in across the
+//      barrier.
+//   -- grid barrier --
+//   D  down items = (assignment, 128-row tile) as gemv_down_kernel, each
+//      requantising its middle row itself; the last item of a (token, tile)
+//      combines the kept ranks in rank order and adds the residual.
+// Every value is computed by the same functions in the same order as the
+// three-kernel path, so results are bit-identical to it.
+namespace {
+
+__device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid-wide barrier (every CTA is resident: cooperative launch) on one
+// counter that only grows: a CTA's arrival returns the count before it, and
+// the barrier it belongs to completes when the count reaches the next
+// multiple of gridDim.x (the counter rests on a multiple of it between
+// barriers, which every launch of the same grid keeps). One atomic per CTA,
+// no reset round trip. Waits at most kWaitLimitNs, then kErrWaitTimeout and
+// false (the caller gives up; the host rearms the counter).
+__device__ bool grid_sync(unsigned long long* cnt, uint32_t* err) {
+    __shared__ int ok_s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        __threadfence();
+        const unsigned long long old = atomicAdd(cnt, 1ull);
+        const unsigned long long target = old - old % gridDim.x + gridDim.x;
+        if (old + 1 != target) {
+            const uint64_t start = global_timer_ns();
+            while (ld_acquire_gpu(cnt) < target) {
+                if (global_timer_ns() - start > kWaitLimitNs) {
+                    atomicOr(err, kErrWaitTimeout);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        __threadfence();
+        ok_s = ok;
+    }
+    __syncthreads();
+    return ok_s != 0;
+}
+
+struct DecodeSmem {
+    uint8_t* st;     // [Smax][kGvStage] stages (phase R: router and token rows)
+    int* acc;        // [128][Gmax + 8]
+    float* val;      // [128]
+    uint64_t* bars;  // [Smax rounded up to even]
+    uint32_t* txp;   // [T][Kg / 4] token activation codes, packed word order
+    int* tgs;        // [T][Gg] their group sums
+    uint32_t* dxp;   // [Kd / 4] middle codes of the current down item
+    int* dgs;        // [Gd]
+    float* sx;       // [T] token activation scales
+    int* rid;        // [T*k] routed expert ids
+    float* rw;       // [T*k] routing weights
+    float* selv;     // [32] one token's selected logits, in rank order
+    uint32_t* keys;  // [E] total-order keys of one token's logits
+};
+
+__device__ __forceinline__ DecodeSmem decode_smem(uint8_t* sm, int Sg, int Sd, int T, int k) {
+    const int Smax = Sg > Sd ? Sg : Sd, Sb = (Smax + 1) & ~1;
+    DecodeSmem d;
+    d.st = sm;
+    d.acc = reinterpret_cast<int*>(sm + (size_t)Smax * kGvStage);
+    d.val = reinterpret_cast<float*>(d.acc + 128 * (Smax * 8 + 8));
+    d.bars = reinterpret_cast<uint64_t*>(d.val + 128);
+    d.txp = reinterpret_cast<uint32_t*>(d.bars + Sb);
+    d.tgs = reinterpret_cast<int*>(d.txp + T * Sg * 64);
+    d.dxp = reinterpret_cast<uint32_t*>(d.tgs + T * Sg * 8);
+    d.dgs = reinterpret_cast<int*>(d.dxp + Sd * 64);
+    d.sx = reinterpret_cast<float*>(d.dgs + Sd * 8);
+    d.rid = reinterpret_cast<int*>(d.sx + T);
+    d.rw = reinterpret_cast<float*>(d.rid + T * k);
+    d.selv = d.rw + T * k;
+    d.keys = reinterpret_cast<uint32_t*>(d.selv + 32);
+    return d;
+}
+
+size_t decode_smem_bytes(int Sg, int Sd, int T, int k, int E) {
+    const int Smax = Sg > Sd ? Sg : Sd, Sb = (Smax + 1) & ~1;
+    return (size_t)Smax * kGvStage + 128 * (size_t)(Smax * 8 + 8) * 4 + 128 * 4 + (size_t)Sb * 8 +
+           (size_t)T * Sg * 64 * 4 + (size_t)T * Sg * 8 * 4 + (size_t)Sd * 64 * 4 +
+           (size_t)Sd * 8 * 4 + (size_t)T * 4 + (size_t)T * k * 8 + 32 * 4 + (size_t)E * 4;
+}
+
+__device__ __forceinline__ GvSmem gv_view(const DecodeSmem& d, uint32_t* xp, int* gsum, int S) {
+    GvSmem m;
+    m.st = d.st;
+    m.xp = xp;
+    m.gsum = gsum;
+    m.acc = d.acc;
+    m.val = d.val;
+    m.bars = d.bars;
+    m.G = S * 8;
+    m.ld = m.G + 8;
+    return m;
+}
+
+__global__ void __launch_bounds__(kGvThreads, 1) decode_layer_kernel(const DecodeArgs dl) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    __shared__ int abort_flag;
+    __shared__ float red[kGvWarps];
+    const RouterArgs& r = dl.r;
+    const GemvArgs& a = dl.g;
+    const int T = a.T, k = a.k, H = a.H, I = a.I, n = T * k;
+    const int Sg = a.gu_stages, Sd = a.dn_stages, Smax = Sg > Sd ? Sg : Sd;
+    const int Kg = Sg * 256, Kd = Sd * 256;
+    const int nb = gridDim.x, b = blockIdx.x, tid = threadIdx.x;
+    const DecodeSmem d = decode_smem(sm, Sg, Sd, T, k);
+    if (tid == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < Smax; ++s) mbar_init(&d.bars[s], 1);
+        fence_barrier_init();
+    }
+    if (b == 0)
+        for (int i = tid; i < n; i += kGvThreads) dl.mmax[i] = 0u;
+
+    // ---- R: logits of this CTA's (token, row) items
+    const int Ew = r.Ew, items = T * Ew, rs = H + 16;  // padded rows
+    const int my_n = items > b ? (items - b + nb - 1) / nb : 0;
+    float* rows_s = reinterpret_cast<float*>(d.st);  // [my_n + T][rs]: item rows, then tokens
+    float* x_s = rows_s + (size_t)my_n * rs;
+    {
+        const int q4 = H / 4;
+        for (int idx = tid; idx < (my_n + T) * q4; idx += kGvThreads) {
+            const int rr = idx / q4, q = idx % q4;
+            const float* src = rr < my_n ? r.w + (size_t)((b + nb * rr) % Ew) * H + 4 * q
+                                         : r.x + (size_t)(rr - my_n) * H + 4 * q;
+            float* dst = rows_s + (size_t)rr * rs + 4 * q;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src));
+        }
+        asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    if (tid < 64) {
+        // warps 0, 1: four 16-lane dot groups over this CTA's items
+        const bool tf = r.order == kOrderTf32;
+        const int H16 = (H / 16) * 16, grp = tid >> 4, j = tid & 15;
+        for (int r0 = 0; r0 < my_n; r0 += 4) {  // uniform over the two warps: both reduce
+            const int rr = r0 + grp;
+            const bool act = rr < my_n;
+            const int it = b + nb * (act ? rr : 0), t = it / Ew, e = it % Ew;
+            const float* wrow = rows_s + (size_t)(act ? rr : 0) * rs;
+            const float* xrow = x_s + (size_t)t * rs;
+            float acc = 0.0f;
+            if (act) {
+                if (tf) {
+#pragma unroll 8
+                    for (int i = 0; i < H16; i += 16)
+                        acc = __fmaf_rn(wrow[i + j], tf32_trunc(xrow[i + j]), acc);
+                } else {
+#pragma unroll 8
+                    for (int i = 0; i < H16; i += 16) acc = __fmaf_rn(wrow[i + j], xrow[i + j], acc);
+                }
+            }
+            const float q = neon16_tree(acc);
+            if (act && j == 0)
+                r.logits[(size_t)t * Ew + e] =
+                    tf ? neon16_finish<true>(q, wrow, xrow, H16, H, r.bias, e, r.E)
+                       : neon16_finish<false>(q, wrow, xrow, H16, H, r.bias, e, r.E);
+        }
+    } else {
+        // warps 2..15, at the same time: the tokens' activation rows -> MoE A8
+        // codes (s = max|x| / 127, 0 -> 1), from the staged rows; named
+        // barrier 1 over these 448 threads
+        constexpr int kQ = kGvThreads - 64;
+        const int qt = tid - 64, warp = tid >> 5, lane = tid & 31;
+        for (int t = 0; t < T; ++t) {
+            const float* xr = x_s + (size_t)t * rs;
+            float mx = 0.0f;
+            for (int ii = qt; ii < H; ii += kQ) mx = fmaxf(mx, fabsf(xr[ii]));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (lane == 0) red[warp] = mx;
+            asm volatile("bar.sync 1, %0;" ::"r"(kQ) : "memory");
+            mx = red[2];
+            for (int wi = 3; wi < kGvWarps; ++wi) mx = fmaxf(mx, red[wi]);
+            asm volatile("bar.sync 1, %0;" ::"r"(kQ) : "memory");
+            const float sxt = mx == 0.0f ? 1.0f : __fdiv_rn(mx, 127.0f);
+            if (!isfinite(sxt) && b == 0 && qt == 0) atomicOr(a.err, kErrNonFinite);
+            if (qt == 0) d.sx[t] = sxt;
+            const GvSmem mt = gv_view(d, d.txp + t * Sg * 64, d.tgs + t * Sg * 8, Sg);
+            for (int wd = qt; wd < Kg / 8; wd += kQ) {  // whole warps (qt and kQ are warp-aligned)
+                uint32_t lo = 0, hi = 0;
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    const int kk = wd * 8 + jj;
+                    const uint32_t q = kk < H ? (uint32_t)(quant_moe(xr[kk], sxt) & 0xFF) : 0u;
+                    if (jj < 4) lo |= q << (8 * jj);
+                    else hi |= q << (8 * (jj - 4));
+                }
+                put_word(mt, wd, lo, hi);
+            }
+        }
+    }
+    if (!grid_sync(dl.bar, a.err)) return;  // no copy in flight yet
+
+    // ---- T: routing of every token, in every CTA
+    if (r.rule == kRouteGroupedSigmoid) {
+        const int warp = tid >> 5, lane = tid & 31;
+        if (warp < T) grouped_row(r.logits + (size_t)warp * Ew, r, d.rid + warp * k, d.rw + warp * k, lane);
+        __syncthreads();
+    } else {
+        // topk_row's selection by the whole block: an element's rank under
+        // (total_cmp desc, id asc) is the number of elements before it; the
+        // element of rank r < k is the r-th pick. Then the same softmax over
+        // the picks in rank order (src/model/qwen35/moe.rs:51-67).
+        for (int t = 0; t < T; ++t) {
+            const float* row = r.logits + (size_t)t * Ew;
+            bool fin = true;
+            for (int e = tid; e < r.E; e += kGvThreads) {
+                const float l = __ldcg(row + e);
+                fin = fin && isfinite(l);
+                d.keys[e] = (uint32_t)total_key(l) ^ 0x80000000u;
+            }
+            if (__syncthreads_or(!fin) && tid == 0) atomicOr(r.err, kErrNonFinite);
+            for (int e = tid; e < r.E; e += kGvThreads) {
+                const uint32_t ke = d.keys[e];
+                int rank = 0;
+                for (int jj = 0; jj < r.E; ++jj) {
+                    const uint32_t kj = d.keys[jj];
+                    rank += (kj > ke || (kj == ke && jj < e)) ? 1 : 0;
+                }
+                if (rank < k) {
+                    d.rid[t * k + rank] = e;
+                    d.selv[rank] = key_value((int32_t)(ke ^ 0x80000000u));
+                }
+            }
+            __syncthreads();
+            if (tid < 32) {
+                const float top = d.selv[0];
+                float w = tid < k ? expf(__fsub_rn(d.selv[tid], top)) : 0.0f;
+                float sum = -0.0f;
+                for (int rr = 0; rr < k; ++rr) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, w, rr));
+                if (tid < k) {
+                    w = __fdiv_rn(w, sum);
+                    if (r.min_weight != 0.0f && tid >= 1 && w < r.min_weight) w = 0.0f;
+                    d.rw[t * k + tid] = w;
+                }
+            }
+            __syncthreads();
+        }
+    }
+    if (b == 0)
+        for (int i = tid; i < n; i += kGvThreads) {
+            r.ids[i] = d.rid[i];
+            r.weights[i] = d.rw[i];
+        }
+
+    const int tg = (I + 63) / 64, td = (H + 127) / 128;
+    const int n_gu = n * tg, n_dn = n * td;
+    uint32_t phases = 0;  // bit s: phase parity of stage barrier s
+    // the stages of a kept down item (after a __syncthreads: nobody reads st)
+    auto dn_issue = [&](int i) -> bool {
+        const int asg = i / td, dt = i % td;
+        const int e = d.rid[asg];
+        if (!(d.rw[asg] > 0.0f) || e < 0 || e >= a.E) return false;
+        if (tid == 0)
+            issue_stages(gv_view(d, d.dxp, d.dgs, Sd),
+                         a.dn_w + (size_t)e * a.dn_expert_stride + (size_t)dt * a.dn_tile_stride,
+                         a.dn_stage_stride, Sd);
+        return true;
+    };
+
+    // ---- G: gate/up items i = b, b + nb, ...
+    for (int i = b; i < n_gu; i += nb) {
+        const int asg = i / tg, rt = i % tg, t = asg / k;
+        const float w = d.rw[asg];
+        const int e = d.rid[asg];
+        if (!(w >= 0.0f) && rt == 0 && tid == 0) atomicOr(a.err, kErrBadRoute);
+        if (!(w > 0.0f)) continue;  // skipped route: its middle row is never read
+        if (e < 0 || e >= a.E) {
+            if (tid == 0) atomicOr(a.err, kErrBadExpert);
+            continue;
+        }
+        const GvSmem m = gv_view(d, d.txp + t * Sg * 64, d.tgs + t * Sg * 8, Sg);
+        __syncthreads();
+        if (tid == 0)
+            issue_stages(m, a.gu_w + (size_t)e * a.gu_expert_stride + (size_t)rt * a.gu_tile_stride,
+                         a.gu_stage_stride, Sg);
+        const bool ok = group_sums_p(m, Sg, phases, &abort_flag, a.err);
+        phases ^= (1u << Sg) - 1u;
+        __syncthreads();
+        if (tid < 128) d.val[tid] = __fmul_rn(fold_row(m, Sg, tid), d.sx[t]);
+        __syncthreads();
+        if (tid < 64) {  // warps 0 and 1
+            float mloc = 0.0f;
+            const int c = rt * 64 + tid;
+            if (ok && c < I) {
+                const float g = d.val[tid], u = d.val[64 + tid];
+                const float dd = __fadd_rn(1.0f, expf(-g));
+                const float mv = __fmul_rn(__fdiv_rn(g, dd), u);
+                a.middle[(size_t)asg * I + c] = mv;
+                mloc = fabsf(mv);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+            // the max of the non-NaN values, as the requantiser's fmaxf reduction
+            if ((tid & 31) == 0 && mloc > 0.0f) atomicMax(dl.mmax + asg, __float_as_uint(mloc));
+        }
+    }
+    // this CTA's down items: i = dn0, dn0 + nb, ... (owner (n_gu + i) % nb, so
+    // CTAs without gate/up work take the first ones); request the first one's
+    // weights before the barrier
+    const int dn0 = ((b - n_gu) % nb + nb) % nb;
+    __syncthreads();
+    const bool pref = dn0 < n_dn && dn_issue(dn0);
+    if (!grid_sync(dl.bar, a.err)) {
+        if (pref) {  // let the requested copies land before the CTA exits
+            int never = 0;
+            for (int s = 0; s < Sd; ++s) mbar_wait(&d.bars[s], (phases >> s) & 1u, &never, a.err);
+        }
+        return;
+    }
+
+    // ---- D: down items
+    for (int i = dn0; i < n_dn; i += nb) {
+        const int asg = i / td, dt = i % td, t = asg / k;
+        const float w = d.rw[asg];
+        const int e = d.rid[asg];
+        const bool valid = e >= 0 && e < a.E, kept = w > 0.0f && valid;
+        if (w > 0.0f && !valid && tid == 0) atomicOr(a.err, kErrBadExpert);
+        if (kept) {
+            if (i != dn0 || !pref) {
+                __syncthreads();
+                dn_issue(i);
+            }
+            // requantise the assignment's middle row (MoE A8) into this CTA's
+            // codes; the row max and the thread's middle values load together
+            const float* mrow = a.middle + (size_t)asg * I;
+            const GvSmem m = gv_view(d, d.dxp, d.dgs, Sd);
+            __syncthreads();  // the previous item's sums are done with dxp
+            const float mm = __uint_as_float(__ldcg(dl.mmax + asg));
+            const float sc = mm == 0.0f ? 1.0f : __fdiv_rn(mm, 127.0f);
+            for (int wd = tid; wd < Kd / 8; wd += kGvThreads) {
+                float mv[8];
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) mv[jj] = wd * 8 + jj < I ? __ldcg(mrow + wd * 8 + jj) : 0.0f;
+                uint32_t lo = 0, hi = 0;
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    const int c = wd * 8 + jj;
+                    const uint32_t q = c < I ? (uint32_t)(quant_moe(mv[jj], sc) & 0xFF) : 0u;
+                    if (jj < 4) lo |= q << (8 * jj);
+                    else hi |= q << (8 * (jj - 4));
+                }
+                put_word(m, wd, lo, hi);
+                if (dt == 0 && wd * 8 < a.ld_qm)
+                    *reinterpret_cast<uint2*>(a.q_m + (size_t)asg * a.ld_qm + wd * 8) = make_uint2(lo, hi);
+            }
+            if (dt == 0 && tid == 0) a.s_m[asg] = sc;
+            __syncthreads();
+            const bool ok = group_sums_p(m, Sd, phases, &abort_flag, a.err);
+            phases ^= (1u << Sd) - 1u;
+            __syncthreads();
+            if (ok && tid < 128) {
+                const int c = dt * 128 + tid;
+                const float f = fold_row(m, Sd, tid);
+                if (c < H) a.y[(size_t)asg * H + c] = __fmul_rn(f, sc);
+            }
+        }
+        if (!last_arrival(&a.counters[a.dn_counter_base + t * td + dt], k)) continue;
+        // combine the token's kept ranks in rank order, then the residual
+        for (int c = dt * 128 + tid; c < min(H, dt * 128 + 128); c += kGvThreads) {
+            float acc = 0.0f;
+            for (int rr = 0; rr < k; ++rr) {
+                const int as = t * k + rr;
+                const float wr = d.rw[as];
+                const int er = d.rid[as];
+                if (!(wr > 0.0f) || er < 0 || er >= a.E) continue;
+                acc = __fmaf_rn(__ldcg(a.y + (size_t)as * H + c), wr, acc);
+            }
+            if (a.residual) acc = __fadd_rn(a.residual[(size_t)t * H + c], acc);
+            a.out[(size_t)t * H + c] = acc;
+        }
+    }
+}
+
+}  // namespace
+
+int launch_decode_layer(const DecodeArgs& d, int num_sms, cudaStream_t s) {
+    const GemvArgs& a = d.g;
+    const int Sg = a.gu_stages, Sd = a.dn_stages, Smax = Sg > Sd ? Sg : Sd;
+    if (a.H % 4 != 0 || Sg > 31 || Sd > 31 || d.r.Ew <= 0 || a.k > 32 || d.r.E > 1024 ||
+        a.T > 32)
+        return -1;
+    const size_t smem = decode_smem_bytes(Sg, Sd, a.T, a.k, d.r.E);
+    if (smem > kGemvMaxSmem) return -1;
+    // phase R stages its item rows and the token rows in the stage region
+    const long items = (long)a.T * d.r.Ew, per = (items + num_sms - 1) / num_sms;
+    if ((size_t)(per + a.T) * (a.H + 16) * 4 > (size_t)Smax * kGvStage) return -1;
+    if (cudaFuncSetAttribute(decode_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+        return -1;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_layer_kernel, kGvThreads,
+                                                      smem) != cudaSuccess ||
+        per_sm < 1)
+        return -1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(num_sms);
+    cfg.blockDim = dim3(kGvThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, decode_layer_kernel, d) == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace moe

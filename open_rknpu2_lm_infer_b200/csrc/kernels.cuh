@@ -70,10 +70,6 @@ struct GemmArgs {
     uint32_t* err;
 };
 
-__device__ void topk_row(const float* row, int E, int k, float min_weight, int32_t* ids,
-                         float* weights, int lane, uint32_t* err);
-__device__ void grouped_row(const float* row, const RouterArgs& a, int32_t* ids, float* weights,
-                            int lane);
 
 int launch_router(const RouterArgs& a, cudaStream_t s);
 int launch_gemm(const CUtensorMap& map, const GemmArgs& a, int fmt, int epi, int nt,
@@ -136,6 +132,18 @@ struct GemvArgs {
 constexpr size_t kGemvMaxSmem = 220 * 1024;
 int launch_gemv(const GemvArgs& a, int part, cudaStream_t s);
 size_t gemv_smem_bytes(int stages);
+
+// gemv.cu: the whole small-batch layer in one cooperative launch: router
+// logits, routing, gate/up + SwiGLU, requantisation, down, combine + residual,
+// with two grid-wide barriers (bounded waits). -1 when the geometry does not
+// fit (the caller then runs the router and the two GEMV kernels).
+struct DecodeArgs {
+    RouterArgs r;              // logits scratch; ids / weights outputs
+    GemvArgs g;                // ids / routes = r.ids / r.weights
+    uint32_t* mmax;            // [T*k] bits of each middle row's max |value| (zeroed by the kernel)
+    unsigned long long* bar;   // grid barrier counter (a multiple of the grid at rest)
+};
+int launch_decode_layer(const DecodeArgs& d, int num_sms, cudaStream_t s);
 
 // exchange.cu: device-initiated expert-parallel exchange (peer memory).
 struct ExchangeArgs {
