@@ -299,6 +299,7 @@ struct moe_b200_workspace {
     cudaStream_t own_stream = nullptr;
     cudaStream_t copy_stream = nullptr;  // host-API residual upload, overlapped with the layer
     cudaEvent_t res_ready = nullptr;
+    cudaEvent_t x_ready = nullptr;  // host-API input upload done (orders the residual's after it)
     cudaStream_t last_stream = nullptr;
     // staging for the host-pointer API
     float *x = nullptr, *out = nullptr, *res = nullptr, *routes = nullptr;
@@ -1008,7 +1009,8 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     }
     if (rc == MOE_B200_OK &&
         (cudaStreamCreateWithFlags(&ws->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
-         cudaEventCreateWithFlags(&ws->res_ready, cudaEventDisableTiming) != cudaSuccess))
+         cudaEventCreateWithFlags(&ws->res_ready, cudaEventDisableTiming) != cudaSuccess ||
+         cudaEventCreateWithFlags(&ws->x_ready, cudaEventDisableTiming) != cudaSuccess))
         rc = MOE_B200_ERR_CUDA;
     if (rc == MOE_B200_OK && cudaStreamCreateWithFlags(&ws->own_stream, cudaStreamNonBlocking) != cudaSuccess)
         rc = MOE_B200_ERR_CUDA;
@@ -1035,6 +1037,7 @@ void moe_b200_workspace_free(moe_b200_workspace* ws) {
         cudaStreamDestroy(ws->copy_stream);
     }
     if (ws->res_ready) cudaEventDestroy(ws->res_ready);
+    if (ws->x_ready) cudaEventDestroy(ws->x_ready);
     delete ws;
 }
 
@@ -1688,6 +1691,10 @@ int moe_b200_forward_f32(moe_b200_workspace* ws, const moe_b200_weights* w,
     cudaMemcpyAsync(ws->x, input, xb, cudaMemcpyHostToDevice, s);
     // the residual is read only by the final combine: upload it beside the layer
     if (residual) {
+        // after the input, which the router needs first: sharing the link from
+        // the start would halve the input's rate and delay the whole layer
+        cudaEventRecord(ws->x_ready, s);
+        cudaStreamWaitEvent(ws->copy_stream, ws->x_ready, 0);
         cudaMemcpyAsync(ws->res, residual, xb, cudaMemcpyHostToDevice, ws->copy_stream);
         cudaEventRecord(ws->res_ready, ws->copy_stream);
     }
