@@ -531,7 +531,9 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
     auto mark = [&](int i) {
         if (evs) cudaEventRecord(evs[i], s);
     };
-    ws->launches += (n + kRouteChunk - 1) / kRouteChunk > 0 ? 6 : 5;
+    // route count + scatter (when there are assignments), quantise, gate/up,
+    // requantise, down, combine
+    ws->launches += (n + kRouteChunk - 1) / kRouteChunk > 0 ? 7 : 5;
     if (w->shared) ws->launches += w->shared_mode == MOE_B200_SHARED_JOINT ? 3 : 4;
     mark(1);
     launch_route_count(d_ids, d_routes, (int)n, E, ws->hist, ws->err, s);
