@@ -63,6 +63,7 @@ constexpr int kStageK = kKPS * kKBlock;  // k per load stage (256)
 constexpr int kSmemTotal = 227 * 1024;
 constexpr int kSmemFixed = 10 * 1024;
 constexpr int kMaxLoadStages = 8;
+constexpr bool kGroupDual = true;  // exact group path, 16-token tiles: two CTAs per SM
 constexpr uint32_t kMagicBits = 0x4B400000u;  // 12582912.0f
 constexpr float kMagic = 12582912.0f;
 
@@ -98,7 +99,12 @@ struct GemmCfg {
     static constexpr int kStageAct = kAtoms * NT * 128;
     // load stage: [activations][weights (+ group scales)]
     static constexpr int kLoadBytes = kStageAct + kStageW;
-    static constexpr int kLoadBudget = kSmemTotal - kSmemFixed;
+    // exact group path at 16-token tiles: two CTAs per SM, each with half of
+    // the shared memory and of the tensor memory, so that two k-block
+    // pipelines overlap each other's latencies
+    static constexpr bool kDual = kGroup && NT == 16 && kGroupDual;
+    static constexpr int kCtasPerSm = kDual ? 2 : 1;
+    static constexpr int kLoadBudget = kSmemTotal / kCtasPerSm - kSmemFixed;
     static constexpr int kLoadStages = kLoadBudget / kLoadBytes > kMaxLoadStages
                                            ? kMaxLoadStages : kLoadBudget / kLoadBytes;
     // TMEM: [W4 weight operand ring: kAStages x kStageACols][accumulators]. The
@@ -110,10 +116,10 @@ struct GemmCfg {
     // exact group path: slots of one k-block (4 group buffers of NT columns);
     // other formats: two tile accumulators.
     static constexpr int kSlotCols = kGroup ? 4 * NT : NT;
-    static constexpr int kAccFree = 512 - kARegion;
+    static constexpr int kAllocCols = kDual ? 256 : 512;  // TMEM columns of one CTA
+    static constexpr int kAccFree = kAllocCols - kARegion;
     static constexpr int kNSlot = kGroup ? ((kAccFree / kSlotCols) < 4 ? (kAccFree / kSlotCols) : 4)
                                          : 2;
-    static constexpr int kAllocCols = 512;
     static constexpr int kHalf = NT / 2;                      // columns per epilogue warp
     static constexpr int kMmaPerStage = kF16 ? kStageK / 16 : kKPS * 4;
     // unpack warps: one per TMEM lane quadrant; two for the fp16 conversion
@@ -182,7 +188,7 @@ __device__ __forceinline__ void g32_word_to_i8(uint32_t word, uint32_t* out) {
 }
 
 template <int FMT, int EPI, int NT>
-__global__ void __launch_bounds__(GemmCfg<FMT, NT>::kThreads, 1)
+__global__ void __launch_bounds__(GemmCfg<FMT, NT>::kThreads, GemmCfg<FMT, NT>::kCtasPerSm)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs a) {
     using C = GemmCfg<FMT, NT>;
     constexpr int SL = C::kLoadStages;
@@ -695,7 +701,8 @@ static size_t gemm_smem_bytes(int E) {
                              2 * C::kNSlot + 1);
     b += sizeof(int) * (2 * (size_t)E + 2);
     // one CTA per SM: the kernel allocates all 512 TMEM columns
-    return b < 120 * 1024 ? 120 * 1024 : b;
+    // one CTA per SM (it allocates all 512 TMEM columns) unless two share it
+    return (C::kCtasPerSm == 1 && b < 120 * 1024) ? 120 * 1024 : b;
 }
 
 template <int FMT, int EPI, int NT>
@@ -706,7 +713,8 @@ static int launch_gemm_t(const CUtensorMap& map, const GemmArgs& a, int num_sms,
     cudaFuncSetAttribute(grouped_gemm_kernel<FMT, EPI, NT>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const long upper = ((long)(a.max_rows + NT - 1) / NT + a.num_experts) * a.row_tiles;
-    const int grid = (int)(upper < num_sms ? (upper > 0 ? upper : 1) : num_sms);
+    const long slots = (long)num_sms * GemmCfg<FMT, NT>::kCtasPerSm;
+    const int grid = (int)(upper < slots ? (upper > 0 ? upper : 1) : slots);
     grouped_gemm_kernel<FMT, EPI, NT><<<grid, GemmCfg<FMT, NT>::kThreads, smem, s>>>(map, a);
     return 0;
 }
