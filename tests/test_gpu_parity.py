@@ -65,7 +65,9 @@ SPECS = {
 # "_exact": the group-32 bank with both GEMMs on exact int32 group sums
 CASES = [("c1", 32), ("c1", 1), ("c2_e32", 1), ("c2_e32", 37), ("c2_e32", 300),
          ("c3_e32", 64), ("w4pc", 48), ("w8pc", 48), ("joint", 40), ("c2", 512),
-         ("c2_e32_exact", 37), ("c2_exact", 512), ("c1_exact", 32)]
+         ("c2_e32_exact", 37), ("c2_exact", 512), ("c1_exact", 32),
+         # 4 rows per expert: 16-token tiles, the exact kernel two CTAs per SM
+         ("c2", 64), ("c2_exact", 64)]
 
 
 @pytest.mark.parametrize("name,T", CASES)
@@ -128,7 +130,8 @@ def test_router_ties_and_bias(cuda, oracle):
     _LAYERS.pop((spec, 3))
 
 
-@pytest.mark.parametrize("name,T", [("c1", 32), ("c2_e32", 200), ("w4pc", 48), ("w8pc", 20)])
+@pytest.mark.parametrize("name,T", [("c1", 32), ("c2_e32", 200), ("w4pc", 48), ("w8pc", 20),
+                                    ("c2", 64)])
 def test_dispatch_and_accumulators_bit_exact(cuda, oracle, name, T):
     torch = cuda
     spec = SPECS[name]
