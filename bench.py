@@ -465,6 +465,8 @@ def run_ep(args):
     }
     del graph
     torch.cuda.synchronize()
+    if args.suite:
+        result["suite"] = {"c4_stack": run_ep_stack(args, world, rank, local, stream)}
     dist.barrier()  # every rank done with its peers' memory before unmapping
     ex.close()
     ops.close()
@@ -683,6 +685,78 @@ def run_suite(args, hbm_peak):
         moe.close(); r.close()
     be.close()
     return out
+
+
+def run_ep_stack(args, world, rank, local, stream):
+    """Config 4 expert parallel: 48 layers of config 2, RMSNorm before each and
+    the residual after, 4096 tokens split over the ranks (4096 / N each); rank
+    g holds experts [g E/N, (g+1) E/N) of every layer. The 48 layers cycle over
+    4 distinct seeded banks (each ~340 MB whole, far above the L2, so every
+    layer streams its weights from HBM as 48 distinct banks would). Eager
+    launches, one exchange (sized for the stack's rows) shared by the layers;
+    CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from open_rknpu2_lm_infer_b200 import synthetic as S
+    from open_rknpu2_lm_infer_b200.ep import DeviceExchange, DeviceOps, ep_forward_device
+    from open_rknpu2_lm_infer_b200.moe import Backend
+    spec, T_all, n_layers, n_banks = S.CONFIGS["c2"], 4096, 48, 4
+    T = T_all // world
+    P = spec.experts // world
+    be = Backend(device=local, max_rows=world * T)
+    banks = []
+    for i in range(n_banks):
+        lay = S.make_layer(spec, seed=SEED + 100 + i)
+        moe = be.load_moe(lay.gate[rank * P:(rank + 1) * P], lay.down[rank * P:(rank + 1) * P],
+                          spec.top)
+        router = be.router(lay.router, spec.top, lay.bias)
+        banks.append((moe, router, DeviceOps(be, moe, router, world, T)))
+        del lay
+    ex = DeviceExchange(banks[0][2], dist)
+    rng = np.random.default_rng(SEED)
+    norms = [torch.from_numpy((1 + rng.standard_normal(spec.hidden) * 0.02).astype(np.float32)).cuda()
+             for _ in range(n_layers)]
+    h0 = torch.from_numpy(S.make_input(spec, T, seed=SEED + rank, stream=4)).cuda()
+    xn = torch.empty_like(h0)
+    lib = be.lib
+    sp = stream.cuda_stream
+
+    def stack():
+        h = h0
+        for l in range(n_layers):
+            moe, router, ops = banks[l % n_banks]
+            rc = lib.moe_b200_rms_norm(h.data_ptr(), norms[l].data_ptr(), T, spec.hidden, 1e-6, 0,
+                                       xn.data_ptr(), sp)
+            if rc:
+                raise RuntimeError(f"RMSNorm failed ({rc})")
+            h = ep_forward_device(ops, ex, xn, h)
+        return h
+
+    stack()
+    torch.cuda.synchronize()
+    ex.status()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(3):
+        stack()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 3
+    t = torch.tensor([ms], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ex.status()
+    for moe, router, ops in banks:
+        ops.status()
+    dist.barrier()  # every rank done with its peers' memory before unmapping
+    ex.close()
+    for moe, router, ops in banks:
+        ops.close(); moe.close(); router.close()
+    be.close()
+    return {"layers": n_layers, "tokens": T_all, "tokens_per_gpu": T, "distinct_banks": n_banks,
+            "ms_per_step": ms, "tokens_per_s": T_all / (ms * 1e-3), "ms_per_layer": ms / n_layers,
+            "n_gpus": world, "parallelism": f"ep{world}"}
 
 
 # ---------------------------------------------------------------- CPU side

@@ -208,9 +208,12 @@ class DeviceExchange:
         ptr = self.lib.moe_b200_ep_exchange_y_back(raw)
         self.y_back = torch.as_tensor(_CAI(ptr, (cap, ops.hidden), "<f4"), device="cuda")
 
-    def step(self, send_q, send_scale, send_expert, counts):
+    def step(self, send_q, send_scale, send_expert, counts, moe=None):
+        """One exchange step; the owners run `moe` (default: the bank of the
+        ops this exchange was made with; a layer stack passes each layer's)."""
+        moe = self.ops.moe if moe is None else moe
         check(self.lib.moe_b200_ep_exchange_step(
-            self.raw, self.ops.moe.workspace, self.ops.moe.weights.raw, send_q.data_ptr(),
+            self.raw, moe.workspace, moe.weights.raw, send_q.data_ptr(),
             send_scale.data_ptr(), send_expert.data_ptr(), counts.data_ptr(), self.ops._stream()),
             "exchange step")
         return self.y_back
@@ -235,5 +238,5 @@ def ep_forward_device(ops: "DeviceOps", ex: DeviceExchange, x, residual=None):
     step, combine; stream-ordered, no host synchronisation."""
     ids, routes = ops.route(x)
     send_q, send_scale, send_expert, counts, pos = ops.pack(x, ids, routes)
-    y_back = ex.step(send_q, send_scale, send_expert, counts)
+    y_back = ex.step(send_q, send_scale, send_expert, counts, ops.moe)
     return ops.combine(y_back, pos, routes, residual)
