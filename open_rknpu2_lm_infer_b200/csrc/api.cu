@@ -441,7 +441,9 @@ cudaEvent_t* prof_slot(moe_b200_workspace* ws, int flags) {
 // The whole routed (+ shared) pipeline on device pointers. ev != null records
 // stage events for run_profiled-style timings.
 // Small batches of group-32 banks without a shared expert run the GEMV path
-// (csrc/gemv.cu): 2 launches after the router, every weight stage in flight.
+// (csrc/gemv.cu): with caller-supplied routes, 2 launches, every weight stage
+// in flight; router-inclusive calls run the whole layer as one cooperative
+// launch (decode_layer_kernel, see layer_impl).
 constexpr int kGemvMaxRows = 4;
 
 bool use_gemv(const moe_b200_workspace* ws, const moe_b200_weights* w, int rows) {
