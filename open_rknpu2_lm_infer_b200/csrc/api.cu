@@ -360,8 +360,10 @@ int ws_alloc(moe_b200_workspace* ws, T** p, size_t count) {
 int map_err_bits(uint32_t bits) {
     if (bits & kErrWaitTimeout) return MOE_B200_ERR_DEVICE_TIMEOUT;
     if (bits & kErrBadExpert) return MOE_B200_ERR_BAD_EXPERT;
-    if (bits & kErrBadRoute) return MOE_B200_ERR_BAD_ROUTE;
+    // a non-finite logit or activation also makes NaN routing weights: report
+    // the cause (caller-supplied bad routes set only the route bit)
     if (bits & kErrNonFinite) return MOE_B200_ERR_NONFINITE;
+    if (bits & kErrBadRoute) return MOE_B200_ERR_BAD_ROUTE;
     if (bits & kErrCapacity) return MOE_B200_ERR_CAPACITY;
     return MOE_B200_OK;
 }

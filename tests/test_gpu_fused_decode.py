@@ -11,7 +11,7 @@ import pytest
 
 from open_rknpu2_lm_infer_b200 import _lib as L
 from open_rknpu2_lm_infer_b200 import synthetic as S
-from open_rknpu2_lm_infer_b200.moe import Backend
+from open_rknpu2_lm_infer_b200.moe import Backend, MoeError
 
 pytestmark = pytest.mark.gpu
 
@@ -84,3 +84,26 @@ class _View:
     def __init__(self, ptr, shape, typestr):
         self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
                                          "data": (ptr, False), "version": 3}
+
+
+@pytest.mark.parametrize("T", [1, 4, 40])
+def test_non_finite_activations_are_flagged_and_the_next_call_is_clean(cuda, T):
+    """A NaN or infinite activation makes the router logits non-finite: the
+    call reports MOE_B200_ERR_NONFINITE (the fused small-batch layer at T <= 4,
+    the tile router and pipeline at 40 tokens), and the next clean call runs
+    normally with the same result as before."""
+    layer = S.make_layer(SPEC, seed=73)
+    be = Backend(device=0, max_rows=64)
+    moe = be.load_moe(layer.gate, layer.down, SPEC.top)
+    router = be.router(layer.router, SPEC.top, layer.bias)
+    x = S.make_input(SPEC, T, seed=74)
+    ref, _, _ = moe.forward(router, x)
+    for bad in (np.nan, np.inf):
+        xb = x.copy()
+        xb[T - 1, 5] = bad
+        with pytest.raises(MoeError) as e:
+            moe.forward(router, xb)
+        assert e.value.code == L.ERR_NONFINITE
+        out, _, _ = moe.forward(router, x)
+        assert np.array_equal(out.view(np.int32), ref.view(np.int32))
+    moe.close(); router.close(); be.close()
