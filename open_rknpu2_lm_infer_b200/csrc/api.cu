@@ -619,8 +619,15 @@ int read_status(moe_b200_workspace* ws, cudaStream_t s) {
     if (e != cudaSuccess) return cuda_rc(e);
     if (bits) {
         cudaMemsetAsync(ws->err, 0, sizeof(uint32_t), s);
-        // a grid barrier that gave up is left mid-count: rearm it
-        if (bits & kErrWaitTimeout) cudaMemsetAsync(ws->dec_state, 0, 2 * sizeof(uint32_t), s);
+        // a wait that gave up can leave the grid barrier and the last-arrival
+        // counters mid-count (CTAs that gave up never arrive): rearm them all,
+        // so that no later call hands off early
+        if (bits & kErrWaitTimeout) {
+            const long T = ws->max_rows, n = ws->n_max;
+            cudaMemsetAsync(ws->dec_state, 0, 2 * sizeof(uint32_t), s);
+            cudaMemsetAsync(ws->gv_counters, 0, sizeof(int) * (size_t)(n + T * ((ws->H + 127) / 128)), s);
+            cudaMemsetAsync(ws->counters, 0, sizeof(int) * (size_t)T, s);
+        }
         cudaStreamSynchronize(s);
     }
     return map_err_bits(bits);
