@@ -360,6 +360,14 @@ int moe_b200_ep_exchange_step(moe_b200_ep_exchange *ex, moe_b200_workspace *ws,
 const float *moe_b200_ep_exchange_y_back(const moe_b200_ep_exchange *ex);
 /* Synchronises the device, reads and clears the exchange's status word. */
 int moe_b200_ep_exchange_status(moe_b200_ep_exchange *ex);
+/* Diagnostics of the failure path (no counterpart in the reference): on a
+ * single-rank exchange (world 1), starts a step that no source completes and
+ * runs the exchange's row wait on it, which gives up after its limit (about
+ * 2 s); the next moe_b200_ep_exchange_status returns
+ * MOE_B200_ERR_DEVICE_TIMEOUT, and the exchange and the context stay usable
+ * (the next real step completes). MOE_B200_ERR_INVALID for world > 1, where
+ * it would break the ranks' lockstep. */
+int moe_b200_ep_exchange_probe_timeout(moe_b200_ep_exchange *ex, void *stream);
 void moe_b200_ep_exchange_free(moe_b200_ep_exchange *ex);
 
 /* Token owner, step 3: out[t] = (residual[t] +) sum over ranks r ascending of

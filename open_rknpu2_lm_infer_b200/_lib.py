@@ -138,6 +138,7 @@ SIGNATURES = [
       C.c_void_p]),
     ("moe_b200_ep_exchange_y_back", C.c_void_p, [C.c_void_p]),
     ("moe_b200_ep_exchange_status", C.c_int, [C.c_void_p]),
+    ("moe_b200_ep_exchange_probe_timeout", C.c_int, [C.c_void_p, C.c_void_p]),
     ("moe_b200_ep_exchange_free", None, [C.c_void_p]),
     ("moe_b200_graph_create", C.c_void_p,
      [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),

@@ -1630,6 +1630,15 @@ int moe_b200_ep_exchange_step(moe_b200_ep_exchange* ex, moe_b200_workspace* ws,
     return cuda_rc(cudaPeekAtLastError());
 }
 
+int moe_b200_ep_exchange_probe_timeout(moe_b200_ep_exchange* ex, void* stream) {
+    if (!ex || !ex->connected || ex->world != 1) return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ex->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    launch_ep_begin(ex->step, s);            // a step that no dispatch completes
+    launch_ep_wait(ex->args, 0, nullptr, s);  // gives up after the wait limit
+    return cuda_rc(cudaPeekAtLastError());
+}
+
 const float* moe_b200_ep_exchange_y_back(const moe_b200_ep_exchange* ex) {
     return ex ? reinterpret_cast<const float*>(ex->region + ex->args.off_y) : nullptr;
 }

@@ -221,6 +221,12 @@ class DeviceExchange:
     def status(self):
         check(self.lib.moe_b200_ep_exchange_status(self.raw), "exchange status")
 
+    def probe_timeout(self):
+        """Single-rank exchanges: run the row wait on a step nothing completes
+        (it gives up after ~2 s; status() then raises the timeout)."""
+        check(self.lib.moe_b200_ep_exchange_probe_timeout(self.raw, self.ops._stream()),
+              "exchange timeout probe")
+
     def close(self):
         if self.raw:
             self.lib.moe_b200_ep_exchange_free(self.raw)

@@ -81,6 +81,33 @@ def test_exchange_one_rank_matches_single_device_and_replays(cuda):
     ex.close(); ops.close(); moe.close(); router.close(); be.close()
 
 
+def test_exchange_wait_gives_up_and_the_exchange_recovers(cuda):
+    """A wait that nothing completes ends with an error, not a hang: the
+    exchange's row wait on a step that no source dispatches gives up after its
+    limit (~2 s) and the status reports MOE_B200_ERR_DEVICE_TIMEOUT; the
+    context and the exchange stay usable and the next layer step is exact."""
+    torch = cuda
+    from open_rknpu2_lm_infer_b200 import _lib as L
+    from open_rknpu2_lm_infer_b200.ep import DeviceExchange, ep_forward_device
+    from open_rknpu2_lm_infer_b200.moe import MoeError
+    layer = S.make_layer(SPEC, seed=5)
+    x = torch.from_numpy(S.make_input(SPEC, T, seed=6)).cuda()
+    res = torch.from_numpy(S.make_input(SPEC, T, seed=7, stream=5)).cuda()
+    ref = _single(torch, layer, x, res)
+    be, moe, router, ops = _rank_setup(1, 0, layer)
+    ex = DeviceExchange(ops, None)
+    ex.probe_timeout()
+    with pytest.raises(MoeError) as e:
+        ex.status()
+    assert e.value.code == L.ERR_DEVICE_TIMEOUT
+    ex.status()  # cleared
+    out = ep_forward_device(ops, ex, x, res)
+    torch.cuda.synchronize()
+    ex.status(); ops.status()
+    assert np.array_equal(out.cpu().numpy(), ref)
+    ex.close(); ops.close(); moe.close(); router.close(); be.close()
+
+
 def _free_port():
     with socket.socket() as sk:
         sk.bind(("127.0.0.1", 0))
