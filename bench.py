@@ -13,9 +13,11 @@ Decode (T=1) and 4096-token prefill are reported under "extra"; `--suite`
 adds the other BASELINE configurations (3, 4 and 5) under "suite".
 
 With N > 1 (torchrun) the layer runs expert parallel: rank g owns experts
-[g*E/N, (g+1)*E/N) and routes its own 512 tokens, rows travel to the expert
-owners and back with NCCL all-to-all (weak scaling); the time is the max over
-ranks.
+[g*E/N, (g+1)*E/N) and routes its own 512 tokens; rows travel to the expert
+owners and back by the GPUs' own stores into peer memory over NVLink
+(moe_b200_ep_exchange_*, no host synchronisation, one CUDA-graph replay per
+step; weak scaling); the time is the max over ranks. With --suite it also
+measures the config-4 stack expert parallel.
 `--impl reference` times the CPU restatement of the reference path (the
 oracle, all host threads) on the same workload, on rank 0 only.
 """
@@ -299,8 +301,9 @@ def run_ours(args):
 def run_ep(args):
     """N > 1: the expert-parallel layer (open_rknpu2_lm_infer_b200.ep). Rank g
     owns experts [g*E/N, (g+1)*E/N) and routes its own 512 tokens; rows travel
-    to the expert owners and back with NCCL all-to-all. Weak scaling: the
-    tokens per GPU are fixed; the time is the max over ranks."""
+    to the expert owners and back through the device-initiated exchange (peer
+    stores over NVLink). Weak scaling: the tokens per GPU are fixed; the time
+    is the max over ranks."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
