@@ -47,6 +47,9 @@
 //                operand from TMEM (no shared-memory operand, no proxy fence).
 //   warps 6..13  epilogue, two warps per TMEM lane quadrant, each owning half
 //                of the token columns.
+// One CTA per SM (all 512 TMEM columns), except the exact group path at
+// 16-token tiles: two CTAs per SM with 256 columns and half the shared memory
+// each, so that two k-block pipelines overlap their latencies.
 #include "kernels.cuh"
 
 namespace moe {
