@@ -29,6 +29,8 @@
 // src/model/qwen35/decoder.rs:215-217.
 #include <float.h>
 
+#include <mutex>
+
 #include "kernels.cuh"
 #include "route.cuh"
 
@@ -752,6 +754,8 @@ __global__ void __launch_bounds__(kGvThreads, 1) decode_layer_kernel(const Decod
 
 }  // namespace
 
+constexpr int kMaxDevices = 64;
+
 int launch_decode_layer(const DecodeArgs& d, int num_sms, cudaStream_t s) {
     const GemvArgs& a = d.g;
     const int Sg = a.gu_stages, Sd = a.dn_stages, Smax = Sg > Sd ? Sg : Sd;
@@ -763,14 +767,28 @@ int launch_decode_layer(const DecodeArgs& d, int num_sms, cudaStream_t s) {
     // phase R stages its item rows and the token rows in the stage region
     const long items = (long)a.T * d.r.Ew, per = (items + num_sms - 1) / num_sms;
     if ((size_t)(per + a.T) * (a.H + 16) * 4 > (size_t)Smax * kGvStage) return -1;
-    if (cudaFuncSetAttribute(decode_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
-        return -1;
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_layer_kernel, kGvThreads,
-                                                      smem) != cudaSuccess ||
-        per_sm < 1)
-        return -1;
+    // the shared-memory limit and the residency check, once per device and
+    // size (a larger limit serves every smaller launch): they cost a call's
+    // worth of host time each
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+    {
+        static std::mutex mu;
+        static size_t ready[kMaxDevices] = {};
+        std::lock_guard<std::mutex> lock(mu);
+        if (ready[dev] < smem) {
+            if (cudaFuncSetAttribute(decode_layer_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem) != cudaSuccess)
+                return -1;
+            int per_sm = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_layer_kernel,
+                                                              kGvThreads, smem) != cudaSuccess ||
+                per_sm < 1)
+                return -1;
+            ready[dev] = smem;
+        }
+    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(num_sms);
     cfg.blockDim = dim3(kGvThreads);
