@@ -154,6 +154,40 @@ def test_ep_two_ranks_match_one_rank(tmp_path, oracle_built):
     assert sum(int(sends[r][0].sum()) for r in range(world)) == world * TOKENS * SPEC.top
 
 
+def _failing_rank_main(rank, world, port, outdir):
+    """Rank 1 leaves before the layer (a host-side failure: it never joins the
+    exchange); rank 0 runs the layer and must get an error from its first
+    collective within the process group's short timeout, not hang."""
+    import time
+    from datetime import timedelta
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    if rank == 1:
+        dist.destroy_process_group()
+        return
+    layer = S.make_layer(SPEC, seed=SEED)
+    x = torch.from_numpy(S.make_input(SPEC, TOKENS, seed=SEED, stream=4))
+    t0 = time.monotonic()
+    status = "completed"
+    try:
+        ep_forward(NumpyOps(layer, rank, world), dist, None, x, None)
+    except Exception as e:  # the collective's error surfaces on the host
+        status = f"error: {type(e).__name__}"
+    with open(os.path.join(outdir, "rank0.txt"), "w") as f:
+        f.write(f"{status}\n{time.monotonic() - t0:.1f}\n")
+
+
+def test_a_rank_that_never_joins_makes_the_others_fail_not_hang(tmp_path, oracle_built):
+    import torch.multiprocessing as mp
+    mp.start_processes(_failing_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                       join=True, start_method="spawn")
+    status, seconds = (tmp_path / "rank0.txt").read_text().split("\n")[:2]
+    assert status.startswith("error"), status
+    assert float(seconds) < 60.0
+
+
 def test_owner_of_partitions_experts():
     ids = np.arange(128)
     own = owner_of(ids, 16)
