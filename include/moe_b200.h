@@ -405,7 +405,11 @@ int moe_b200_rms_norm(const float *d_x, const float *d_weight, int32_t rows, int
  * first call before any stream capture. All calls on a device share the
  * scratch: calls that overlap on the GPU (other streams or host threads) race
  * and must be serialised by the caller. Asynchronous; non-finite logits are
- * not reported by this entry point. */
+ * not reported by this entry point. Checked before anything is launched:
+ * hidden % 32 == 0 and, for fewer than 16 rows in the NEON16 order, hidden
+ * <= 5664 (the router rows are staged in shared memory), else
+ * MOE_B200_ERR_UNSUPPORTED; d_input and d_router 16-byte aligned, d_bias,
+ * d_ids and d_routes 4-byte aligned, else MOE_B200_ERR_INVALID. */
 #define MOE_B200_NOALLOC_MAX_LOGITS (1 << 20)
 int moe_b200_route_noalloc(const float *d_input, const float *d_router, const float *d_bias,
                            int32_t rows, int32_t hidden, int32_t experts, int32_t top,

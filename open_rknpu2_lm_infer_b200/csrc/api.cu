@@ -1256,7 +1256,7 @@ static int route_impl(moe_b200_workspace* ws, const moe_b200_router* r, int rows
                       float* d_logits, int32_t* d_ids, float* d_routes, cudaStream_t s) {
     const RouterArgs a = router_args(ws, r, rows, d_x, d_logits, d_ids, d_routes);
     ws->last_logit_cols = r->rows();
-    launch_router(a, s);
+    if (launch_router(a, s)) return MOE_B200_ERR_UNSUPPORTED;  // geometry does not fit
     // the decode-sized router routes in its last CTA; the others launch a
     // separate routing kernel
     ws->launches += (r->order == MOE_B200_ROUTER_SEQUENTIAL || rows >= 16) ? 2 : 1;
@@ -1271,6 +1271,7 @@ int moe_b200_route_device(moe_b200_workspace* ws, const moe_b200_router* r, int3
     if (rows < 0) return MOE_B200_ERR_INVALID;
     if (rows > ws->max_rows) return MOE_B200_ERR_CAPACITY;
     if (rows == 0) return MOE_B200_OK;
+    if (!d_input || !d_ids || !d_routes || !aligned16(d_input)) return MOE_B200_ERR_INVALID;
     DeviceGuard guard(ws->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     ws->last_stream = s;

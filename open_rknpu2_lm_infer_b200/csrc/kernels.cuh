@@ -71,7 +71,12 @@ struct GemmArgs {
 };
 
 
+// -1 (nothing launched) when the geometry does not fit: see router_fits.
 int launch_router(const RouterArgs& a, cudaStream_t s);
+// Whether launch_router can run `rows` tokens of width `hidden` in dot order
+// `order`: the NEON16 / TF32 orders at fewer than 16 tokens stage 8 router
+// rows and the token in shared memory (<= 200 KiB).
+bool router_fits(int rows, int hidden, int order);
 int launch_gemm(const CUtensorMap& map, const GemmArgs& a, int fmt, int epi, int nt,
                 int num_sms, cudaStream_t s);
 

@@ -64,9 +64,19 @@ extern "C" int moe_b200_route_noalloc(const float* d_input, const float* d_route
     if (order != MOE_B200_ROUTER_NEON16 && order != MOE_B200_ROUTER_SEQUENTIAL)
         return MOE_B200_ERR_INVALID;
     if (!(min_weight >= 0.0f && min_weight <= 1.0f)) return MOE_B200_ERR_INVALID;
+    // the router kernels stream rows in 16-byte vectors (the workspace path's
+    // hidden % 32 rule); a small batch stages its weight rows in shared memory
+    if (hidden % 32) return MOE_B200_ERR_UNSUPPORTED;
     if ((long)rows * experts > kMaxLogits) return MOE_B200_ERR_NOALLOC_LIMIT;
     if (rows == 0) return MOE_B200_OK;
+    if (!moe::router_fits(rows, hidden, order)) return MOE_B200_ERR_UNSUPPORTED;
     if (!d_input || !d_router || !d_ids || !d_routes) return MOE_B200_ERR_INVALID;
+    auto misaligned = [](const void* p, uintptr_t a) {
+        return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0;
+    };
+    if (misaligned(d_input, 16) || misaligned(d_router, 16) || misaligned(d_bias, 4) ||
+        misaligned(d_ids, 4) || misaligned(d_routes, 4))
+        return MOE_B200_ERR_INVALID;
     int dev = -1, major = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return MOE_B200_ERR_NO_DEVICE;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
@@ -100,6 +110,6 @@ extern "C" int moe_b200_route_noalloc(const float* d_input, const float* d_route
     a.ids = d_ids;
     a.weights = d_routes;
     a.err = err;
-    moe::launch_router(a, s);
+    if (moe::launch_router(a, s)) return MOE_B200_ERR_UNSUPPORTED;
     return cudaPeekAtLastError() == cudaSuccess ? MOE_B200_OK : MOE_B200_ERR_CUDA;
 }

@@ -237,11 +237,18 @@ static void launch_tile4(const RouterArgs& a, cudaStream_t s) {
     k<<<grid, 32 * WY * WX, smem, s>>>(a);
 }
 
+constexpr size_t kDecMaxSmem = 200 * 1024;
+static size_t decode_router_smem(int H) { return sizeof(float) * ((size_t)kDecEB * (H + 16) + H); }
+
+bool router_fits(int rows, int hidden, int order) {
+    return order == kOrderSequential || rows >= 16 || decode_router_smem(hidden) <= kDecMaxSmem;
+}
+
 template <bool TF32>
 static int launch_router_t(const RouterArgs& a, cudaStream_t s) {
     if (a.T < 16) {
-        const size_t smem = sizeof(float) * ((size_t)kDecEB * (a.H + 16) + a.H);
-        if (smem > 200 * 1024) return -1;
+        const size_t smem = decode_router_smem(a.H);
+        if (smem > kDecMaxSmem) return -1;
         cudaFuncSetAttribute(router_decode_kernel<TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem);
         dim3 grid(a.T, (a.Ew + kDecEB - 1) / kDecEB);
