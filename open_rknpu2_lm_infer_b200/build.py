@@ -21,6 +21,9 @@ INCLUDE = PKG.parent / "include"
 
 SOURCES = ["api.cu", "router.cu", "dispatch.cu", "gemm.cu", "gemv.cu", "exchange.cu", "noalloc.cu",
            "norm.cu"]
+# the tensor-core rate probe (open_rknpu2_lm_infer_b200/mma_peak.py), a separate library
+PEAK_SOURCE = "mma_peak.cu"
+PEAK_LIB = PKG / "libmoe_b200_peak.so"
 HEADERS = ["common.cuh", "kernels.cuh"]
 
 # -fmad=false: no implicit a*b+c contraction; every fused multiply-add in the
@@ -70,6 +73,9 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
             objs.append(obj)
             if force or ptxas_info or _stale(obj, [src, *headers, Path(__file__)]):
                 jobs.append(ex.submit(_compile, src, obj, verbose, ptxas_info))
+        peak_obj = BUILD / (Path(PEAK_SOURCE).stem + ".o")
+        if force or ptxas_info or _stale(peak_obj, [CSRC / PEAK_SOURCE, *headers, Path(__file__)]):
+            jobs.append(ex.submit(_compile, CSRC / PEAK_SOURCE, peak_obj, verbose, ptxas_info))
         logs = [j.result() for j in jobs]
     if ptxas_info:
         for log in logs:
@@ -79,6 +85,12 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
                *map(str, objs), "-o", str(LIB), "-lcudart"]
         if verbose:
             print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    if force or _stale(PEAK_LIB, [peak_obj]):
+        cmd = [nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", str(peak_obj),
+               "-o", str(PEAK_LIB), "-lcudart"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
