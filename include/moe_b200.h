@@ -42,15 +42,19 @@ extern "C" {
 
 /* Routed-expert weight formats. */
 #define MOE_B200_W4_PER_CHANNEL 0 /* reference native format: int4 codes, f32 scale per n */
-/* int4 codes, fp16 scale per (32 k, n) group. The gate/up GEMM keeps one exact
- * int32 sum per group (its output is requantised, where a rounding difference
- * would flip int8 codes); the down GEMM runs on the fp16 tensor cores with
- * w * s rounded once to fp16 and fp32 accumulation (outputs within the
- * 1e-2 rel / 1e-3 abs contract, ~3x faster than exact group sums). */
+/* int4 codes, fp16 scale per (32 k, n) group (an extension: the reference
+ * loader rejects group scales, src/model/checkpoint.rs:251-263). Both GEMMs
+ * keep one exact int32 sum per group and fold them in f32 in group order:
+ * f = fma((float)acc_g, s_g, f), then * s_x. */
 #define MOE_B200_W4_G32_FP16 1
 #define MOE_B200_W8_PER_CHANNEL 2 /* int8 codes, f32 scale per n */
-/* The same group-32 bank with both GEMMs on exact int32 group sums. */
+/* The same as MOE_B200_W4_G32_FP16 (kept for callers of an earlier version). */
 #define MOE_B200_W4_G32_FP16_EXACT 3
+/* The group-32 bank with the down GEMM on the fp16 tensor cores instead: w * s
+ * rounded once to fp16, fp32 accumulation over all of K. No int32 down
+ * accumulators; outputs stay within 1e-2 rel / 1e-3 abs of the exact format.
+ * The gate/up GEMM stays exact (its output is requantised). Opt-in. */
+#define MOE_B200_W4_G32_FP16_ROUNDED_DOWN 4
 
 /* Router accumulation order (src/model/cpu.rs:96-153, dense_dot). */
 #define MOE_B200_ROUTER_NEON16 0     /* aarch64 F32 branch: 4x4-lane FMA + fixed tree */

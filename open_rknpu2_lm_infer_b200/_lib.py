@@ -29,6 +29,7 @@ W4_PER_CHANNEL = 0
 W4_G32_FP16 = 1
 W8_PER_CHANNEL = 2
 W4_G32_FP16_EXACT = 3
+W4_G32_FP16_ROUNDED_DOWN = 4
 ROUTER_NEON16 = 0
 ROUTER_SEQUENTIAL = 1
 ROUTER_TF32 = 2

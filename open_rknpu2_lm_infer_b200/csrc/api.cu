@@ -17,6 +17,7 @@
 #include <mutex>
 #include <string>
 #include <type_traits>
+#include <functional>
 #include <vector>
 
 #include "../../include/moe_b200.h"
@@ -140,9 +141,9 @@ int choose_nt(long rows, int experts) {
 // The exact int8 group-32 kernel keeps four K=32 buffers per k-block in TMEM,
 // which caps its tile at 32 tokens.
 int exact_nt(int nt, int fmt) { return fmt == kFmtW4G32 && nt > 32 ? 32 : nt; }
-// Group-32 down projections (their output is not requantised) run on the fp16
-// tensor cores unless the bank asks for exact group sums; gate/up projections
-// always keep the exact per-group sums.
+// Group-32 down projections keep exact group sums unless the bank opted into
+// the fp16 tensor cores (MOE_B200_W4_G32_FP16_ROUNDED_DOWN); gate/up
+// projections always keep the exact per-group sums.
 int down_fmt(int fmt, bool exact) { return fmt == kFmtW4G32 && !exact ? kFmtW4G32H : fmt; }
 
 // ---- packed matrices ------------------------------------------------------
@@ -321,6 +322,7 @@ struct moe_b200_workspace {
     float* gate_up = nullptr;  // dequantised gate | up rows [n][2I]
     int8_t* q_m = nullptr;
     float *s_m = nullptr, *y = nullptr;
+
     // shared expert
     int8_t *q_xd = nullptr, *sq_m = nullptr;
     float *s_xd = nullptr, *s_middle = nullptr, *ss_m = nullptr, *s_y = nullptr;
@@ -390,6 +392,25 @@ GemmArgs gemm_args(moe_b200_workspace* ws, const PackedMat& m, const float* act_
     a.swiglu_layout = m.swiglu ? 1 : 0;
     a.err = ws->err;
     return a;
+}
+
+// Routed gate/up GEMM (gate | up rows) and the middle requantisation (SwiGLU,
+// row max, int8 codes). `mark` records the gate/up and middle stage events of
+// the profiling ring (index 4 and 5). A SwiGLU + requantisation fused into the
+// group-32 GEMM's epilogue was measured slower: its tile tail (an exchange of
+// the up values, SwiGLU, a per-token-tile arrival counter) stalls the three
+// accumulator slots of the pipeline (c2, 512 tokens: 441 us against 176 + 15).
+int run_gate_up(moe_b200_workspace* ws, const moe_b200_weights* w, long n, int nt_g, bool hd,
+                cudaStream_t s, const std::function<void(int)>& mark) {
+    const int E = ws->E, I = ws->I;
+    GemmArgs g = gemm_args(ws, w->gu, ws->s_perm, ws->offsets, E, n, ws->gate_up, 2 * I);
+    if (launch_gemm(ws->map_a[nt_index(nt_g)], g, w->gu.fmt, kEpiGateUp, nt_g, ws->num_sms, s))
+        return MOE_B200_ERR_UNSUPPORTED;
+    mark(4);
+    launch_requant(ws->gate_up, ws->offsets + E, (int)n, I, ws->Ki, kQuantMoe, ws->q_m,
+                   hd ? ws->q_m_h : nullptr, ws->s_m, s);
+    mark(5);
+    return MOE_B200_OK;
 }
 
 // Shared expert FFN over all rows (joint: reuses q_x; dense: own quantisation).
@@ -549,17 +570,14 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
     mark(3);
     const int nt = choose_nt(n, E);
     const int nt_g = exact_nt(nt, w->gu.fmt);
-    GemmArgs g = gemm_args(ws, w->gu, ws->s_perm, ws->offsets, E, n, ws->gate_up, 2 * I);
-    if (launch_gemm(ws->map_a[nt_index(nt_g)], g, w->gu.fmt, kEpiGateUp, nt_g, ws->num_sms, s))
-        return MOE_B200_ERR_UNSUPPORTED;
-    mark(4);
-    // group-32 down projections read an fp16 copy of the middle codes
+    // a rounded group-32 down projection reads an fp16 copy of the middle codes
     const int dfmt = down_fmt(w->dn.fmt, w->exact_down);
     const bool hd = dfmt == kFmtW4G32H;
     const int nt_d = exact_nt(nt, dfmt);
-    launch_requant(ws->gate_up, ws->offsets + E, (int)n, I, ws->Ki, kQuantMoe, ws->q_m,
-                   hd ? ws->q_m_h : nullptr, ws->s_m, s);
-    mark(5);
+    {
+        const int rc = run_gate_up(ws, w, n, nt_g, hd, s, mark);
+        if (rc) return rc;
+    }
     GemmArgs d = gemm_args(ws, w->dn, ws->s_m, ws->offsets, E, n, ws->y, H);
     if (launch_gemm(hd ? ws->map_qm_h[nt_index(nt_d)] : ws->map_qm[nt_index(nt_d)], d, dfmt,
                     kEpiStore, nt_d, ws->num_sms, s))
@@ -627,6 +645,7 @@ int read_status(moe_b200_workspace* ws, cudaStream_t s) {
             cudaMemsetAsync(ws->dec_state, 0, 2 * sizeof(uint32_t), s);
             cudaMemsetAsync(ws->gv_counters, 0, sizeof(int) * (size_t)(n + T * ((ws->H + 127) / 128)), s);
             cudaMemsetAsync(ws->counters, 0, sizeof(int) * (size_t)T, s);
+
         }
         cudaStreamSynchronize(s);
     }
@@ -689,9 +708,11 @@ moe_b200_weights* moe_b200_weights_create(const moe_b200_config* cfg,
     if (format) fmt = *format;
     const int H = cfg->weights.hidden, I = cfg->weights.intermediate, E = cfg->weights.routed_experts;
     const int Is = cfg->weights.shared_intermediate > 0 ? cfg->weights.shared_intermediate : I;
-    if (fmt.routed_format < 0 || fmt.routed_format > MOE_B200_W4_G32_FP16_EXACT) return nullptr;
-    const bool exact_down = fmt.routed_format == MOE_B200_W4_G32_FP16_EXACT;
-    if (exact_down) fmt.routed_format = MOE_B200_W4_G32_FP16;  // one packing for both
+    if (fmt.routed_format < 0 || fmt.routed_format > MOE_B200_W4_G32_FP16_ROUNDED_DOWN) return nullptr;
+    const bool exact_down = fmt.routed_format != MOE_B200_W4_G32_FP16_ROUNDED_DOWN;
+    if (fmt.routed_format == MOE_B200_W4_G32_FP16_EXACT ||
+        fmt.routed_format == MOE_B200_W4_G32_FP16_ROUNDED_DOWN)
+        fmt.routed_format = MOE_B200_W4_G32_FP16;  // one packing for all three
     if (fmt.shared_format != MOE_B200_W8_PER_CHANNEL && fmt.shared_format != MOE_B200_W4_PER_CHANNEL)
         return nullptr;
     if (cfg->weights.shared_expert && fmt.shared_mode == MOE_B200_SHARED_JOINT && Is != I)
@@ -799,7 +820,7 @@ void expert_regions(const moe_b200_weights* w, int e, Region r[4]) {
 
 uint32_t public_format(const moe_b200_weights* w) {
     if (w->gu.fmt == kFmtW4G32)
-        return w->exact_down ? MOE_B200_W4_G32_FP16_EXACT : MOE_B200_W4_G32_FP16;
+        return w->exact_down ? MOE_B200_W4_G32_FP16 : MOE_B200_W4_G32_FP16_ROUNDED_DOWN;
     return (uint32_t)w->gu.fmt;  // kFmtW4PC / kFmtW8PC match the public values
 }
 
@@ -839,11 +860,14 @@ uint32_t moe_b200_blob_version(void) { return MOE_B200_BLOB_VERSION; }
 
 moe_b200_weights* moe_b200_slots_create(const moe_b200_config* cfg, int32_t routed_format) {
     if (validate_config(cfg) || cfg->weights.shared_expert) return nullptr;
-    if (routed_format < 0 || routed_format > MOE_B200_W4_G32_FP16_EXACT) return nullptr;
+    if (routed_format < 0 || routed_format > MOE_B200_W4_G32_FP16_ROUNDED_DOWN) return nullptr;
     if (check_device(cfg->device, nullptr)) return nullptr;
     DeviceGuard guard(cfg->device);
-    const bool exact_down = routed_format == MOE_B200_W4_G32_FP16_EXACT;
-    const int f = exact_down ? MOE_B200_W4_G32_FP16 : routed_format;
+    const bool exact_down = routed_format != MOE_B200_W4_G32_FP16_ROUNDED_DOWN;
+    const int f = (routed_format == MOE_B200_W4_G32_FP16_EXACT ||
+                   routed_format == MOE_B200_W4_G32_FP16_ROUNDED_DOWN)
+                      ? MOE_B200_W4_G32_FP16
+                      : routed_format;
     auto* w = new moe_b200_weights();
     w->device = cfg->device;
     w->H = cfg->weights.hidden;
@@ -980,6 +1004,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     rc |= ws_alloc(ws, &ws->q_m, (n + pad_rows) * ws->Ki);
     rc |= ws_alloc(ws, &ws->s_m, n);
     rc |= ws_alloc(ws, &ws->y, n * ws->H);
+
     rc |= ws_alloc(ws, &ws->logits, T * (ws->E + 1));  // + the shared-gate column
     rc |= ws_alloc(ws, &ws->err, 1);
     if (ws->Is > 0 && rc == MOE_B200_OK) {
@@ -998,6 +1023,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     cudaMemset(ws->counters, 0, sizeof(int) * T);
     cudaMemset(ws->gv_counters, 0, sizeof(int) * (size_t)(n + T * ((ws->H + 127) / 128)));
     cudaMemset(ws->dec_state, 0, sizeof(uint32_t) * (size_t)(n + 2));
+
     {
         int coop = 0;
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ws->device);
@@ -1431,7 +1457,7 @@ int moe_b200_ep_pack(moe_b200_workspace* ws, int32_t rows, const float* d_x, con
 static int ep_expert_rows_impl(moe_b200_workspace* ws, const moe_b200_weights* w, int n,
                                const int8_t* d_q, const float* d_scale, const int32_t* d_expert,
                                const float* d_mask, float* d_y, cudaStream_t s) {
-    const int E = ws->E, H = ws->H, I = ws->I;
+    const int E = ws->E, H = ws->H;
     ws->launches += 6;
     // stage events of the profiling ring: schedule+gather, gate/up, requant, down
     cudaEvent_t* evs = prof_slot(ws, 0);
@@ -1449,16 +1475,13 @@ static int ep_expert_rows_impl(moe_b200_workspace* ws, const moe_b200_weights* w
     mark(3);
     const int nt = choose_nt(n, E);
     const int nt_g = exact_nt(nt, w->gu.fmt);
-    GemmArgs g = gemm_args(ws, w->gu, ws->s_perm, ws->offsets, E, n, ws->gate_up, 2 * I);
-    if (launch_gemm(ws->map_a[nt_index(nt_g)], g, w->gu.fmt, kEpiGateUp, nt_g, ws->num_sms, s))
-        return MOE_B200_ERR_UNSUPPORTED;
-    mark(4);
     const int dfmt = down_fmt(w->dn.fmt, w->exact_down);
     const bool hd = dfmt == kFmtW4G32H;
     const int nt_d = exact_nt(nt, dfmt);
-    launch_requant(ws->gate_up, ws->offsets + E, n, I, ws->Ki, kQuantMoe, ws->q_m,
-                   hd ? ws->q_m_h : nullptr, ws->s_m, s);
-    mark(5);
+    {
+        const int rc = run_gate_up(ws, w, n, nt_g, hd, s, mark);
+        if (rc) return rc;
+    }
     // down GEMM straight into the received order (permuted row p -> row perm[p])
     GemmArgs d = gemm_args(ws, w->dn, ws->s_m, ws->offsets, E, n, d_y, H);
     d.out_rows = ws->perm;

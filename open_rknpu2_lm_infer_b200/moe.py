@@ -112,9 +112,10 @@ class Backend:
 
     # ---- bank construction (src/npu/moe.rs:70-220) --------------------------
     def load_moe(self, gate: list[QuantMatrix], down: list[QuantMatrix], top: int,
-                 exact: bool = False) -> "Moe":
-        """exact: group-32 banks run the down GEMM on exact int32 group sums too
-        (MOE_B200_W4_G32_FP16_EXACT) instead of the fp16 tensor cores."""
+                 exact: bool = True) -> "Moe":
+        """exact=False: group-32 banks run the down GEMM on the fp16 tensor
+        cores (MOE_B200_W4_G32_FP16_ROUNDED_DOWN: w * s rounded to fp16, no
+        int32 down accumulators) instead of exact int32 group sums."""
         return self._load(gate, down, top, None, None, exact)
 
     def load_moe_with_shared(self, gate, down, top, shared: tuple[QuantMatrix, QuantMatrix],
@@ -125,7 +126,7 @@ class Backend:
         # the full-K variant is the default schedule here
         return self._load(gate, down, top, None, None)
 
-    def _load(self, gate, down, top, shared, mode, exact=False) -> "Moe":
+    def _load(self, gate, down, top, shared, mode, exact=True) -> "Moe":
         if not gate or len(gate) != len(down):
             raise ValueError("invalid expert bank")
         for m in [*gate, *down]:
@@ -177,8 +178,8 @@ class Backend:
         for i in range(e):
             table[i] = expert(gate[i], down[i])
         routed = fmts.pop()
-        if exact and routed == L.W4_G32_FP16:
-            routed = L.W4_G32_FP16_EXACT
+        if not exact and routed == L.W4_G32_FP16:
+            routed = L.W4_G32_FP16_ROUNDED_DOWN
         fmt = L.Format(routed, L.W8_PER_CHANNEL, L.SHARED_DENSE if mode is None else mode)
         if shared is not None:
             table[e] = expert(*shared)
