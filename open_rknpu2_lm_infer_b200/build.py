@@ -24,7 +24,7 @@ SOURCES = ["api.cu", "router.cu", "dispatch.cu", "gemm.cu", "gemv.cu", "exchange
 # the tensor-core rate probe (open_rknpu2_lm_infer_b200/mma_peak.py), a separate library
 PEAK_SOURCE = "mma_peak.cu"
 PEAK_LIB = PKG / "libmoe_b200_peak.so"
-HEADERS = ["common.cuh", "kernels.cuh"]
+HEADERS = ["common.cuh", "kernels.cuh", "quant.cuh", "route.cuh"]
 
 # -fmad=false: no implicit a*b+c contraction; every fused multiply-add in the
 # kernels is an explicit fmaf, so rounding matches the CPU restatement.

@@ -90,6 +90,48 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     }
 }
 
+// try_wait without a suspend-time hint: returns when the phase completes or
+// after a short system-dependent time.
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// The bounded wait of the pipelined kernels: polls without a suspend hint (a
+// thread suspended with a long hint was measured to resume well after the
+// phase completed), checks the abort flag and the time limit every 64 polls.
+static __device__ __noinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity,
+                                                   volatile int* abort_flag, uint32_t* err) {
+    const uint64_t start = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_poll(bar, parity)) return true;
+        if ((i & 63u) == 0u) {
+            if (*abort_flag) return false;
+            if (global_timer_ns() - start > kWaitLimitNs) {
+                *abort_flag = 1;
+                atomicOr(err, kErrWaitTimeout);
+                return false;
+            }
+        }
+    }
+}
+
+// Only the first poll inline: a loop issuing MMAs then holds one try_wait and
+// a branch per wait (an inline spin loop measured ~2x the per-MMA issue cost
+// of the issuing thread, even when never entered).
+__device__ __forceinline__ bool mbar_wait_fast(uint64_t* bar, uint32_t parity,
+                                               volatile int* abort_flag, uint32_t* err) {
+    if (mbar_poll(bar, parity)) return true;
+    return mbar_wait_spin(bar, parity, abort_flag, err);
+}
+
 // Programmatic dependent launch: a kernel launched with programmatic stream
 // serialization may start while its predecessor still runs. pdl_wait() blocks
 // until the predecessor grid has completed with its memory visible (it returns

@@ -21,6 +21,7 @@
 #include <algorithm>
 
 #include "kernels.cuh"
+#include "quant.cuh"
 
 namespace moe {
 
@@ -148,33 +149,6 @@ route_scatter_kernel(const int32_t* __restrict__ ids, const float* __restrict__ 
     }
 }
 
-__device__ __forceinline__ int quant_one(float x, float s, float inv, int rule) {
-    float v = rule == kQuantMoe ? __fdiv_rn(x, s) : roundf(__fmul_rn(x, inv));
-    int q = rule == kQuantMoe ? __float2int_rn(v) : (int)v;
-    return q > 127 ? 127 : (q < -127 ? -127 : q);
-}
-
-__device__ __forceinline__ uint32_t quant4(float4 v, float s, float inv, int rule) {
-    return (uint32_t)(quant_one(v.x, s, inv, rule) & 0xFF) |
-           ((uint32_t)(quant_one(v.y, s, inv, rule) & 0xFF) << 8) |
-           ((uint32_t)(quant_one(v.z, s, inv, rule) & 0xFF) << 16) |
-           ((uint32_t)(quant_one(v.w, s, inv, rule) & 0xFF) << 24);
-}
-
-// The four int8 codes of a packed word as two fp16 pairs (exact: |q| <= 127),
-// the activation operand of the fp16 tensor-core path of group-32 weights.
-__device__ __forceinline__ uint2 codes_to_half4(uint32_t packed) {
-    const __half2 a = __halves2half2(__int2half_rn((int8_t)(packed & 0xFF)),
-                                     __int2half_rn((int8_t)((packed >> 8) & 0xFF)));
-    const __half2 b = __halves2half2(__int2half_rn((int8_t)((packed >> 16) & 0xFF)),
-                                     __int2half_rn((int8_t)(packed >> 24)));
-    return make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
-}
-
-__device__ __forceinline__ float amax4(float4 v) {
-    return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-}
-
 // Block-wide max of non-negative values (blockDim.x a multiple of 32, <= 1024).
 __device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
@@ -184,13 +158,6 @@ __device__ __forceinline__ float block_max(float v, float* red) {
     float m = red[0];
     for (int i = 1; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
     return m;
-}
-
-__device__ __forceinline__ float row_scale(float m, int rule) {
-    if (m == 0.0f) return 1.0f;
-    float s = __fdiv_rn(m, 127.0f);
-    if (rule == kQuantDense && !(s >= FLT_MIN)) s = FLT_MIN;
-    return s;
 }
 
 // One CTA (256 threads) per token: the row is read once into registers
@@ -251,14 +218,6 @@ quant_gather_kernel(const float* __restrict__ x, int H, int ld_q, int rule, int 
             }
         }
     }
-}
-
-// SwiGLU of x86 native/cpu_kernels/swiglu.cpp:23-25 with the gate/up split of
-// Cpu::swiglu (src/model/cpu.rs:269-294): h = (g / (1 + exp(-g))) * u, IEEE
-// division and multiply (no contraction).
-__device__ __forceinline__ float silu_mul(float g, float u) {
-    const float d = __fadd_rn(1.0f, expf(-g));
-    return __fmul_rn(__fdiv_rn(g, d), u);
 }
 
 // One CTA (128 threads) per permuted row; rows >= *count exit. Reads the row's

@@ -62,9 +62,10 @@ constexpr int kTileRows = 128;        // weight rows per tile (MMA M)
 constexpr int kKBlock = 128;          // int8 k per k-block (one 128-byte swizzle row)
 constexpr int kStageK = kKPS * kKBlock;  // k per load stage (256)
 // Shared memory: the load ring gets what is left of 227 KB after the tile
-// tables (up to 1024 experts), barriers and the 1 KB alignment slack.
+// tables and grouping offsets (up to 1024 experts), barriers and the 1 KB
+// alignment slack.
 constexpr int kSmemTotal = 227 * 1024;
-constexpr int kSmemFixed = 10 * 1024;
+constexpr int kSmemFixed = 14 * 1024;
 constexpr int kMaxLoadStages = 8;
 constexpr bool kGroupDual = true;  // exact group path, 16-token tiles: two CTAs per SM
 constexpr uint32_t kMagicBits = 0x4B400000u;  // 12582912.0f
@@ -96,7 +97,9 @@ struct GemmCfg {
     // weights of one stage in HBM and the part of them one request copies
     static constexpr int kStageWStride = kG32Pack ? 128 * 128 + 128 * 16
                                                   : kKPS * kTileRows * (kW4 ? kKBlock / 2 : kKBlock);
-    static constexpr int kStageW = kGroup ? 128 * 128 : kStageWStride;
+    // (the exact group path copies the stage's group scales too: the epilogue
+    // reads them from shared memory)
+    static constexpr int kStageW = kStageWStride;
     // activations of one stage: int8 kKPS atoms of NT x 128 B, fp16 2*kKPS
     static constexpr int kAtoms = kF16 ? 2 * kKPS : kKPS;
     static constexpr int kStageAct = kAtoms * NT * 128;
@@ -136,14 +139,6 @@ struct GemmCfg {
     static_assert(kNSlot >= 2, "TMEM budget: the exact group path needs NT <= 32");
     static_assert(kARegion + kNSlot * kSlotCols <= 512, "TMEM budget");
     static_assert(kHalf % 2 == 0, "paired f32x2 epilogue math");
-};
-
-// Group scales of (tile, stage) for one weight row: 16 bytes (8 groups of
-// fp16) after the stage's weights, read through the read-only path two stages
-// ahead of use.
-struct ScaleCursor {
-    int t, st;
-    const uint8_t* base;  // weights of the current tile
 };
 
 struct TileCoord {
@@ -210,6 +205,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     uint64_t* done = tempty + C::kNSlot;
     int* tcnt = reinterpret_cast<int*>(done + 1);
     int* tb = tcnt + a.num_experts + 1;
+    int* offs = tb + a.num_experts + 1;  // the grouping offsets, read once
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_s;
     __shared__ int total_tiles_s;
@@ -223,7 +219,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
         abort_s = 0;
         for (int i = 0; i < SL; ++i) {
             mbar_init(&lfull[i], 1);
-            mbar_init(&lempty[i], 1);
+            // exact group path: the MMA commit and every epilogue warp (the stage
+            // holds the group scales the epilogue reads)
+            mbar_init(&lempty[i], C::kGroup ? 1 + kEpiWarps : 1);
         }
         for (int i = 0; i < AS; ++i) mbar_init(&ofull[i], C::kConvWarps);
         for (int i = 0; i < C::kNSlot; ++i) {
@@ -240,8 +238,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
         for (int i = 0; i < per; ++i) {
             int e = lane * per + i;
             if (e < E) {
-                int m = a.offsets[e + 1] - a.offsets[e];
-                int c = (m + NT - 1) / NT;
+                const int o0 = a.offsets[e], o1 = a.offsets[e + 1];
+                offs[e] = o0;
+                if (e == E - 1) offs[E] = o1;
+                int c = (o1 - o0 + NT - 1) / NT;
                 tcnt[e] = c;
                 local += c;
             }
@@ -279,6 +279,18 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     // lane quadrant of this warp's TMEM accesses
     const int quad = warp & 3;
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
+    if constexpr (C::kGroup) {
+        // every group buffer starts as the bits of 12582912.0f: the MMAs
+        // accumulate onto them, the epilogue re-arms a slot after reading it
+        if (warp >= C::kEpiWarp0) {
+            const int c0 = ((warp - C::kEpiWarp0) >> 2) * C::kHalf;
+            for (int sl = 0; sl < C::kNSlot; ++sl)
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    tmem_fill<C::kHalf>(acc_base + lane_addr + sl * C::kSlotCols + j * NT + c0, kMagicBits);
+            tmem_wait_st();
+        }
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -290,7 +302,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
                 const TileCoord c = decode_tile(t, tb, tcnt, E);
-                const int row0 = a.offsets[c.e] + c.mt * NT;
+                const int row0 = offs[c.e] + c.mt * NT;
                 const uint8_t* wtile = a.w + (size_t)c.e * a.w_expert_stride +
                                        (size_t)c.rt * a.w_tile_stride;
                 for (int st = 0; st < kstages; ++st, ++it) {
@@ -322,7 +334,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                 uint32_t dcol = 0;
                 if (!C::kGroup) {
                     const uint32_t buf = ti % 2u;
-                    if (!mbar_wait(&tempty[buf], ((ti / 2u) & 1u) ^ 1u, abort_flag, a.err)) break;
+                    if (!mbar_wait_fast(&tempty[buf], ((ti / 2u) & 1u) ^ 1u, abort_flag, a.err)) break;
                     tc_fence_after();
                     dcol = buf * NT;
                 }
@@ -331,8 +343,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                     const int ao = it % AS1;
                     // W4 stages: the unpack warps' barrier alone (they waited for the
                     // stage's copies before arriving); W8 stages: the copies
-                    if (C::kW4 ? !mbar_wait(&ofull[ao], (it / AS1) & 1u, abort_flag, a.err)
-                               : !mbar_wait(&lfull[s], (it / SL) & 1u, abort_flag, a.err)) {
+                    if (C::kW4 ? !mbar_wait_fast(&ofull[ao], (it / AS1) & 1u, abort_flag, a.err)
+                               : !mbar_wait_fast(&lfull[s], (it / SL) & 1u, abort_flag, a.err)) {
                         ok = false;
                         break;
                     }
@@ -353,7 +365,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                             uint32_t slot = 0;
                             if (C::kGroup) {
                                 slot = kbc % C::kNSlot;
-                                if (!mbar_wait(&tempty[slot], ((kbc / C::kNSlot) & 1u) ^ 1u, abort_flag,
+                                if (!mbar_wait_fast(&tempty[slot], ((kbc / C::kNSlot) & 1u) ^ 1u, abort_flag,
                                                a.err)) {
                                     ok = false;
                                     break;
@@ -370,7 +382,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                                 const uint32_t d = C::kGroup ? acc_base + slot * C::kSlotCols + j * NT
                                                              : acc_base + dcol;
                                 const uint32_t acc =
-                                    C::kGroup ? 0u : ((st > 0 || jk > 0 || j > 0) ? 1u : 0u);
+                                    C::kGroup ? 1u : ((st > 0 || jk > 0 || j > 0) ? 1u : 0u);
                                 if (C::kW4)
                                     mma_i8_ts(d, a_tmem + jk * 32 + 8 * j, db, idesc, acc);
                                 else
@@ -496,40 +508,169 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
         const int half = (warp - C::kEpiWarp0) >> 2;  // column half (0..1)
         const int r = quad * 32 + lane;             // weight row within the tile = TMEM lane
         const int c0 = half * C::kHalf;             // first token column of this warp
-        // group scales: a cursor two stages ahead of use over the same tile order
-        ScaleCursor cur{(int)blockIdx.x, 0, nullptr};
-        auto cursor_tile = [&](ScaleCursor& k) {
-            k.base = nullptr;
-            if (k.t < total) {
-                const TileCoord c = decode_tile(k.t, tb, tcnt, E);
-                k.base = a.w + (size_t)c.e * a.w_expert_stride + (size_t)c.rt * a.w_tile_stride;
+        if constexpr (C::kGroup) {
+            // Exact group path. A tile's coordinates are worked out, and its
+            // activation scales loaded, during the tile before (between its first
+            // TMEM loads and their wait): nothing at a tile boundary waits for
+            // memory or for the binary search of the tile table.
+            struct TileInfo {
+                int row0, nvalid;
+                int oc;    // this lane's output column (gate | up rows: up at n + channel), -1: none
+                float sx;  // lane q: the activation scale of token column c0 + q
+            };
+            auto tile_info = [&](int t) -> TileInfo {
+                TileInfo ti_{0, 0, -1, 0.0f};
+                if (t >= total) return ti_;
+                const TileCoord c = decode_tile(t, tb, tcnt, E);
+                ti_.row0 = offs[c.e] + c.mt * NT;
+                ti_.nvalid = min(NT, offs[c.e + 1] - ti_.row0);
+                const bool swiglu_tile = (EPI == kEpiGateUp) || (EPI == kEpiAcc && a.swiglu_layout);
+                const bool is_up = swiglu_tile && r >= 64;
+                const int col = swiglu_tile ? c.rt * 64 + (r & 63) : c.rt * kTileRows + r;
+                if (col < a.n_valid) ti_.oc = is_up ? a.n_valid + col : col;
+                if (EPI != kEpiAcc && lane < C::kHalf && c0 + lane < ti_.nvalid)
+                    ti_.sx = __ldg(a.act_scale + ti_.row0 + c0 + lane);
+                return ti_;
+            };
+            TileInfo cur = tile_info(blockIdx.x), nxt = cur;
+            uint32_t it = 0, ist = 0;  // k-blocks and load stages seen
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                const int row0 = cur.row0, nvalid = cur.nvalid, ocol = cur.oc;
+                const bool col_ok = cur.oc >= 0;
+                bool side_done = false;
+                auto side = [&]() { nxt = tile_info(t + gridDim.x); };
+                float2 facc[C::kHalf / 2];
+#pragma unroll
+                for (int q = 0; q < C::kHalf / 2; ++q) facc[q] = make_float2(0.0f, 0.0f);
+                const bool active = c0 < nvalid;  // idle warps still take part in the handshakes
+                for (int st = 0; st < kstages && ok; ++st, ++ist) {
+                    float2 sg[4];
+#pragma unroll 1
+                    for (int jk = 0; jk < kKPS; ++jk, ++it) {
+                        const int kb = st * kKPS + jk;
+                        const uint32_t slot = it % C::kNSlot;
+                        if (!mbar_wait(&tfull[slot], (it / C::kNSlot) & 1u, abort_flag, a.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        if (jk == 0) {
+                            // the stage's 8 group scales of row r (k-block jk, group j at
+                            // 4 * jk + j) from the load stage, whose refill waits for
+                            // every epilogue warp; the 1/16 of the W4 codes folded in
+                            const uint8_t* ws = w_at(ist % SL) + 128 * 128;
+                            const uint4 sc = *reinterpret_cast<const uint4*>(ws + r * 16);
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&lempty[ist % SL]);
+                            const uint32_t w[4] = {sc.x, sc.y, sc.z, sc.w};
+#pragma unroll
+                            for (int i = 0; i < 4; ++i)
+                                sg[i] = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&w[i])),
+                                                   make_float2(0.0625f, 0.0625f));
+                        }
+                        const float2 sga = jk ? sg[2] : sg[0];  // groups 0, 1 of this k-block
+                        const float2 sgb = jk ? sg[3] : sg[1];  // groups 2, 3
+                        const uint32_t sbase = acc_base + lane_addr + slot * C::kSlotCols + c0;
+                        // rounds of 8 token columns x 4 groups bound the registers; each
+                        // round is loaded, re-armed and folded into its columns' sums
+                        // (the group order per column stays 0..3)
+                        constexpr int kRound = C::kHalf < 8 ? C::kHalf : 8;
+#pragma unroll
+                        for (int r0 = 0; r0 < C::kHalf && active; r0 += kRound) {
+                            uint32_t v[4][kRound];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) tmem_ld<kRound>(sbase + j * NT + r0, v[j]);
+                            if (!side_done) {
+                                // in the shadow of the loads: the previous tile's
+                                // outputs, the next tile's coordinates
+                                side();
+                                side_done = true;
+                            }
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) tmem_ld_pin(v[j]);
+                            if (EPI == kEpiAcc) {
+#pragma unroll
+                                for (int j = 0; j < 4; ++j)
+#pragma unroll
+                                    for (int q = 0; q < kRound; ++q)
+                                        if (c0 + r0 + q < nvalid && col_ok)
+                                            a.acc_out[((size_t)(row0 + c0 + r0 + q) * (a.kblocks * 4) + kb * 4 +
+                                                       j) * a.acc_ld + ocol] =
+                                                (int)(v[j][q] - kMagicBits) >> 4;
+                            } else {
+                                // the buffer holds the int32 0x4B400000 + 16 * acc, whose
+                                // bits are the float 12582912 + 16 * acc (|16 * acc| < 2^22)
+                                const float2 nm = make_float2(-kMagic, -kMagic);
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) {
+                                    const float2 sp = (j >> 1) ? sgb : sga;
+                                    const float sj = (j & 1) ? sp.y : sp.x;
+                                    const float2 s2 = make_float2(sj, sj);
+#pragma unroll
+                                    for (int q = 0; q < kRound / 2; ++q) {
+                                        const float2 d = __fadd2_rn(
+                                            make_float2(__uint_as_float(v[j][2 * q]),
+                                                        __uint_as_float(v[j][2 * q + 1])),
+                                            nm);
+                                        facc[r0 / 2 + q] = __ffma2_rn(d, s2, facc[r0 / 2 + q]);
+                                    }
+                                }
+                            }
+                        }
+                        {
+                            const uint32_t sb = acc_base + lane_addr + slot * C::kSlotCols + c0;
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) tmem_fill<C::kHalf>(sb + j * NT, kMagicBits);
+                            tmem_wait_st();
+                        }
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[slot]);
+                        if (!side_done) {  // a warp with no valid column loads nothing
+                            side();
+                            side_done = true;
+                        }
+                    }
+                }
+                if (!ok) break;
+                if (EPI != kEpiAcc) {
+#pragma unroll
+                    for (int q = 0; q < C::kHalf; ++q) {
+                        const int j = c0 + q;
+                        const float val = __fmul_rn((q & 1) ? facc[q >> 1].y : facc[q >> 1].x,
+                                                    __shfl_sync(0xffffffffu, cur.sx, q));
+                        if (j < nvalid && col_ok) {
+                            const int orow = (EPI == kEpiStore && a.out_rows) ? a.out_rows[row0 + j] : row0 + j;
+                            a.out[(size_t)orow * a.ldo + ocol] = val;
+                        }
+                    }
+                }
+                cur = nxt;
             }
+            if (!ok) *abort_flag = 1;
+        } else {
+        // the activation scales of a tile (lane q: token column c0 + q), loaded
+        // a whole tile ahead of use: at a tile boundary the epilogue then
+        // reads nothing from global memory before its first accumulator
+        auto tile_sx = [&](int t) -> float {
+            if (t >= total) return 0.0f;
+            const TileCoord c = decode_tile(t, tb, tcnt, E);
+            const int row0 = offs[c.e] + c.mt * NT;
+            const int nvalid = min(NT, offs[c.e + 1] - row0);
+            return (lane < C::kHalf && c0 + lane < nvalid) ? __ldg(a.act_scale + row0 + c0 + lane) : 0.0f;
         };
-        auto cursor_load = [&](ScaleCursor& k) -> uint4 {
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (k.base)
-                v = __ldg(reinterpret_cast<const uint4*>(k.base + (size_t)k.st * a.w_stage_stride +
-                                                         C::kStageW + r * 16));
-            if (++k.st == kstages) {
-                k.st = 0;
-                k.t += gridDim.x;
-                cursor_tile(k);
-            }
-            return v;
-        };
-        uint4 pf0 = make_uint4(0u, 0u, 0u, 0u), pf1 = pf0;
-        if (C::kGroup && EPI != kEpiAcc) {
-            cursor_tile(cur);
-            pf0 = cursor_load(cur);
-            pf1 = cursor_load(cur);
-        }
-        uint32_t ti = 0, it = 0;
+        float next_sx = tile_sx(blockIdx.x);
+        uint32_t ti = 0;  // tiles seen
         bool ok = true;
         for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++ti) {
             const TileCoord c = decode_tile(t, tb, tcnt, E);
-            const int m_e = a.offsets[c.e + 1] - a.offsets[c.e];
-            const int row0 = a.offsets[c.e] + c.mt * NT;
+            const int m_e = offs[c.e + 1] - offs[c.e];
+            const int row0 = offs[c.e] + c.mt * NT;
             const int nvalid = min(NT, m_e - c.mt * NT);
+            const float my_sx = next_sx;
+            next_sx = tile_sx(t + gridDim.x);
             // output channel of this lane (gate/up tiles: 64 gate rows then 64 up rows)
             const bool swiglu_tile = (EPI == kEpiGateUp) || (EPI == kEpiAcc && a.swiglu_layout);
             int col;
@@ -543,99 +684,6 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             const bool col_ok = col < a.n_valid;
             const int ocol = is_up ? a.n_valid + col : col;  // gate | up halves of a row
 
-            // lane q prefetches the scale of token column c0 + q; broadcast by shuffles
-            const float my_sx = (lane < C::kHalf && c0 + lane < nvalid) ? a.act_scale[row0 + c0 + lane]
-                                                                        : 0.0f;
-            if constexpr (C::kGroup) {
-                // one slot of 4 group buffers per k-block: load, re-arm, release, fold
-                float2 facc[C::kHalf / 2];
-#pragma unroll
-                for (int q = 0; q < C::kHalf / 2; ++q) facc[q] = make_float2(0.0f, 0.0f);
-                const bool active = c0 < nvalid;  // idle warps still take part in the handshakes
-                for (int st = 0; st < kstages && ok; ++st) {
-                    const uint4 sc = pf0;
-                    pf0 = pf1;
-                    pf1 = cursor_load(cur);
-                    // the stage's 8 group scales (k-block jk, group j at 4*jk + j), with
-                    // the 1/16 of the W4 codes folded in (exact)
-                    float2 sg[4];
-                    {
-                        const uint32_t w[4] = {sc.x, sc.y, sc.z, sc.w};
-#pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            sg[i] = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&w[i])),
-                                               make_float2(0.0625f, 0.0625f));
-                    }
-#pragma unroll 1
-                    for (int jk = 0; jk < kKPS; ++jk, ++it) {
-                        const int kb = st * kKPS + jk;
-                        const float2 sga = jk ? sg[2] : sg[0];  // groups 0, 1 of this k-block
-                        const float2 sgb = jk ? sg[3] : sg[1];  // groups 2, 3
-                        const uint32_t slot = it % C::kNSlot;
-                        if (!mbar_wait(&tfull[slot], (it / C::kNSlot) & 1u, abort_flag, a.err)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const uint32_t sbase = acc_base + lane_addr + slot * C::kSlotCols + c0;
-                        // rounds of 8 token columns x 4 groups bound the registers; each
-                        // round is loaded, re-armed and folded into its columns' sums
-                        // (the group order per column stays 0..3)
-                        constexpr int kRound = C::kHalf < 8 ? C::kHalf : 8;
-#pragma unroll
-                        for (int r0 = 0; r0 < C::kHalf && active; r0 += kRound) {
-                            uint32_t v[4][kRound];
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) tmem_ld<kRound>(sbase + j * NT + r0, v[j]);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) tmem_ld_pin(v[j]);
-                            if (EPI == kEpiAcc) {
-#pragma unroll
-                                for (int j = 0; j < 4; ++j)
-#pragma unroll
-                                    for (int q = 0; q < kRound; ++q)
-                                        if (c0 + r0 + q < nvalid && col_ok)
-                                            a.acc_out[((size_t)(row0 + c0 + r0 + q) * (a.kblocks * 4) + kb * 4 +
-                                                       j) * a.acc_ld + ocol] = (int)v[j][q] >> 4;
-                            } else {
-                                // int32 -> f32 exactly: the bits of 12582912.0f plus the
-                                // sum are the float 12582912 + sum (|sum| < 2^22)
-                                const float2 nm = make_float2(-kMagic, -kMagic);
-#pragma unroll
-                                for (int j = 0; j < 4; ++j) {
-                                    const float2 sp = (j >> 1) ? sgb : sga;
-                                    const float sj = (j & 1) ? sp.y : sp.x;
-                                    const float2 s2 = make_float2(sj, sj);
-#pragma unroll
-                                    for (int q = 0; q < kRound / 2; ++q) {
-                                        const float2 d = __fadd2_rn(
-                                            make_float2(__uint_as_float(v[j][2 * q] + kMagicBits),
-                                                        __uint_as_float(v[j][2 * q + 1] + kMagicBits)),
-                                            nm);
-                                        facc[r0 / 2 + q] = __ffma2_rn(d, s2, facc[r0 / 2 + q]);
-                                    }
-                                }
-                            }
-                        }
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&tempty[slot]);
-                    }
-                }
-                if (EPI == kEpiAcc || !ok) continue;
-#pragma unroll
-                for (int q = 0; q < C::kHalf; ++q) {
-                    const int j = c0 + q;
-                    const float sxq = __shfl_sync(0xffffffffu, my_sx, q);
-                    const float f = (q & 1) ? facc[q >> 1].y : facc[q >> 1].x;
-                    if (j < nvalid && col_ok) {
-                        const int orow = (EPI == kEpiStore && a.out_rows) ? a.out_rows[row0 + j] : row0 + j;
-                        a.out[(size_t)orow * a.ldo + (EPI == kEpiGateUp ? ocol : col)] = __fmul_rn(f, sxq);
-                    }
-                }
-                continue;
-            }
 
             float wscale_pc = 0.0f;
             if (!C::kF16) {
@@ -685,6 +733,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             }
         }
         if (!ok) *abort_flag = 1;
+        }  // per-channel formats
     }
 
     tc_fence_before();
@@ -702,7 +751,7 @@ static size_t gemm_smem_bytes(int E) {
     b += (size_t)C::kLoadStages * C::kLoadBytes;
     b += sizeof(uint64_t) * (2 * C::kLoadStages + (C::kAStages > 0 ? C::kAStages : 1) +
                              2 * C::kNSlot + 1);
-    b += sizeof(int) * (2 * (size_t)E + 2);
+    b += sizeof(int) * (3 * (size_t)E + 3);
     // one CTA per SM: the kernel allocates all 512 TMEM columns
     // one CTA per SM (it allocates all 512 TMEM columns) unless two share it
     return (C::kCtasPerSm == 1 && b < 120 * 1024) ? 120 * 1024 : b;
