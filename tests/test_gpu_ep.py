@@ -2,13 +2,15 @@
 
 One GPU plays every rank: the EP forward with one rank, and two ranks each
 owning half of the experts with the all-to-all done by hand, must reproduce
-the single-device layer (moe_b200_forward_device) bit for bit.
+the single-device layer (moe_b200_forward_device) bit for bit, and the CPU
+restatement of the reference layer within 1e-2 rel / 1e-3 abs.
 """
 from __future__ import annotations
 
 import numpy as np
 import pytest
 
+from conftest import assert_close
 from open_rknpu2_lm_infer_b200 import synthetic as S
 from open_rknpu2_lm_infer_b200.ep import DeviceOps, ep_forward
 from open_rknpu2_lm_infer_b200.moe import Backend
@@ -47,7 +49,7 @@ def _rank(world, g, layer, rows):
     return be, moe, router, DeviceOps(be, moe, router, world, rows)
 
 
-def test_ep_one_rank_matches_single_device(cuda):
+def test_ep_one_rank_matches_single_device(cuda, oracle):
     torch = cuda
     layer = S.make_layer(SPEC, seed=5)
     x = torch.from_numpy(S.make_input(SPEC, T, seed=6)).cuda()
@@ -59,10 +61,12 @@ def test_ep_one_rank_matches_single_device(cuda):
     ops.status()
     assert plan.n_send == plan.n_recv == T * SPEC.top
     assert np.array_equal(out.cpu().numpy(), ref)
+    assert_close(out.cpu().numpy(), oracle.OracleLayer(layer).forward(x.cpu().numpy(), res.cpu().numpy()),
+                 what="EP one rank vs restatement")
     ops.close(); moe.close(); router.close(); be.close()
 
 
-def test_ep_two_ranks_by_hand_match_single_device(cuda):
+def test_ep_two_ranks_by_hand_match_single_device(cuda, oracle):
     torch = cuda
     world = 2
     layer = S.make_layer(SPEC, seed=5)
@@ -95,6 +99,9 @@ def test_ep_two_ranks_by_hand_match_single_device(cuda):
         torch.cuda.synchronize()
         ops[a].status()
         assert np.array_equal(out.cpu().numpy(), refs[a]), f"rank {a} differs"
+        assert_close(out.cpu().numpy(),
+                     oracle.OracleLayer(layer).forward(xs[a].cpu().numpy(), rs[a].cpu().numpy()),
+                     what=f"EP rank {a} vs restatement")
     for be, moe, router, op in ranks:
         op.close(); moe.close(); router.close(); be.close()
 

@@ -49,13 +49,17 @@ def _rank_setup(world, g, layer):
     return be, moe, router, DeviceOps(be, moe, router, world, T)
 
 
-def test_exchange_one_rank_matches_single_device_and_replays(cuda):
+def test_exchange_one_rank_matches_single_device_and_replays(cuda, oracle):
     torch = cuda
     from open_rknpu2_lm_infer_b200.ep import DeviceExchange, ep_forward_device
     layer = S.make_layer(SPEC, seed=5)
     x = torch.from_numpy(S.make_input(SPEC, T, seed=6)).cuda()
     res = torch.from_numpy(S.make_input(SPEC, T, seed=7, stream=5)).cuda()
     ref = _single(torch, layer, x, res)
+    # the single-device layer itself against the CPU restatement
+    from conftest import assert_close
+    assert_close(ref, oracle.OracleLayer(layer).forward(x.cpu().numpy(), res.cpu().numpy()),
+                 what="single-device layer vs restatement")
     be, moe, router, ops = _rank_setup(1, 0, layer)
     ex = DeviceExchange(ops, None)
     for _ in range(2):  # the step counter advances; results repeat
@@ -81,7 +85,7 @@ def test_exchange_one_rank_matches_single_device_and_replays(cuda):
     ex.close(); ops.close(); moe.close(); router.close(); be.close()
 
 
-def test_exchange_wait_gives_up_and_the_exchange_recovers(cuda):
+def test_exchange_wait_gives_up_and_the_exchange_recovers(cuda, oracle):
     """A wait that nothing completes ends with an error, not a hang: the
     exchange's row wait on a step that no source dispatches gives up after its
     limit (~2 s) and the status reports MOE_B200_ERR_DEVICE_TIMEOUT; the
@@ -94,6 +98,10 @@ def test_exchange_wait_gives_up_and_the_exchange_recovers(cuda):
     x = torch.from_numpy(S.make_input(SPEC, T, seed=6)).cuda()
     res = torch.from_numpy(S.make_input(SPEC, T, seed=7, stream=5)).cuda()
     ref = _single(torch, layer, x, res)
+    # the single-device layer itself against the CPU restatement
+    from conftest import assert_close
+    assert_close(ref, oracle.OracleLayer(layer).forward(x.cpu().numpy(), res.cpu().numpy()),
+                 what="single-device layer vs restatement")
     be, moe, router, ops = _rank_setup(1, 0, layer)
     ex = DeviceExchange(ops, None)
     ex.probe_timeout()
@@ -138,7 +146,12 @@ def _two_rank_main(rank, world, port, outdir):
         torch.cuda.synchronize()
         ex.status(); ops.status()
         same = all(np.array_equal(o.cpu().numpy(), ref) for o in outs)
-        np.save(os.path.join(outdir, f"ok{rank}.npy"), np.array([same]))
+        # and the CPU restatement of the reference layer on this rank's tokens
+        from oracle import oracle as O
+        want = O.OracleLayer(layer).forward(x.cpu().numpy(), res.cpu().numpy())
+        got = outs[-1].cpu().numpy().astype(np.float64)
+        close = bool(np.all(np.abs(got - want) <= 1e-3 + 1e-2 * np.abs(want)))
+        np.save(os.path.join(outdir, f"ok{rank}.npy"), np.array([same and close]))
         dist.barrier()  # every rank done with its peers' memory before unmapping
         ex.close(); ops.close(); moe.close(); router.close(); be.close()
     finally:

@@ -3,10 +3,13 @@ moe_b200_export_expert / import_expert / swap_slots; experts.Pager).
 
 A bank assembled slot by slot from exported blobs, in a permuted slot order,
 must compute the resident layer bit for bit once the expert ids are mapped to
-their slots; so must the pager, with a window smaller than the demand."""
+their slots; so must the pager, with a window smaller than the demand. Both
+are also checked against the CPU restatement of the reference layer (within
+1e-2 rel / 1e-3 abs)."""
 import numpy as np
 import pytest
 
+from conftest import assert_close
 from open_rknpu2_lm_infer_b200 import _lib as L
 from open_rknpu2_lm_infer_b200 import synthetic as S
 from open_rknpu2_lm_infer_b200.experts import Geometry, Pager, Store, Writer
@@ -18,7 +21,7 @@ FORMATS = {"w4g32": L.W4_G32_FP16, "w4pc": L.W4_PER_CHANNEL, "w8pc": L.W8_PER_CH
 
 
 @pytest.mark.parametrize("routed", ["w4g32", "w4pc", "w8pc"])
-def test_slot_bank_from_blobs_matches_resident_bank(cuda, routed):
+def test_slot_bank_from_blobs_matches_resident_bank(cuda, oracle, routed):
     spec = S.small_spec("c2", experts=16, routed=routed)
     layer = S.make_layer(spec, seed=21)
     T = 33
@@ -41,7 +44,10 @@ def test_slot_bank_from_blobs_matches_resident_bank(cuda, routed):
     slots = be.moe_packed(spec.hidden, spec.inter, spec.experts, spec.top, FORMATS[routed])
     for e in range(spec.experts):
         slots.import_(int(perm[e]), blobs[e])
-    assert np.array_equal(run(slots, perm[ids]), ref)
+    got = run(slots, perm[ids])
+    assert np.array_equal(got, ref)
+    # the restatement with the same routing, on the original expert ids
+    assert_close(got, oracle.OracleLayer(layer).run(x, ids, routes), what=f"{routed} slot bank")
     # blobs round-trip through the slot bank unchanged
     assert slots.export(int(perm[5])) == blobs[5]
     # a staging bank: promote swaps a staged expert into a live slot
@@ -63,7 +69,7 @@ def test_slot_bank_from_blobs_matches_resident_bank(cuda, routed):
 
 
 @pytest.mark.parametrize("slots_n,T", [(16, 1), (8, 40), (8, 1)])
-def test_pager_matches_resident_layer(cuda, tmp_path, slots_n, T):
+def test_pager_matches_resident_layer(cuda, oracle, tmp_path, slots_n, T):
     torch = cuda
     spec = S.small_spec("c2", experts=32)
     layer = S.make_layer(spec, seed=31)
@@ -88,6 +94,8 @@ def test_pager_matches_resident_layer(cuda, tmp_path, slots_n, T):
                         torch.from_numpy(routes).cuda(), torch.from_numpy(res).cuda())
         torch.cuda.synchronize()
         assert np.array_equal(out.cpu().numpy(), ref), f"step {step}"
+        assert_close(out.cpu().numpy(), oracle.OracleLayer(layer).forward(x, res),
+                     what=f"pager step {step} vs restatement")
     st = pager.stats
     assert st.calls == 3 and st.imports >= min(slots_n, st.unique_demand // 3)
     if slots_n < spec.experts and T > 1:
