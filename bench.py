@@ -43,7 +43,18 @@ CONFIG = "c2"
 TOKENS = 512
 SEED = 1234
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
-INT8_DENSE_TOPS = 4500.0  # B200 datasheet dense int8 (TOPS); not yet measured here
+INT8_DATASHEET_TOPS = 4500.0  # B200 datasheet dense int8, for context only
+
+
+def int8_peak():
+    """Dense int8 tensor-core rate measured on this GPU by the tcgen05 probe
+    (open_rknpu2_lm_infer_b200/mma_peak.py: M=128 x N=256 x K=32 MMAs back to
+    back on every SM), in TOPS; the datasheet figure if the probe is missing."""
+    try:
+        from open_rknpu2_lm_infer_b200 import mma_peak
+        return mma_peak.int8_peak_tops(), "measured (tcgen05 kind::i8 probe, this GPU)"
+    except Exception as e:  # the probe library is built with the package
+        return INT8_DATASHEET_TOPS, f"datasheet ({type(e).__name__})"
 
 
 def peaks():
@@ -124,22 +135,35 @@ def measured_traffic(key: str):
 
 
 def layer_bytes(spec, T, U, A):
-    """Algorithmic HBM bytes of one layer call (weights of the U experts hit,
-    router, activations in/out, residual)."""
+    """Algorithmic HBM bytes of one layer call, the formula of the hot-path
+    plan: the int4 codes + fp16 group scales of the U experts hit, the f32
+    router, x in, residual in, out."""
     H, I = spec.hidden, spec.inter
     w = 3 * H * I // 2 + 3 * H * I // 32 * 2          # int4 codes + fp16 group scales
-    b = U * w + spec.experts * H * 4 + 3 * T * H * 4  # router f32, x in, residual, out
-    # permuted int8 rows; gate | up f32 written and read; middle codes int8 + fp16; y
-    b += A * H + A * 2 * I * 4 * 2 + A * I * 3 + A * H * 4 * 2
-    return b
+    return U * w + spec.experts * H * 4 + 3 * T * H * 4
+
+
+def layer_bytes_with_intermediates(spec, T, U, A):
+    """The same plus the intermediates this design writes and reads back: the
+    permuted int8 activation rows, the f32 SwiGLU middle and its int8 codes,
+    the f32 expert rows y (written by the down GEMM, read by the combine)."""
+    H, I = spec.hidden, spec.inter
+    return (layer_bytes(spec, T, U, A) + A * H * 2 + A * I * 4 * 2 + A * I * 2 +
+            A * H * 4 * 2)
 
 
 def gate_up_bytes(spec, U, A):
     """Algorithmic bytes of one gate/up GEMM launch: int4 codes + fp16 scales of
-    the experts hit, the permuted int8 activation rows, the f32 gate | up rows
-    written."""
+    the experts hit, the permuted int8 activation rows, the f32 SwiGLU middle
+    rows written (SwiGLU and the requantisation run in its epilogue) and their
+    int8 codes."""
     H, I = spec.hidden, spec.inter
-    return U * (2 * I * H // 2 + 2 * I * H // 32 * 2) + A * H + A * 2 * I * 4
+    return U * (2 * I * H // 2 + 2 * I * H // 32 * 2) + A * H + A * I * 4 + A * I
+
+
+def gate_up_ops(spec, A):
+    """int8 tensor-core ops of one gate/up launch (2 per multiply-add)."""
+    return 2 * A * 2 * spec.inter * spec.hidden
 
 
 # ---------------------------------------------------------------- ours
@@ -247,7 +271,8 @@ def run_ours(args):
     traffic = measured_traffic(f"{CONFIG}_T{T}_gate_up")
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                 "frac": (achieved / hbm_peak) if achieved else None, "traffic": traffic,
-                "kernel": "grouped_gemm_kernel<W4G32, GateUp> (gate/up, exact int8 group sums)",
+                "kernel": "group_gemm_kernel<GateUpQ> (gate/up + SwiGLU + requantisation, "
+                          "exact int32 group sums)",
                 "algorithmic_bytes_per_launch": gu_bytes, "kernel_us": gate_us,
                 "peak_kind": f"{pk_kind} (hbm_gbs, STREAM-style copy)"}
 
@@ -257,6 +282,7 @@ def run_ours(args):
     value = world * T / (ms * 1e-3)
     lbytes = layer_bytes(spec, T, U, A)
     ops = 2 * A * 3 * spec.hidden * spec.inter
+    i8_peak, i8_kind = int8_peak()
     result = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -266,7 +292,9 @@ def run_ours(args):
         "config": {"workload": f"{CONFIG}: Qwen3-30B-A3B-shaped W4A8 MoE layer, {T}-token prefill "
                                "per GPU, router-inclusive forward with residual",
                    "hidden": spec.hidden, "experts": spec.experts, "top_k": spec.top,
-                   "intermediate": spec.inter, "weights": "int4 g32 fp16 scales",
+                   "intermediate": spec.inter,
+                   "weights": "int4 g32 fp16 scales (MOE_B200_W4_G32_FP16): exact int32 group "
+                              "sums in both GEMMs, int8 activations",
                    "tokens_per_gpu": T, "global_batch": T * world, "seq_len": T,
                    "parallelism": f"replica x{world}" if world > 1 else "single GPU",
                    "l2": "no flush: the expert weights read per step (~330 MB) exceed the "
@@ -280,11 +308,13 @@ def run_ours(args):
         "layer": {"experts_hit": U, "assignments": A,
                   "algorithmic_bytes": lbytes,
                   "hbm_frac_layer": lbytes / (ms * 1e-3) / 1e9 / hbm_peak,
+                  "bytes_with_intermediates": layer_bytes_with_intermediates(spec, T, U, A),
                   "int8_tops": ops / (ms * 1e-3) / 1e12,
-                  "int8_frac_of_datasheet": ops / (ms * 1e-3) / 1e12 / INT8_DENSE_TOPS},
+                  "int8_peak_tops": i8_peak, "int8_peak_kind": i8_kind,
+                  "int8_frac": ops / (ms * 1e-3) / 1e12 / i8_peak},
     }
     if args.extra and world == 1:
-        result["extra"] = run_extra(args, moe, router, spec, lib, wsp, hbm_peak)
+        result["extra"] = run_extra(args, moe, router, spec, lib, wsp, hbm_peak, i8_peak, i8_kind)
     if args.suite and world == 1:
         result["suite"] = run_suite(args, hbm_peak)
     if rank == 0 and world == 1 and args.cpu_baseline:
@@ -505,7 +535,9 @@ def cudart_copy(dst: np.ndarray, src_ptr: int):
 def run_e2e(args, moe, router, spec, T, rank, world):
     """Public host API (moe_b200_forward_f32): pinned input/residual -> device,
     layer, output + routing -> host, all inside the timed call. Time per call =
-    CUDA events on the library's stream around the copies and the layer."""
+    the host wall clock around the call (validation, the ctypes call, the
+    copies, the layer and the synchronising return), max over ranks; the
+    library's own CUDA-event time of the same calls is reported beside it."""
     import torch
     from open_rknpu2_lm_infer_b200 import synthetic as S
     xh = torch.empty((T, spec.hidden), dtype=torch.float32, pin_memory=True)
@@ -519,25 +551,31 @@ def run_e2e(args, moe, router, spec, T, rank, world):
     wh = torch.empty((T, spec.top), dtype=torch.float32, pin_memory=True).numpy()
     for _ in range(args.warmup):
         moe.forward(router, x, r, out=oh, ids=ih, routes=wh)
-    times = []
+    ev_times = []
     for _ in range(args.steps):
         *_, tm = moe.forward(router, x, r, timings=True, out=oh, ids=ih, routes=wh)
-        times.append(tm["total_us"])
-    mean_us = statistics.mean(times)
+        ev_times.append(tm["total_us"])
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        moe.forward(router, x, r, out=oh, ids=ih, routes=wh)
+    mean_us = (time.perf_counter() - t0) / args.steps * 1e6
+    ev_us = statistics.mean(ev_times)
     if world > 1:
         import torch.distributed as dist
-        t = torch.tensor([mean_us], device="cuda")
+        t = torch.tensor([mean_us, ev_us], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        mean_us = float(t.item())
+        mean_us, ev_us = float(t[0].item()), float(t[1].item())
     h2d = 2 * T * spec.hidden * 4
     d2h = T * spec.hidden * 4 + 2 * T * spec.top * 4
     return {"value": world * T / (mean_us * 1e-6), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": mean_us / 1000.0,
+            "timing": "host wall clock (time.perf_counter) around each moe_b200_forward_f32 call",
+            "device_event_ms_per_step": ev_us / 1000.0,
             "api": "moe_b200_forward_f32 (pinned host buffers)"}
 
 
-def run_extra(args, moe, router, spec, lib, wsp, hbm_peak):
+def run_extra(args, moe, router, spec, lib, wsp, hbm_peak, i8_peak, i8_kind):
     import torch
     from open_rknpu2_lm_infer_b200 import _lib as L
     from open_rknpu2_lm_infer_b200 import synthetic as S
@@ -576,13 +614,23 @@ def run_extra(args, moe, router, spec, lib, wsp, hbm_peak):
         lb = layer_bytes(spec, T, U, A)
         ops = 2 * A * 3 * spec.hidden * spec.inter
         gb = gate_up_bytes(spec, U, A)
+        gu_us = avg.get("gate_us")
         out[name] = {"tokens": T, "ms_per_step": ms, "tokens_per_s": T / (ms * 1e-3),
                      "experts_hit": U, "hbm_frac_layer": lb / (ms * 1e-3) / 1e9 / hbm_peak,
                      "int8_tops": ops / (ms * 1e-3) / 1e12,
-                     "int8_frac_of_datasheet": ops / (ms * 1e-3) / 1e12 / INT8_DENSE_TOPS,
-                     "gate_up_us": avg.get("gate_us"), "down_us": avg.get("down_us"),
-                     "gate_up_gbs": gb / (avg["gate_us"] * 1e-6) / 1e9 if avg else None,
+                     "int8_frac": ops / (ms * 1e-3) / 1e12 / i8_peak,
+                     "gate_up_us": gu_us, "down_us": avg.get("down_us"),
+                     "gate_up_gbs": gb / (gu_us * 1e-6) / 1e9 if avg else None,
                      "stage_us": avg}
+        if name == "prefill_t4096" and gu_us:
+            # the prefill-sized gate/up GEMM against the tensor-core roofline
+            a = gate_up_ops(spec, A) / (gu_us * 1e-6) / 1e12
+            out[name]["roofline"] = {
+                "bound": "tensor", "achieved": a, "peak": i8_peak, "unit": "TOPS",
+                "frac": a / i8_peak, "peak_kind": i8_kind,
+                "kernel": "group_gemm_kernel<GateUpQ> (gate/up, 4096 tokens)",
+                "ops_per_launch": gate_up_ops(spec, A), "kernel_us": gu_us,
+                "traffic": measured_traffic(f"{CONFIG}_T4096_gate_up")}
     return out
 
 

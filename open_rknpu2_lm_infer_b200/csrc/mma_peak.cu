@@ -62,10 +62,18 @@ __device__ __forceinline__ int sw128(int row, int byte) {
 
 __device__ __forceinline__ uint32_t lcg(uint32_t x) { return x * 1664525u + 1013904223u; }
 
+// the bounded spin of a wait, kept out of line so that the issuing loop holds
+// only the first try_wait and a branch
+__device__ __noinline__ bool wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                       uint32_t* err) {
+    return mbar_wait(bar, parity, abort_flag, err);
+}
+
 // KIND 0: int8, 1: fp16. A: 128 rows, B: N rows, one 128-byte k-block each.
 template <int KIND, int N, bool TS>
 __global__ void __launch_bounds__(kThreads, 1)
-rate_kernel(int iters, int issuers, int rot, int gap, int waits, unsigned long long* cycles) {
+rate_kernel(int iters, int issuers, int rot, int gap, int waits, int mode,
+            unsigned long long* cycles) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
@@ -116,32 +124,23 @@ rate_kernel(int iters, int issuers, int rot, int gap, int waits, unsigned long l
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // Loop variants (mode >> 2): 0 bare MMA loop; 1 + a spin of `gap` cycles
+    // after each MMA; 2 + `waits` try_waits on a completed phase; 3 + `waits`
+    // bounded waits (the GEMM's mbar_wait). Lane 0 of each issuing warp runs it.
+    const int variant = mode >> 2;
     if (warp < issuers && lane == 0) {
         constexpr uint32_t idesc = KIND == 0 ? idesc_i8(128, N) : idesc_f16_(128, N);
         // rot > 1: the MMAs rotate over rot accumulators (independent
         // instructions); rot = 1: every MMA accumulates into the previous one's
         const uint32_t dbase = tmem + kACols + warp * rot * N;
         const uint32_t a0 = smem_u32(As), b0 = smem_u32(Bs);
-        const unsigned long long t0 = clock64();
-        int ri = 0;
-        for (int i = 0; i < iters; ++i) {
+        unsigned long long t0 = 0, t1 = 0;
+        bool ok = true;
+        auto issue = [&](int i, int ri) {
             const int j = i & 3;  // the four 32-byte K steps of the k-block
             const uint64_t bd = smem_desc_k_sw128(b0 + 32 * j);
             const uint32_t d = dbase + ri * N;
             const uint32_t acc = i >= rot ? 1u : 0u;
-            if (++ri == rot) ri = 0;
-            // gap > 0: the issuing thread spins `gap` cycles after each MMA (does
-            // issue block it, or do the MMAs run behind it?); waits > 0: it
-            // waits that many times on an mbarrier phase that is already complete
-            if (gap > 0) {
-                const unsigned long long g0 = clock64();
-                while (clock64() - g0 < (unsigned long long)gap) {
-                }
-            }
-            for (int w = 0; w < waits; ++w) {
-                int never = 0;
-                mbar_wait(&bar[3], 0, &never, &err_s);
-            }
             if (KIND == 0) {
                 if (TS) mma_i8_ts(d, tmem + 8 * j, bd, idesc, acc);
                 else mma_i8(d, smem_desc_k_sw128(a0 + 32 * j), bd, idesc, acc);
@@ -149,11 +148,71 @@ rate_kernel(int iters, int issuers, int rot, int gap, int waits, unsigned long l
                 if (TS) mma_f16_ts_(d, tmem + 8 * j, bd, idesc, acc);
                 else mma_f16_ss(d, smem_desc_k_sw128(a0 + 32 * j), bd, idesc, acc);
             }
+        };
+        int never = 0;
+        t0 = clock64();
+        if (variant == 0) {
+            int ri = 0;
+            for (int i = 0; i < iters; ++i) {
+                issue(i, ri);
+                if (++ri == rot) ri = 0;
+            }
+        } else if (variant == 1) {
+            int ri = 0;
+            for (int i = 0; i < iters; ++i) {
+                issue(i, ri);
+                if (++ri == rot) ri = 0;
+                if (gap > 0) {
+                    const unsigned long long g0 = clock64();
+                    while (clock64() - g0 < (unsigned long long)gap) {
+                    }
+                }
+            }
+        } else if (variant == 2) {
+            int ri = 0;
+            for (int i = 0; i < iters; ++i) {
+                issue(i, ri);
+                if (++ri == rot) ri = 0;
+                for (int w = 0; w < waits; ++w) mbar_try_wait(&bar[3], 0);
+            }
+        } else if (variant == 3) {
+            int ri = 0;
+            for (int i = 0; i < iters; ++i) {
+                issue(i, ri);
+                if (++ri == rot) ri = 0;
+                for (int w = 0; w < waits; ++w) mbar_wait(&bar[3], 0, &never, &err_s);
+            }
+        } else if (variant == 4) {
+            // waits as an inline try_wait with the bounded spin out of line, unrolled
+            int ri = 0;
+            for (int i = 0; i < iters; ++i) {
+                issue(i, ri);
+                if (++ri == rot) ri = 0;
+                if (waits > 0 && !mbar_try_wait(&bar[3], 0)) wait_slow(&bar[3], 0, &never, &err_s);
+                if (waits > 1 && !mbar_try_wait(&bar[3], 0)) wait_slow(&bar[3], 0, &never, &err_s);
+            }
+        } else if (variant == 5) {
+            // a commit to an mbarrier after every `gap`-th MMA (gap >= 1)
+            int ri = 0;
+            for (int i = 0; i < iters; ++i) {
+                issue(i, ri);
+                if (++ri == rot) ri = 0;
+                if (gap > 0 && (i % gap) == gap - 1) mma_commit(&bar[2]);
+            }
+        } else {
+            // four MMAs unrolled per iteration, then one wait (inline fast path)
+            for (int i = 0; i < iters; i += 4) {
+                issue(i, 0);
+                issue(i + 1, 1 % rot);
+                issue(i + 2, 2 % rot);
+                issue(i + 3, 3 % rot);
+                if (waits > 0 && !mbar_try_wait(&bar[3], 0)) wait_slow(&bar[3], 0, &never, &err_s);
+                if (waits > 1) mma_commit(&bar[2]);
+            }
         }
         mma_commit(&bar[warp]);
-        int never = 0;
-        const bool ok = mbar_wait(&bar[warp], 0, &never, &err_s);
-        const unsigned long long t1 = clock64();
+        ok = mbar_wait(&bar[warp], 0, &never, &err_s);
+        t1 = clock64();
         cycles[blockIdx.x * 4 + warp] = ok ? t1 - t0 : ~0ull;
     }
     tc_fence_before();
@@ -248,8 +307,109 @@ __global__ void __launch_bounds__(kThreads, 1) exact_kernel(int pattern, uint32_
     }
 }
 
+// Wake-up latency: warp 1 waits on an mbarrier phase that warp 0 completes
+// after a delay; both read the SM clock (same SM). mode 0: try_wait with a
+// 1 ms suspend hint, 1: try_wait without a hint, 2: test_wait spin. Each of
+// `reps` rounds records (wake clock - arrive clock); the median is returned.
+__global__ void __launch_bounds__(64, 1) wake_kernel(int mode, int reps, int delay,
+                                                     long long* lat) {
+    __shared__ uint64_t bar;
+    __shared__ long long t_arrive;
+    __shared__ uint32_t err_s;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+        err_s = 0;
+    }
+    __syncthreads();
+    for (int i = 0; i < reps; ++i) {
+        const uint32_t parity = i & 1;
+        if (warp == 0 && lane == 0) {
+            const long long t0 = clock64();
+            while (clock64() - t0 < delay) {
+            }
+            t_arrive = clock64();
+            mbar_arrive(&bar);
+        } else if (warp == 1 && lane == 0) {
+            const unsigned long long g0 = global_timer_ns();
+            bool done = false;
+            while (!done) {
+                if (mode == 0) {
+                    done = mbar_try_wait(&bar, parity);
+                } else if (mode == 1) {
+                    done = mbar_poll(&bar, parity);
+                } else {
+                    uint32_t ok;
+                    asm volatile(
+                        "{\n\t.reg .pred p;\n\t"
+                        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                        "selp.u32 %0, 1, 0, p;\n\t}"
+                        : "=r"(ok)
+                        : "r"(smem_u32(&bar)), "r"(parity)
+                        : "memory");
+                    done = ok != 0;
+                }
+                if (global_timer_ns() - g0 > 100000000ull) break;  // 0.1 s bound
+            }
+            const long long t1 = clock64();
+            __threadfence_block();
+            lat[i] = done ? t1 : -1;
+        }
+        __syncthreads();
+        if (warp == 1 && lane == 0 && lat[i] >= 0) lat[i] -= t_arrive;
+        __syncthreads();
+    }
+}
+
+// TMEM bandwidth: `warps` warps (a multiple of 4, each in its lane quadrant)
+// repeat tcgen05.ld (mode 0) or tcgen05.st (mode 1) of 32 lanes x `cols`
+// 32-bit columns, `batch` instructions per wait. Returns cycles per round of
+// every warp in *cycles (median over CTAs).
+template <int COLS>
+__global__ void __launch_bounds__(512, 1) tmem_bw_kernel(int mode, int iters, int batch, int warps,
+                                                         unsigned long long* cycles) {
+    __shared__ uint32_t tmem_s;
+    const int warp = threadIdx.x >> 5;
+    if (warp == 0) {
+        tmem_alloc(&tmem_s, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t base = tmem_s + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((warp >> 2) * 64 % 512);
+    uint32_t acc = 0;
+    const unsigned long long t0 = clock64();
+    if (warp < warps) {
+        for (int i = 0; i < iters; ++i) {
+            if (mode == 0) {
+                uint32_t v[COLS];
+                for (int b = 0; b < batch; ++b) {
+                    tmem_ld<COLS>(base + (uint32_t)((b * COLS) % 256), v);
+                }
+                tmem_wait_ld();
+                tmem_ld_pin(v);
+                acc += v[0];
+            } else {
+                for (int b = 0; b < batch; ++b) tmem_fill<COLS>(base + (uint32_t)((b * COLS) % 256), (uint32_t)i);
+                tmem_wait_st();
+            }
+        }
+    }
+    __syncthreads();
+    const unsigned long long t1 = clock64();
+    if (threadIdx.x == 0) cycles[blockIdx.x] = t1 - t0 + (acc == 12345678u ? 1 : 0);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_s, 512);
+    }
+}
+
 template <int KIND, int N, bool TS>
-int launch_rate(int grid, int iters, int issuers, int rot, int gap, int waits,
+int launch_rate(int grid, int iters, int issuers, int rot, int gap, int waits, int mode,
                 unsigned long long* d_cycles, cudaStream_t s) {
     // at least 120 KB of shared memory keeps one CTA per SM (each allocates
     // all 512 TMEM columns)
@@ -257,19 +417,19 @@ int launch_rate(int grid, int iters, int issuers, int rot, int gap, int waits,
     auto k = rate_kernel<KIND, N, TS>;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return -1;
-    k<<<grid, kThreads, smem, s>>>(iters, issuers, rot, gap, waits, d_cycles);
+    k<<<grid, kThreads, smem, s>>>(iters, issuers, rot, gap, waits, mode, d_cycles);
     return 0;
 }
 
 template <int KIND, bool TS>
-int launch_rate_n(int n, int grid, int iters, int issuers, int rot, int gap, int waits,
+int launch_rate_n(int n, int grid, int iters, int issuers, int rot, int gap, int waits, int mode,
                   unsigned long long* c, cudaStream_t s) {
     switch (n) {
-        case 16: return launch_rate<KIND, 16, TS>(grid, iters, issuers, rot, gap, waits, c, s);
-        case 32: return launch_rate<KIND, 32, TS>(grid, iters, issuers, rot, gap, waits, c, s);
-        case 64: return launch_rate<KIND, 64, TS>(grid, iters, issuers, rot, gap, waits, c, s);
-        case 128: return launch_rate<KIND, 128, TS>(grid, iters, issuers, rot, gap, waits, c, s);
-        case 256: return launch_rate<KIND, 256, TS>(grid, iters, issuers, rot, gap, waits, c, s);
+        case 16: return launch_rate<KIND, 16, TS>(grid, iters, issuers, rot, gap, waits, mode, c, s);
+        case 32: return launch_rate<KIND, 32, TS>(grid, iters, issuers, rot, gap, waits, mode, c, s);
+        case 64: return launch_rate<KIND, 64, TS>(grid, iters, issuers, rot, gap, waits, mode, c, s);
+        case 128: return launch_rate<KIND, 128, TS>(grid, iters, issuers, rot, gap, waits, mode, c, s);
+        case 256: return launch_rate<KIND, 256, TS>(grid, iters, issuers, rot, gap, waits, mode, c, s);
         default: return -1;
     }
 }
@@ -280,11 +440,11 @@ extern "C" {
 
 // kind: 0 int8, 1 fp16. Returns 0 and fills median cycles per MMA (over the
 // issuers of all CTAs) and the grid's wall time in ms, or a negative code.
-int mma_peak_rate(int kind, int n, int ts, int issuers, int rot, int gap, int waits, int iters,
-                  int grid, double* cycles_per_mma, double* ms) {
+int mma_peak_rate(int kind, int n, int ts, int issuers, int rot, int gap, int waits, int mode,
+                  int iters, int grid, double* cycles_per_mma, double* ms) {
     const int acc_cols = 32 + issuers * rot * n;
     if (issuers < 1 || issuers > 3 || rot < 1 || acc_cols > 512 || iters < 1 || grid < 1 ||
-        gap < 0 || gap > 100000 || waits < 0 || waits > 64)
+        gap < 0 || gap > 100000 || waits < 0 || waits > 64 || mode < 0 || mode > 31)
         return -2;
     unsigned long long* d = nullptr;
     if (cudaMalloc(&d, sizeof(unsigned long long) * 4 * grid) != cudaSuccess) return -3;
@@ -294,10 +454,10 @@ int mma_peak_rate(int kind, int n, int ts, int issuers, int rot, int gap, int wa
     cudaEventCreate(&e1);
     auto run = [&]() -> int {
         if (kind == 0)
-            return ts ? launch_rate_n<0, true>(n, grid, iters, issuers, rot, gap, waits, d, 0)
-                      : launch_rate_n<0, false>(n, grid, iters, issuers, rot, gap, waits, d, 0);
-        return ts ? launch_rate_n<1, true>(n, grid, iters, issuers, rot, gap, waits, d, 0)
-                  : launch_rate_n<1, false>(n, grid, iters, issuers, rot, gap, waits, d, 0);
+            return ts ? launch_rate_n<0, true>(n, grid, iters, issuers, rot, gap, waits, mode, d, 0)
+                      : launch_rate_n<0, false>(n, grid, iters, issuers, rot, gap, waits, mode, d, 0);
+        return ts ? launch_rate_n<1, true>(n, grid, iters, issuers, rot, gap, waits, mode, d, 0)
+                  : launch_rate_n<1, false>(n, grid, iters, issuers, rot, gap, waits, mode, d, 0);
     };
     int rc = run();  // warm-up
     if (rc == 0) {
@@ -324,6 +484,59 @@ int mma_peak_rate(int kind, int n, int ts, int issuers, int rot, int gap, int wa
     cudaEventDestroy(e1);
     cudaFree(d);
     return rc;
+}
+
+// Median wake-up latency (SM cycles) of a waiter on an mbarrier (see
+// wake_kernel), or a negative code.
+double mma_peak_wake(int mode, int reps, int delay) {
+    long long* d = nullptr;
+    if (reps < 1 || reps > 4096 || mode < 0 || mode > 2 || delay < 0 || delay > 1000000) return -2;
+    if (cudaMalloc(&d, sizeof(long long) * reps) != cudaSuccess) return -3;
+    wake_kernel<<<1, 64>>>(mode, reps, delay, d);
+    double r = -4;
+    if (cudaDeviceSynchronize() == cudaSuccess) {
+        std::vector<long long> h(reps);
+        cudaMemcpy(h.data(), d, sizeof(long long) * reps, cudaMemcpyDeviceToHost);
+        std::sort(h.begin(), h.end());
+        r = (double)h[reps / 2];
+    }
+    cudaFree(d);
+    return r;
+}
+
+// TMEM bytes per SM cycle of tcgen05.ld (mode 0) / tcgen05.st (mode 1) by
+// `warps` warps, 32 x cols per instruction, `batch` per wait; or < 0.
+double mma_peak_tmem_bw(int mode, int cols, int batch, int warps, int iters, int grid) {
+    if ((cols != 8 && cols != 16 && cols != 32) || batch < 1 || batch > 8 || warps < 4 ||
+        warps > 16 || (warps & 3) || iters < 1 || grid < 1 || mode < 0 || mode > 1)
+        return -2;
+    unsigned long long* d = nullptr;
+    if (cudaMalloc(&d, sizeof(unsigned long long) * grid) != cudaSuccess) return -3;
+    const int smem = 120 * 1024;  // one CTA per SM (it allocates all 512 columns)
+    auto go = [&]() {
+        if (cols == 8) {
+            cudaFuncSetAttribute(tmem_bw_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            tmem_bw_kernel<8><<<grid, 512, smem>>>(mode, iters, batch, warps, d);
+        } else if (cols == 16) {
+            cudaFuncSetAttribute(tmem_bw_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            tmem_bw_kernel<16><<<grid, 512, smem>>>(mode, iters, batch, warps, d);
+        } else {
+            cudaFuncSetAttribute(tmem_bw_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            tmem_bw_kernel<32><<<grid, 512, smem>>>(mode, iters, batch, warps, d);
+        }
+    };
+    go();
+    go();
+    double r = -4;
+    if (cudaDeviceSynchronize() == cudaSuccess) {
+        std::vector<unsigned long long> h(grid);
+        cudaMemcpy(h.data(), d, sizeof(unsigned long long) * grid, cudaMemcpyDeviceToHost);
+        std::sort(h.begin(), h.end());
+        const double cyc = (double)h[grid / 2];
+        r = (double)warps * 32.0 * cols * 4.0 * batch * iters / cyc;
+    }
+    cudaFree(d);
+    return r;
 }
 
 // Returns the number of fp32 accumulators that differ from the integer dot
