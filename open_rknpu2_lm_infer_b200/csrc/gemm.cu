@@ -132,7 +132,8 @@ struct GemmCfg {
     // (each converts half of a stage's groups), the heaviest per weight
     static constexpr int kConvWarps = kF16 ? 8 : 4;
     static constexpr int kEpiWarp0 = kConvWarp0 + kConvWarps;  // first epilogue warp
-    static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
+    static constexpr int kStoreWarp = kEpiWarp0 + kEpiWarps;   // exact group path only
+    static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps + (kGroup ? 1 : 0));
     static_assert(kLoadBytes % 1024 == 0, "stage alignment of the swizzled operands");
     static_assert(kLoadStages >= 2, "smem budget");
     static_assert(kLoadStages >= kAStages, "operand ring reuse is ordered by the load ring");
@@ -185,25 +186,48 @@ __device__ __forceinline__ void g32_word_to_i8(uint32_t word, uint32_t* out) {
     out[1] = __byte_perm(lo, hi, 0x7531);         // k 4,5,6,7
 }
 
+// Shared-memory layout of one instantiation. The exact group path's Store
+// epilogue (the down GEMM) stages each tile's outputs as [NT][128] f32 for a
+// store warp whose bulk copies write them, at the price of load stages (a down
+// tile has 6 k-blocks, so the per-tile store cost dominates); its gate/up
+// tiles (16 k-blocks, a deeper weight stream) keep every load stage and store
+// directly.
+template <int FMT, int EPI, int NT>
+struct GemmLayout {
+    using C = GemmCfg<FMT, NT>;
+    static constexpr bool kStaged = C::kGroup && EPI == kEpiStore;
+    static constexpr int kStgBytes = kStaged ? NT * 128 * 4 : 0;
+    static constexpr int kFit = (C::kLoadBudget - kStgBytes) / C::kLoadBytes;
+    static constexpr int kLoadStages = kFit > kMaxLoadStages ? kMaxLoadStages : kFit;
+    static_assert(kStgBytes % 1024 == 0, "staging tile alignment (bulk copies)");
+    static_assert(kLoadStages >= 2 && kLoadStages >= C::kAStages, "smem budget");
+};
+
 template <int FMT, int EPI, int NT>
 __global__ void __launch_bounds__(GemmCfg<FMT, NT>::kThreads, GemmCfg<FMT, NT>::kCtasPerSm)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs a) {
     using C = GemmCfg<FMT, NT>;
-    constexpr int SL = C::kLoadStages;
+    using Lay = GemmLayout<FMT, EPI, NT>;
+    constexpr int SL = Lay::kLoadStages;
     constexpr int AS = C::kAStages;
     constexpr int AS1 = AS > 0 ? AS : 1;  // ring arithmetic of formats without one
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
     uint8_t* load = smem;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(load + SL * C::kLoadBytes);
+    // exact group path: the staging tile of the outputs, 1024-byte aligned (the
+    // store warp's bulk copies read it from 16-byte aligned rows)
+    float* stg = reinterpret_cast<float*>(load + SL * C::kLoadBytes);  // [NT][128]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(load + SL * C::kLoadBytes + Lay::kStgBytes);
     uint64_t* lfull = bars;             // TMA bytes of stage s landed
     uint64_t* lempty = lfull + SL;      // MMAs that read stage s completed
     uint64_t* ofull = lempty + SL;      // W4 operand slot a unpacked into TMEM
     uint64_t* tfull = ofull + AS1;
     uint64_t* tempty = tfull + C::kNSlot;
     uint64_t* done = tempty + C::kNSlot;
-    int* tcnt = reinterpret_cast<int*>(done + 1);
+    uint64_t* sfull = done + 1;         // staging tile written by the epilogue warps
+    uint64_t* sempty = sfull + 1;       // staging tile read by the store warp's copies
+    int* tcnt = reinterpret_cast<int*>(sempty + 1);
     int* tb = tcnt + a.num_experts + 1;
     int* offs = tb + a.num_experts + 1;  // the grouping offsets, read once
     __shared__ uint32_t tmem_base_s;
@@ -229,6 +253,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             mbar_init(&tempty[i], kEpiWarps);
         }
         mbar_init(done, 1);
+        mbar_init(sfull, kEpiWarps);
+        mbar_init(sempty, 1);
         fence_barrier_init();
     }
     // tile table: tcnt[e] = token tiles of expert e, tb[e] = its first tile index
@@ -282,7 +308,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
     if constexpr (C::kGroup) {
         // every group buffer starts as the bits of 12582912.0f: the MMAs
         // accumulate onto them, the epilogue re-arms a slot after reading it
-        if (warp >= C::kEpiWarp0) {
+        if (warp >= C::kEpiWarp0 && warp < C::kEpiWarp0 + kEpiWarps) {
             const int c0 = ((warp - C::kEpiWarp0) >> 2) * C::kHalf;
             for (int sl = 0; sl < C::kNSlot; ++sl)
 #pragma unroll
@@ -503,6 +529,41 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                 }
             }
         }
+    } else if (C::kGroup && warp == C::kStoreWarp) {
+        if constexpr (Lay::kStaged) {
+        // ------------------------------------------------------------ store warp
+        // Exact group path: each finished tile's outputs, staged by the epilogue
+        // warps as [NT tokens][128 channels] f32, go to global memory as one
+        // bulk copy per token row (gate/up tiles: a gate and an up half), so the
+        // epilogue warps never stall on global stores.
+        if (lane == 0 && EPI != kEpiAcc) {
+            uint32_t ts = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++ts) {
+                if (!mbar_wait(sfull, ts & 1u, abort_flag, a.err)) break;
+                const TileCoord c = decode_tile(t, tb, tcnt, E);
+                const int row0 = offs[c.e] + c.mt * NT;
+                const int nvalid = min(NT, offs[c.e + 1] - row0);
+                for (int j = 0; j < nvalid; ++j) {
+                    const int orow = (EPI == kEpiStore && a.out_rows) ? a.out_rows[row0 + j] : row0 + j;
+                    float* dst = a.out + (size_t)orow * a.ldo;
+                    const float* src = stg + j * kTileRows;
+                    if (EPI == kEpiGateUp) {
+                        const int cols = min(64, a.n_valid - c.rt * 64);
+                        bulk_s2g(dst + c.rt * 64, src, (uint32_t)cols * 4u);
+                        bulk_s2g(dst + a.n_valid + c.rt * 64, src + 64, (uint32_t)cols * 4u);
+                    } else {
+                        const int cols = min(kTileRows, a.n_valid - c.rt * kTileRows);
+                        bulk_s2g(dst + c.rt * kTileRows, src, (uint32_t)cols * 4u);
+                    }
+                }
+                bulk_commit();
+                bulk_wait_read();
+                mbar_arrive(sempty);
+            }
+            bulk_wait_all();
+        }
+        }  // kStaged
     } else if (warp >= C::kEpiWarp0) {
         // ------------------------------------------------------------ epilogue
         const int half = (warp - C::kEpiWarp0) >> 2;  // column half (0..1)
@@ -533,7 +594,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                 return ti_;
             };
             TileInfo cur = tile_info(blockIdx.x), nxt = cur;
-            uint32_t it = 0, ist = 0;  // k-blocks and load stages seen
+            uint32_t it = 0, ist = 0, ts = 0;  // k-blocks, load stages, staged tiles
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
                 const int row0 = cur.row0, nvalid = cur.nvalid, ocol = cur.oc;
@@ -635,7 +696,22 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                     }
                 }
                 if (!ok) break;
-                if (EPI != kEpiAcc) {
+                if (Lay::kStaged) {
+                    // stage the dequantised tile for the store warp (its previous
+                    // tile's copies have read the buffer once sempty completes)
+                    if (!mbar_wait(sempty, (ts & 1u) ^ 1u, abort_flag, a.err)) {
+                        ok = false;
+                        break;
+                    }
+#pragma unroll
+                    for (int q = 0; q < C::kHalf; ++q)
+                        stg[(c0 + q) * kTileRows + r] = __fmul_rn((q & 1) ? facc[q >> 1].y : facc[q >> 1].x,
+                                                                  __shfl_sync(0xffffffffu, cur.sx, q));
+                    fence_proxy_async_smem();  // generic writes -> the bulk copies' reads
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(sfull);
+                    ++ts;
+                } else if (EPI != kEpiAcc) {
 #pragma unroll
                     for (int q = 0; q < C::kHalf; ++q) {
                         const int j = c0 + q;
@@ -748,9 +824,11 @@ template <int FMT, int EPI, int NT>
 static size_t gemm_smem_bytes(int E) {
     using C = GemmCfg<FMT, NT>;
     size_t b = 1024;  // alignment slack
-    b += (size_t)C::kLoadStages * C::kLoadBytes;
-    b += sizeof(uint64_t) * (2 * C::kLoadStages + (C::kAStages > 0 ? C::kAStages : 1) +
-                             2 * C::kNSlot + 1);
+    using Lay = GemmLayout<FMT, EPI, NT>;
+    b += (size_t)Lay::kLoadStages * C::kLoadBytes;
+    b += sizeof(uint64_t) * (2 * Lay::kLoadStages + (C::kAStages > 0 ? C::kAStages : 1) +
+                             2 * C::kNSlot + 3);
+    b += Lay::kStgBytes;
     b += sizeof(int) * (3 * (size_t)E + 3);
     // one CTA per SM: the kernel allocates all 512 TMEM columns
     // one CTA per SM (it allocates all 512 TMEM columns) unless two share it
