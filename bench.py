@@ -145,20 +145,20 @@ def layer_bytes(spec, T, U, A):
 
 def layer_bytes_with_intermediates(spec, T, U, A):
     """The same plus the intermediates this design writes and reads back: the
-    permuted int8 activation rows, the f32 SwiGLU middle and its int8 codes,
+    permuted int8 activation rows, the f32 gate | up rows (written by the
+    gate/up GEMM, read by the SwiGLU + requantisation), the int8 middle codes,
     the f32 expert rows y (written by the down GEMM, read by the combine)."""
     H, I = spec.hidden, spec.inter
-    return (layer_bytes(spec, T, U, A) + A * H * 2 + A * I * 4 * 2 + A * I * 2 +
+    return (layer_bytes(spec, T, U, A) + A * H * 2 + A * 2 * I * 4 * 2 + A * I * 2 +
             A * H * 4 * 2)
 
 
 def gate_up_bytes(spec, U, A):
     """Algorithmic bytes of one gate/up GEMM launch: int4 codes + fp16 scales of
-    the experts hit, the permuted int8 activation rows, the f32 SwiGLU middle
-    rows written (SwiGLU and the requantisation run in its epilogue) and their
-    int8 codes."""
+    the experts hit, the permuted int8 activation rows read, the f32 gate | up
+    rows written."""
     H, I = spec.hidden, spec.inter
-    return U * (2 * I * H // 2 + 2 * I * H // 32 * 2) + A * H + A * I * 4 + A * I
+    return U * (2 * I * H // 2 + 2 * I * H // 32 * 2) + A * H + A * 2 * I * 4
 
 
 def gate_up_ops(spec, A):
@@ -271,8 +271,8 @@ def run_ours(args):
     traffic = measured_traffic(f"{CONFIG}_T{T}_gate_up")
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                 "frac": (achieved / hbm_peak) if achieved else None, "traffic": traffic,
-                "kernel": "group_gemm_kernel<GateUpQ> (gate/up + SwiGLU + requantisation, "
-                          "exact int32 group sums)",
+                "kernel": "grouped_gemm_kernel<W4G32, GateUp, 32> (gate/up, exact int32 "
+                          "group sums, f32 gate | up rows out)",
                 "algorithmic_bytes_per_launch": gu_bytes, "kernel_us": gate_us,
                 "peak_kind": f"{pk_kind} (hbm_gbs, STREAM-style copy)"}
 
@@ -628,7 +628,7 @@ def run_extra(args, moe, router, spec, lib, wsp, hbm_peak, i8_peak, i8_kind):
             out[name]["roofline"] = {
                 "bound": "tensor", "achieved": a, "peak": i8_peak, "unit": "TOPS",
                 "frac": a / i8_peak, "peak_kind": i8_kind,
-                "kernel": "group_gemm_kernel<GateUpQ> (gate/up, 4096 tokens)",
+                "kernel": "grouped_gemm_kernel<W4G32, GateUp, 32> (gate/up, 4096 tokens)",
                 "ops_per_launch": gate_up_ops(spec, A), "kernel_us": gu_us,
                 "traffic": measured_traffic(f"{CONFIG}_T4096_gate_up")}
     return out
