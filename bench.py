@@ -432,6 +432,7 @@ def run_ep(args):
             stages.append(tm.as_dict())
     lib.moe_b200_workspace_profile(moe.workspace, 0)
     gate_us = statistics.mean(s_["gate_us"] for s_ in stages) if stages else float("nan")
+    ep_stages = ep_stage_breakdown(args, ops, ex, x, res, stream, world)
     rows_here = recv // max(args.steps, 1)
     # the experts of this rank hit by its received rows: all of them at this size
     U = P
@@ -490,6 +491,7 @@ def run_ep(args):
                        "(graph replay, pinned host buffers)"},
         "gpu_launches": int(launches),
         "clocks": clk,
+        "ep_stages_us": ep_stages,
         "exchange": {"rows_sent_per_step_rank0": sent // max(args.steps, 1),
                      "rows_received_per_step_rank0": rows_here,
                      "dispatch_bytes_per_row": row_bytes + 8,
@@ -509,6 +511,43 @@ def run_ep(args):
     dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result), flush=True)
+
+
+def ep_stage_breakdown(args, ops, ex, x, res, stream, world):
+    """Per-stage device times of eager EP layer steps (CUDA events on the
+    layer's stream): route, pack, the exchange's five stages (dispatch, rows
+    wait, expert rows, return, return wait), combine. Mean over the profiled
+    steps on each rank, then the max and min over ranks of each stage."""
+    import torch
+    import torch.distributed as dist
+    names = ["route_us", "pack_us", *ex.STAGES, "combine_us"]
+    per = []
+    ex.profile(True)
+    for _ in range(max(args.steps, 1)):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record(stream)
+        ids, routes = ops.route(x)
+        ev[1].record(stream)
+        send_q, send_scale, send_expert, counts, pos = ops.pack(x, ids, routes)
+        ev[2].record(stream)
+        y_back = ex.step(send_q, send_scale, send_expert, counts, ops.moe)
+        ev[3].record(stream)
+        ops.combine(y_back, pos, routes, res)
+        ev4 = torch.cuda.Event(enable_timing=True)
+        ev4.record(stream)
+        torch.cuda.synchronize()
+        xs = ex.profile_read()
+        per.append([1000 * ev[0].elapsed_time(ev[1]), 1000 * ev[1].elapsed_time(ev[2]),
+                    *(xs[k] for k in ex.STAGES), 1000 * ev[3].elapsed_time(ev4)])
+    ex.profile(False)
+    mean = torch.tensor([statistics.mean(col) for col in zip(*per)], device="cuda")
+    hi, lo = mean.clone(), mean.clone()
+    dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+    dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+    return {"max_over_ranks": dict(zip(names, hi.tolist())),
+            "min_over_ranks": dict(zip(names, lo.tolist())),
+            "steps": max(args.steps, 1), "n_ranks": world,
+            "timing": "eager steps, CUDA events on the layer stream"}
 
 
 def routing_stats(moe, spec, T):
@@ -743,9 +782,9 @@ def run_ep_stack(args, world, rank, local, stream):
     the residual after, 4096 tokens split over the ranks (4096 / N each); rank
     g holds experts [g E/N, (g+1) E/N) of every layer. The 48 layers cycle over
     4 distinct seeded banks (each ~340 MB whole, far above the L2, so every
-    layer streams its weights from HBM as 48 distinct banks would). Eager
-    launches, one exchange (sized for the stack's rows) shared by the layers;
-    CUDA events, max over ranks."""
+    layer streams its weights from HBM as 48 distinct banks would). One
+    exchange (sized for the stack's rows) shared by the layers; the stack is
+    timed eagerly and as one captured CUDA graph; CUDA events, max over ranks."""
     import torch
     import torch.distributed as dist
     from open_rknpu2_lm_infer_b200 import synthetic as S
@@ -787,16 +826,35 @@ def run_ep_stack(args, world, rank, local, stream):
     torch.cuda.synchronize()
     ex.status()
     dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(3):
-        stack()
-    e1.record(stream)
+
+    def timed(fn, n=3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / n], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    eager_ms = timed(stack)
+    # the whole 48-layer stack captured once (the exchange's step counter
+    # lives on the device, so replays stay in lockstep across the ranks)
+    side = torch.cuda.Stream()
+    side.wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            stack()
+    stream.wait_stream(side)
+    graph.replay()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / 3
-    t = torch.tensor([ms], device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms = timed(graph.replay)
+    del graph
+    torch.cuda.synchronize()
     ex.status()
     for moe, router, ops in banks:
         ops.status()
@@ -807,6 +865,8 @@ def run_ep_stack(args, world, rank, local, stream):
     be.close()
     return {"layers": n_layers, "tokens": T_all, "tokens_per_gpu": T, "distinct_banks": n_banks,
             "ms_per_step": ms, "tokens_per_s": T_all / (ms * 1e-3), "ms_per_layer": ms / n_layers,
+            "eager_ms_per_step": eager_ms, "timing": "CUDA-graph replays of the whole stack, "
+            "CUDA events, max over ranks",
             "n_gpus": world, "parallelism": f"ep{world}"}
 
 

@@ -372,6 +372,15 @@ int moe_b200_ep_exchange_status(moe_b200_ep_exchange *ex);
  * (the next real step completes). MOE_B200_ERR_INVALID for world > 1, where
  * it would break the ranks' lockstep. */
 int moe_b200_ep_exchange_probe_timeout(moe_b200_ep_exchange *ex, void *stream);
+/* Stage timings of exchange steps (no counterpart in the reference; the
+ * exchange-side analogue of moe_b200_workspace_profile): while enabled, each
+ * step records CUDA events on its stream; _read waits for the last step and
+ * writes its five stage times in microseconds: dispatch (the rows' peer
+ * stores), rows wait (until every source's rows arrived), expert rows
+ * (grouping, gate/up, requantisation, down), return (the expert rows' peer
+ * stores), return wait. MOE_B200_ERR_INVALID before a profiled step. */
+int moe_b200_ep_exchange_profile(moe_b200_ep_exchange *ex, int32_t enable);
+int moe_b200_ep_exchange_profile_read(moe_b200_ep_exchange *ex, float *stage_us);
 void moe_b200_ep_exchange_free(moe_b200_ep_exchange *ex);
 
 /* Token owner, step 3: out[t] = (residual[t] +) sum over ranks r ascending of

@@ -140,6 +140,8 @@ SIGNATURES = [
     ("moe_b200_ep_exchange_y_back", C.c_void_p, [C.c_void_p]),
     ("moe_b200_ep_exchange_status", C.c_int, [C.c_void_p]),
     ("moe_b200_ep_exchange_probe_timeout", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("moe_b200_ep_exchange_profile", C.c_int, [C.c_void_p, C.c_int32]),
+    ("moe_b200_ep_exchange_profile_read", C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
     ("moe_b200_ep_exchange_free", None, [C.c_void_p]),
     ("moe_b200_graph_create", C.c_void_p,
      [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),

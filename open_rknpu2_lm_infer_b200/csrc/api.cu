@@ -551,7 +551,7 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
                  GateRef gate = {}) {
     if (use_gemv(ws, w, rows))
         return run_small(ws, w, rows, d_x, d_ids, d_routes, d_res, d_out, s, evs, res_ready);
-    const int E = ws->E, k = ws->k, H = ws->H, I = ws->I;
+    const int E = ws->E, k = ws->k, H = ws->H;
     const long n = (long)rows * k;
     auto mark = [&](int i) {
         if (evs) cudaEventRecord(evs[i], s);
@@ -1525,6 +1525,10 @@ struct moe_b200_ep_exchange {
     float* y = nullptr;                 // [world * cap][H] expert rows of the received rows
     ExchangeArgs args{};
     bool connected = false;
+    // stage events of profiled steps: begin, dispatched, rows arrived, expert
+    // rows done, returned, returned rows arrived
+    bool profiling = false;
+    cudaEvent_t ev[6] = {};
 };
 
 moe_b200_ep_exchange* moe_b200_ep_exchange_create(int32_t device, int32_t world, int32_t rank,
@@ -1640,18 +1644,50 @@ int moe_b200_ep_exchange_step(moe_b200_ep_exchange* ex, moe_b200_workspace* ws,
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const ExchangeArgs& a = ex->args;
     uint8_t* own = ex->region;
+    auto mark = [&](int i) {
+        if (ex->profiling) cudaEventRecord(ex->ev[i], s);
+    };
+    mark(0);
     launch_ep_begin(ex->step, s);
     launch_ep_dispatch(a, d_send_q, d_send_scale, d_send_expert, d_send_counts, s);
+    mark(1);
     launch_ep_wait(a, 0, ex->mask, s);
+    mark(2);
     rc = ep_expert_rows_impl(ws, w, (int)n, reinterpret_cast<const int8_t*>(own + a.off_q),
                              reinterpret_cast<const float*>(own + a.off_scale),
                              reinterpret_cast<const int32_t*>(own + a.off_expert), ex->mask, ex->y,
                              s);
     if (rc) return rc;
+    mark(3);
     launch_ep_return(a, ex->y, s);
+    mark(4);
     launch_ep_wait(a, 1, nullptr, s);
+    mark(5);
     ws->launches += 5;
     return cuda_rc(cudaPeekAtLastError());
+}
+
+int moe_b200_ep_exchange_profile(moe_b200_ep_exchange* ex, int32_t enable) {
+    if (!ex) return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ex->device);
+    if (enable && !ex->ev[0])
+        for (auto& e : ex->ev)
+            if (cudaEventCreate(&e) != cudaSuccess) return MOE_B200_ERR_CUDA;
+    ex->profiling = enable != 0;
+    return MOE_B200_OK;
+}
+
+int moe_b200_ep_exchange_profile_read(moe_b200_ep_exchange* ex, float* stage_us) {
+    if (!ex || !stage_us || !ex->ev[0]) return MOE_B200_ERR_INVALID;
+    DeviceGuard guard(ex->device);
+    if (cudaEventSynchronize(ex->ev[5]) != cudaSuccess) return MOE_B200_ERR_CUDA;
+    for (int i = 0; i < 5; ++i) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, ex->ev[i], ex->ev[i + 1]) != cudaSuccess)
+            return MOE_B200_ERR_CUDA;
+        stage_us[i] = 1000.0f * ms;
+    }
+    return MOE_B200_OK;
 }
 
 int moe_b200_ep_exchange_probe_timeout(moe_b200_ep_exchange* ex, void* stream) {
@@ -1683,6 +1719,8 @@ void moe_b200_ep_exchange_free(moe_b200_ep_exchange* ex) {
     if (!ex) return;
     DeviceGuard guard(ex->device);
     cudaDeviceSynchronize();
+    for (auto& e : ex->ev)
+        if (e) cudaEventDestroy(e);
     for (int r = 0; r < (int)ex->peers.size(); ++r)
         if (r != ex->rank && ex->peers[r]) cudaIpcCloseMemHandle(ex->peers[r]);
     for (void* p : {(void*)ex->region, (void*)ex->d_peers, (void*)ex->step, (void*)ex->done,

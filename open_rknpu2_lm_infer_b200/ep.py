@@ -221,6 +221,18 @@ class DeviceExchange:
     def status(self):
         check(self.lib.moe_b200_ep_exchange_status(self.raw), "exchange status")
 
+    STAGES = ("dispatch_us", "rows_wait_us", "expert_rows_us", "return_us", "return_wait_us")
+
+    def profile(self, enable: bool = True):
+        """Record the stage events of the following steps (moe_b200_ep_exchange_profile)."""
+        check(self.lib.moe_b200_ep_exchange_profile(self.raw, int(enable)), "exchange profile")
+
+    def profile_read(self) -> dict:
+        """Stage times (us) of the last profiled step; waits for it."""
+        buf = (C.c_float * 5)()
+        check(self.lib.moe_b200_ep_exchange_profile_read(self.raw, buf), "exchange profile read")
+        return dict(zip(self.STAGES, (float(v) for v in buf)))
+
     def probe_timeout(self):
         """Single-rank exchanges: run the row wait on a step nothing completes
         (it gives up after ~2 s; status() then raises the timeout)."""

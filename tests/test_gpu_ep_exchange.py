@@ -62,11 +62,21 @@ def test_exchange_one_rank_matches_single_device_and_replays(cuda, oracle):
                  what="single-device layer vs restatement")
     be, moe, router, ops = _rank_setup(1, 0, layer)
     ex = DeviceExchange(ops, None)
+    from open_rknpu2_lm_infer_b200 import _lib as L
+    from open_rknpu2_lm_infer_b200.moe import MoeError
+    with pytest.raises(MoeError) as e:  # no profiled step yet
+        ex.profile_read()
+    assert e.value.code == L.ERR_INVALID
+    ex.profile(True)
     for _ in range(2):  # the step counter advances; results repeat
         out = ep_forward_device(ops, ex, x, res)
         torch.cuda.synchronize()
         ex.status(); ops.status()
         assert np.array_equal(out.cpu().numpy(), ref)
+    stages = ex.profile_read()  # the stage timings of the last profiled step
+    assert set(stages) == set(ex.STAGES)
+    assert all(v >= 0.0 for v in stages.values()) and stages["expert_rows_us"] > 0.0
+    ex.profile(False)
     # the same step captured once and replayed
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
