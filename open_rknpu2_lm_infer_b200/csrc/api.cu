@@ -299,6 +299,10 @@ struct moe_b200_workspace {
     uint64_t bytes = 0;
     cudaStream_t own_stream = nullptr;
     cudaStream_t copy_stream = nullptr;  // host-API residual upload, overlapped with the layer
+    // small-batch layers of banks with a shared expert: the shared FFN runs on
+    // a side stream beside the routed GEMVs (fork / join events)
+    cudaStream_t side_stream = nullptr;
+    cudaEvent_t side_fork = nullptr, side_join = nullptr;
     cudaEvent_t res_ready = nullptr;
     cudaEvent_t x_ready = nullptr;  // host-API input upload done (orders the residual's after it)
     cudaStream_t last_stream = nullptr;
@@ -471,7 +475,7 @@ constexpr int kGemvMaxRows = 4;
 
 bool use_gemv(const moe_b200_workspace* ws, const moe_b200_weights* w, int rows) {
     return rows <= kGemvMaxRows && w->gu.fmt == kFmtW4G32 && w->dn.fmt == kFmtW4G32 &&
-           !w->shared && (int)(gemv_smem_bytes((int)(w->gu.kblocks / kKPS))) <= (int)kGemvMaxSmem &&
+           (int)(gemv_smem_bytes((int)(w->gu.kblocks / kKPS))) <= (int)kGemvMaxSmem &&
            gemv_smem_bytes((int)(w->dn.kblocks / kKPS)) <= kGemvMaxSmem && ws->k <= 32;
 }
 
@@ -479,9 +483,23 @@ GemvArgs gemv_args(const moe_b200_workspace* ws, const moe_b200_weights* w, int 
                    const float* d_x, const int32_t* d_ids, const float* d_routes,
                    const float* d_res, float* d_out);
 
+// The shared-gate logits of a gated router: column E of the workspace logits.
+struct GateRef {
+    const float* logits = nullptr;
+    int ld = 0;
+};
+
+int run_shared(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
+               cudaStream_t s);
+
+// The small-batch layer: the routed experts as two GEMV kernels (gate/up with
+// SwiGLU and requantisation, down with the combine). A shared expert runs its
+// FFN on the workspace's side stream at the same time (its own activation
+// quantisation, the one-expert grouping, the tensor-core GEMMs) and enters
+// the down kernel's combine after the ranks, as in combine_kernel.
 int run_small(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
               const int32_t* d_ids, const float* d_routes, const float* d_res, float* d_out,
-              cudaStream_t s, cudaEvent_t* evs, cudaEvent_t res_ready) {
+              cudaStream_t s, cudaEvent_t* evs, cudaEvent_t res_ready, GateRef gate = {}) {
     auto mark = [&](int i) {
         if (evs) cudaEventRecord(evs[i], s);
     };
@@ -489,11 +507,34 @@ int run_small(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const
     mark(1);
     mark(2);
     mark(3);
-    const GemvArgs a = gemv_args(ws, w, rows, d_x, d_ids, d_routes, d_res, d_out);
-    if (launch_gemv(a, 0, s)) return MOE_B200_ERR_UNSUPPORTED;
+    GemvArgs a = gemv_args(ws, w, rows, d_x, d_ids, d_routes, d_res, d_out);
+    if (w->shared) {
+        cudaStream_t side = ws->side_stream;
+        cudaEventRecord(ws->side_fork, s);
+        cudaStreamWaitEvent(side, ws->side_fork, 0);
+        launch_set_range(ws->shared_offsets, rows, side);
+        ws->launches += 5;  // range, quantisation, gate/up, requantisation, down
+        if (w->shared_mode == MOE_B200_SHARED_JOINT)  // the routed rows' MoE A8 codes
+            launch_quant_gather(d_x, rows, ws->H, ws->Kh, kQuantMoe, 1, nullptr, ws->q_x, ws->s_x,
+                                nullptr, nullptr, nullptr, nullptr, ws->err, side);
+        const int rc = run_shared(ws, w, rows, d_x, side);
+        cudaEventRecord(ws->side_join, side);
+        if (rc) {
+            cudaStreamWaitEvent(s, ws->side_join, 0);
+            return rc;
+        }
+        a.shared = ws->s_y;
+        a.gate = gate.logits;
+        a.gate_ld = gate.ld;
+    }
+    if (launch_gemv(a, 0, s)) {
+        if (w->shared) cudaStreamWaitEvent(s, ws->side_join, 0);
+        return MOE_B200_ERR_UNSUPPORTED;
+    }
     mark(4);
     mark(5);
     if (res_ready) cudaStreamWaitEvent(s, res_ready, 0);
+    if (w->shared) cudaStreamWaitEvent(s, ws->side_join, 0);
     if (launch_gemv(a, 1, s)) return MOE_B200_ERR_UNSUPPORTED;
     mark(6);
     mark(7);
@@ -539,18 +580,13 @@ GemvArgs gemv_args(const moe_b200_workspace* ws, const moe_b200_weights* w, int 
     return a;
 }
 
-// The shared-gate logits of a gated router: column E of the workspace logits.
-struct GateRef {
-    const float* logits = nullptr;
-    int ld = 0;
-};
 
 int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
                  const int32_t* d_ids, const float* d_routes, const float* d_res, float* d_out,
                  cudaStream_t s, cudaEvent_t* evs, cudaEvent_t res_ready = nullptr,
                  GateRef gate = {}) {
     if (use_gemv(ws, w, rows))
-        return run_small(ws, w, rows, d_x, d_ids, d_routes, d_res, d_out, s, evs, res_ready);
+        return run_small(ws, w, rows, d_x, d_ids, d_routes, d_res, d_out, s, evs, res_ready, gate);
     const int E = ws->E, k = ws->k, H = ws->H;
     const long n = (long)rows * k;
     auto mark = [&](int i) {
@@ -1048,6 +1084,9 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     }
     if (rc == MOE_B200_OK &&
         (cudaStreamCreateWithFlags(&ws->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
+         cudaStreamCreateWithFlags(&ws->side_stream, cudaStreamNonBlocking) != cudaSuccess ||
+         cudaEventCreateWithFlags(&ws->side_fork, cudaEventDisableTiming) != cudaSuccess ||
+         cudaEventCreateWithFlags(&ws->side_join, cudaEventDisableTiming) != cudaSuccess ||
          cudaEventCreateWithFlags(&ws->res_ready, cudaEventDisableTiming) != cudaSuccess ||
          cudaEventCreateWithFlags(&ws->x_ready, cudaEventDisableTiming) != cudaSuccess))
         rc = MOE_B200_ERR_CUDA;
@@ -1071,6 +1110,12 @@ void moe_b200_workspace_free(moe_b200_workspace* ws) {
         if (ws->ev[i]) cudaEventDestroy(ws->ev[i]);
     for (cudaEvent_t e : ws->prof_ev) cudaEventDestroy(e);
     if (ws->own_stream) cudaStreamDestroy(ws->own_stream);
+    if (ws->side_stream) {
+        cudaStreamSynchronize(ws->side_stream);
+        cudaStreamDestroy(ws->side_stream);
+    }
+    if (ws->side_fork) cudaEventDestroy(ws->side_fork);
+    if (ws->side_join) cudaEventDestroy(ws->side_join);
     if (ws->copy_stream) {
         cudaStreamSynchronize(ws->copy_stream);
         cudaStreamDestroy(ws->copy_stream);
@@ -1312,7 +1357,8 @@ int moe_b200_route_device(moe_b200_workspace* ws, const moe_b200_router* r, int3
 static int layer_impl(moe_b200_workspace* ws, const moe_b200_weights* w, const moe_b200_router* r,
                       int rows, const float* d_x, const float* d_res, float* d_out, cudaStream_t s,
                       cudaEvent_t* evs, cudaEvent_t res_ready) {
-    if (ws->coop && use_gemv(ws, w, rows) && r->order != MOE_B200_ROUTER_SEQUENTIAL && !r->gate) {
+    if (ws->coop && use_gemv(ws, w, rows) && !w->shared && r->order != MOE_B200_ROUTER_SEQUENTIAL &&
+        !r->gate) {
         if (res_ready) cudaStreamWaitEvent(s, res_ready, 0);
         DecodeArgs d{};
         d.r = router_args(ws, r, rows, d_x, nullptr, ws->ids, ws->routes);

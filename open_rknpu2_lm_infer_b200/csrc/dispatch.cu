@@ -385,6 +385,15 @@ void launch_ep_gather_rows(const int8_t* q, const float* scale, const int32_t* p
     ep_gather_rows_kernel<<<n, 128, 0, s>>>(q, scale, pos, ld, q_perm, s_perm);
 }
 
+__global__ void set_range_kernel(int32_t* offsets, int rows) {
+    offsets[0] = 0;
+    offsets[1] = rows;
+}
+
+void launch_set_range(int32_t* offsets, int rows, cudaStream_t s) {
+    set_range_kernel<<<1, 1, 0, s>>>(offsets, rows);
+}
+
 void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k,
                          const int32_t* pos, int8_t* q_rows, float* s_rows, int8_t* q_perm,
                          float* s_perm, __half* h_rows, __half* h_perm, uint32_t* err,

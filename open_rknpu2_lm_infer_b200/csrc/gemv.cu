@@ -314,7 +314,12 @@ __global__ void __launch_bounds__(kGvThreads) gemv_down_kernel(const GemvArgs a)
         }
     }
     if (!last_arrival(&a.counters[a.dn_counter_base + t * gridDim.y + dt], a.k)) return;
-    // combine the token's kept ranks in rank order, then the residual
+    // combine the token's kept ranks in rank order, then the shared expert's
+    // row (scaled by the sigmoid of its gate logit, if gated), then the
+    // residual: combine_kernel's order and roundings
+    float gs = 1.0f;
+    if (a.shared && a.gate)
+        gs = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_f32(-a.gate[(size_t)t * a.gate_ld])));
     for (int c = dt * 128 + threadIdx.x; c < min(a.H, dt * 128 + 128); c += kGvThreads) {
         float acc = 0.0f;
         for (int r = 0; r < a.k; ++r) {
@@ -323,6 +328,11 @@ __global__ void __launch_bounds__(kGvThreads) gemv_down_kernel(const GemvArgs a)
             const int er = a.ids[as];
             if (!(wr > 0.0f) || er < 0 || er >= a.E) continue;
             acc = __fmaf_rn(__ldcg(a.y + (size_t)as * a.H + c), wr, acc);
+        }
+        if (a.shared) {
+            float sv = __ldcg(a.shared + (size_t)t * a.H + c);
+            if (a.gate) sv = __fmul_rn(gs, sv);
+            acc = __fadd_rn(acc, sv);
         }
         if (a.residual) acc = __fadd_rn(a.residual[(size_t)t * a.H + c], acc);
         a.out[(size_t)t * a.H + c] = acc;

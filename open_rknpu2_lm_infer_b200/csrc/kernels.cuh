@@ -105,11 +105,15 @@ void launch_requant(const float* gate_up, const int32_t* count, int max_rows, in
                     int rule, int8_t* q, __half* qh, float* sc, cudaStream_t s);
 // gate (may be null): the shared-gate logit of token t at gate[t * gate_ld];
 // the shared row then enters as sigmoid(gate) * shared.
+// offsets[0] = 0, offsets[1] = rows: the one-expert grouping of the shared
+// expert when no routed grouping ran.
+void launch_set_range(int32_t* offsets, int rows, cudaStream_t s);
 void launch_combine(const float* y, const int32_t* pos, const float* routes, const float* shared,
                     const float* residual, int T, int H, int k, float* out, cudaStream_t s,
                     const float* gate = nullptr, int gate_ld = 0);
 
-// gemv.cu: the small-batch path of group-32 int4 banks (no shared expert).
+// gemv.cu: the small-batch path of group-32 int4 banks (a shared expert, if
+// any, runs beside it and enters the combine of the down kernel).
 struct GemvArgs {
     const int32_t* ids;       // [T][k]
     const float* routes;      // [T][k]
@@ -130,6 +134,9 @@ struct GemvArgs {
     float* out;               // [T][H]
     int* counters;            // [T*k] gate/up, then [T][H/128] down (zeroed)
     int dn_counter_base;
+    const float* shared;      // [T][H] shared-expert rows added after the ranks, or null
+    const float* gate;        // shared-gate logits gate[t * gate_ld] (sigmoid scale), or null
+    int gate_ld;
     uint32_t* err;
 };
 // part 0: gate/up (+ SwiGLU + requant), part 1: down (+ combine + residual).

@@ -68,7 +68,10 @@ CASES = [("c1", 32), ("c1", 1), ("c2_e32", 1), ("c2_e32", 37), ("c2_e32", 300),
          ("c3_e32", 64), ("w4pc", 48), ("w8pc", 48), ("joint", 40), ("c2", 512),
          ("c2_e32_rounded", 37), ("c2_rounded", 512), ("c1_rounded", 32),
          # 4 rows per expert: 16-token tiles
-         ("c2", 64), ("c2_rounded", 64)]
+         ("c2", 64), ("c2_rounded", 64),
+         # small batches of a bank with a shared expert: the routed GEMVs with
+         # the shared FFN beside them on the side stream
+         ("c3_e32", 1), ("c3_e32", 3), ("c3_e32", 4)]
 
 
 @pytest.mark.parametrize("name,T", CASES)

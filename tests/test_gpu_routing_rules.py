@@ -180,7 +180,8 @@ class _CAI:
 GATE_SPECS = {"q35g_e32": S.small_spec("q35g", experts=32), "q35g": S.CONFIGS["q35g"]}
 
 
-@pytest.mark.parametrize("name,T", [("q35g_e32", 1), ("q35g_e32", 40), ("q35g", 512)])
+@pytest.mark.parametrize("name,T", [("q35g_e32", 1), ("q35g_e32", 4), ("q35g_e32", 40),
+                                    ("q35g", 512)])
 def test_shared_gate_layer_matches_oracle(cuda, oracle, name, T):
     torch = cuda
     spec = GATE_SPECS[name]
