@@ -19,8 +19,8 @@ BUILD = PKG / "_build"
 LIB = PKG / "libmoe_b200.so"
 INCLUDE = PKG.parent / "include"
 
-SOURCES = ["api.cu", "router.cu", "dispatch.cu", "gemm.cu", "gemv.cu", "exchange.cu", "noalloc.cu",
-           "norm.cu"]
+SOURCES = ["api.cu", "router.cu", "dispatch.cu", "gemm.cu", "gemv.cu", "gemv_w8.cu", "exchange.cu",
+           "noalloc.cu", "norm.cu"]
 # the tensor-core rate probe (open_rknpu2_lm_infer_b200/mma_peak.py), a separate library
 PEAK_SOURCE = "mma_peak.cu"
 PEAK_LIB = PKG / "libmoe_b200_peak.so"

@@ -330,6 +330,11 @@ struct moe_b200_workspace {
     // shared expert
     int8_t *q_xd = nullptr, *sq_m = nullptr;
     float *s_xd = nullptr, *s_middle = nullptr, *ss_m = nullptr, *s_y = nullptr;
+    // small-batch shared FFN of per-channel int8 banks (split-K GEMVs):
+    // int32 accumulators, last-arrival counters, middle row maxima
+    int32_t* w8_acc = nullptr;
+    int* w8_cnt = nullptr;
+    uint32_t* w8_max = nullptr;
     float* logits = nullptr;
     uint32_t* err = nullptr;
     CUtensorMap map_a[3], map_qm[3], map_qx[3], map_qxd[3], map_sqm[3];
@@ -418,9 +423,63 @@ int run_gate_up(moe_b200_workspace* ws, const moe_b200_weights* w, long n, int n
 }
 
 // Shared expert FFN over all rows (joint: reuses q_x; dense: own quantisation).
+// Tokens per call of the small-batch paths (the group-32 GEMVs and the
+// split-K GEMVs of a shared per-channel int8 bank).
+constexpr int kGemvMaxRows = 4;
+
+// Whether the shared FFN of `rows` tokens runs as the split-K GEMVs
+// (gemv_w8.cu): a per-channel int8 bank at one to four tokens.
+bool shared_gemv(const moe_b200_weights* w, int rows) {
+    return rows >= 1 && rows <= kGemvMaxRows && w->sgu.fmt == kFmtW8PC && w->sdn.fmt == kFmtW8PC &&
+           w->Is % 4 == 0 && w->H % 4 == 0;
+}
+
 int run_shared(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
                cudaStream_t s) {
     const int rule = w->shared_mode == MOE_B200_SHARED_JOINT ? kQuantMoe : kQuantDense;
+    if (shared_gemv(w, rows)) {
+        const bool joint = w->shared_mode == MOE_B200_SHARED_JOINT;
+        if (!joint)
+            launch_quant_gather(d_x, rows, ws->H, ws->Kh, kQuantDense, 1, nullptr, ws->q_xd, ws->s_xd,
+                                nullptr, nullptr, nullptr, nullptr, ws->err, s);
+        W8GemvArgs g{};
+        g.w = w->sgu.w;
+        g.w_tile_stride = w->sgu.w_tile_stride;
+        g.w_stage_stride = w->sgu.w_stage_stride;
+        g.wscale = w->sgu.s;
+        g.ws_tile_stride = w->sgu.s_tile_stride;
+        g.q = joint ? ws->q_x : ws->q_xd;
+        g.ld = ws->Kh;
+        g.sx = joint ? ws->s_x : ws->s_xd;
+        g.T = rows;
+        g.n = w->Is;
+        g.acc = ws->w8_acc;
+        g.counters = ws->w8_cnt;
+        g.row_max = ws->w8_max;
+        g.out = ws->s_middle;
+        g.q_out = ws->sq_m;
+        g.q_scale = ws->ss_m;
+        g.ld_q = ws->Kis;
+        g.rule = rule;
+        g.err = ws->err;
+        if (launch_shared_w8(g, true, w->sgu.row_tiles, w->sgu.kblocks / kKPS, s))
+            return MOE_B200_ERR_UNSUPPORTED;
+        W8GemvArgs d = g;
+        d.w = w->sdn.w;
+        d.w_tile_stride = w->sdn.w_tile_stride;
+        d.w_stage_stride = w->sdn.w_stage_stride;
+        d.wscale = w->sdn.s;
+        d.ws_tile_stride = w->sdn.s_tile_stride;
+        d.q = ws->sq_m;
+        d.ld = ws->Kis;
+        d.sx = ws->ss_m;
+        d.n = ws->H;
+        d.counters = ws->w8_cnt + 512;
+        d.out = ws->s_y;
+        if (launch_shared_w8(d, false, w->sdn.row_tiles, w->sdn.kblocks / kKPS, s))
+            return MOE_B200_ERR_UNSUPPORTED;
+        return MOE_B200_OK;
+    }
     const int nt = choose_nt(rows, 1);
     const int nt_g = exact_nt(nt, w->sgu.fmt);
     const bool hd = down_fmt(w->sdn.fmt, false) == kFmtW4G32H;
@@ -467,11 +526,11 @@ cudaEvent_t* prof_slot(moe_b200_workspace* ws, int flags) {
 
 // The whole routed (+ shared) pipeline on device pointers. ev != null records
 // stage events for run_profiled-style timings.
-// Small batches of group-32 banks without a shared expert run the GEMV path
-// (csrc/gemv.cu): with caller-supplied routes, 2 launches, every weight stage
-// in flight; router-inclusive calls run the whole layer as one cooperative
-// launch (decode_layer_kernel, see layer_impl).
-constexpr int kGemvMaxRows = 4;
+// Small batches of group-32 banks run the GEMV path (csrc/gemv.cu): with
+// caller-supplied routes, 2 launches, every weight stage in flight (a shared
+// expert beside them on the side stream); router-inclusive calls of banks
+// without a shared expert run the whole layer as one cooperative launch
+// (decode_layer_kernel, see layer_impl).
 
 bool use_gemv(const moe_b200_workspace* ws, const moe_b200_weights* w, int rows) {
     return rows <= kGemvMaxRows && w->gu.fmt == kFmtW4G32 && w->dn.fmt == kFmtW4G32 &&
@@ -492,14 +551,38 @@ struct GateRef {
 int run_shared(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
                cudaStream_t s);
 
+// The shared expert's FFN of a small batch on the workspace's side stream (its
+// own activation quantisation, the one-expert grouping, the tensor-core GEMMs),
+// forked from stream s; side_join marks its end. It needs no routing, so a
+// router-inclusive call starts it before the router.
+int start_shared_side(moe_b200_workspace* ws, const moe_b200_weights* w, int rows,
+                      const float* d_x, cudaStream_t s) {
+    cudaStream_t side = ws->side_stream;
+    cudaEventRecord(ws->side_fork, s);
+    cudaStreamWaitEvent(side, ws->side_fork, 0);
+    if (shared_gemv(w, rows)) {
+        ws->launches += 3;  // quantisation, gate/up (+ requantisation), down
+    } else {
+        launch_set_range(ws->shared_offsets, rows, side);  // the tensor-core GEMMs' grouping
+        ws->launches += 5;  // range, quantisation, gate/up, requantisation, down
+    }
+    if (w->shared_mode == MOE_B200_SHARED_JOINT)  // the routed rows' MoE A8 codes
+        launch_quant_gather(d_x, rows, ws->H, ws->Kh, kQuantMoe, 1, nullptr, ws->q_x, ws->s_x,
+                            nullptr, nullptr, nullptr, nullptr, ws->err, side);
+    const int rc = run_shared(ws, w, rows, d_x, side);
+    cudaEventRecord(ws->side_join, side);
+    return rc;
+}
+
 // The small-batch layer: the routed experts as two GEMV kernels (gate/up with
-// SwiGLU and requantisation, down with the combine). A shared expert runs its
-// FFN on the workspace's side stream at the same time (its own activation
-// quantisation, the one-expert grouping, the tensor-core GEMMs) and enters
-// the down kernel's combine after the ranks, as in combine_kernel.
+// SwiGLU and requantisation, down with the combine). A shared expert's FFN
+// runs beside them on the side stream (started here unless the caller already
+// did: shared_started) and enters the down kernel's combine after the ranks,
+// as in combine_kernel.
 int run_small(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
               const int32_t* d_ids, const float* d_routes, const float* d_res, float* d_out,
-              cudaStream_t s, cudaEvent_t* evs, cudaEvent_t res_ready, GateRef gate = {}) {
+              cudaStream_t s, cudaEvent_t* evs, cudaEvent_t res_ready, GateRef gate = {},
+              bool shared_started = false) {
     auto mark = [&](int i) {
         if (evs) cudaEventRecord(evs[i], s);
     };
@@ -509,16 +592,7 @@ int run_small(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const
     mark(3);
     GemvArgs a = gemv_args(ws, w, rows, d_x, d_ids, d_routes, d_res, d_out);
     if (w->shared) {
-        cudaStream_t side = ws->side_stream;
-        cudaEventRecord(ws->side_fork, s);
-        cudaStreamWaitEvent(side, ws->side_fork, 0);
-        launch_set_range(ws->shared_offsets, rows, side);
-        ws->launches += 5;  // range, quantisation, gate/up, requantisation, down
-        if (w->shared_mode == MOE_B200_SHARED_JOINT)  // the routed rows' MoE A8 codes
-            launch_quant_gather(d_x, rows, ws->H, ws->Kh, kQuantMoe, 1, nullptr, ws->q_x, ws->s_x,
-                                nullptr, nullptr, nullptr, nullptr, ws->err, side);
-        const int rc = run_shared(ws, w, rows, d_x, side);
-        cudaEventRecord(ws->side_join, side);
+        const int rc = shared_started ? MOE_B200_OK : start_shared_side(ws, w, rows, d_x, s);
         if (rc) {
             cudaStreamWaitEvent(s, ws->side_join, 0);
             return rc;
@@ -584,9 +658,10 @@ GemvArgs gemv_args(const moe_b200_workspace* ws, const moe_b200_weights* w, int 
 int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
                  const int32_t* d_ids, const float* d_routes, const float* d_res, float* d_out,
                  cudaStream_t s, cudaEvent_t* evs, cudaEvent_t res_ready = nullptr,
-                 GateRef gate = {}) {
+                 GateRef gate = {}, bool shared_started = false) {
     if (use_gemv(ws, w, rows))
-        return run_small(ws, w, rows, d_x, d_ids, d_routes, d_res, d_out, s, evs, res_ready, gate);
+        return run_small(ws, w, rows, d_x, d_ids, d_routes, d_res, d_out, s, evs, res_ready, gate,
+                         shared_started);
     const int E = ws->E, k = ws->k, H = ws->H;
     const long n = (long)rows * k;
     auto mark = [&](int i) {
@@ -595,7 +670,8 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
     // route count + scatter (when there are assignments), quantise, gate/up,
     // requantise, down, combine
     ws->launches += (n + kRouteChunk - 1) / kRouteChunk > 0 ? 7 : 5;
-    if (w->shared) ws->launches += w->shared_mode == MOE_B200_SHARED_JOINT ? 3 : 4;
+    if (w->shared)
+        ws->launches += (w->shared_mode == MOE_B200_SHARED_JOINT ? 0 : 1) + (shared_gemv(w, rows) ? 2 : 3);
     mark(1);
     launch_route_count(d_ids, d_routes, (int)n, E, ws->hist, ws->err, s);
     launch_route_scatter(d_ids, d_routes, (int)n, E, ws->hist, ws->offsets, ws->perm, ws->pos,
@@ -681,6 +757,12 @@ int read_status(moe_b200_workspace* ws, cudaStream_t s) {
             cudaMemsetAsync(ws->dec_state, 0, 2 * sizeof(uint32_t), s);
             cudaMemsetAsync(ws->gv_counters, 0, sizeof(int) * (size_t)(n + T * ((ws->H + 127) / 128)), s);
             cudaMemsetAsync(ws->counters, 0, sizeof(int) * (size_t)T, s);
+            if (ws->Is > 0) {
+                cudaMemsetAsync(ws->w8_acc, 0, sizeof(int32_t) * (size_t)kGemvMaxRows *
+                                    std::max(2L * pad_to(ws->Is, 64), (long)pad_to(ws->H, 128)), s);
+                cudaMemsetAsync(ws->w8_cnt, 0, sizeof(int) * 1024, s);
+                cudaMemsetAsync(ws->w8_max, 0, sizeof(uint32_t) * kGemvMaxRows, s);
+            }
 
         }
         cudaStreamSynchronize(s);
@@ -1051,6 +1133,10 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
         rc |= ws_alloc(ws, &ws->sq_m_h, (T + pad_rows) * ws->Kis);
         rc |= ws_alloc(ws, &ws->ss_m, T);
         rc |= ws_alloc(ws, &ws->s_y, T * ws->H);
+        rc |= ws_alloc(ws, &ws->w8_acc, (long)kGemvMaxRows * std::max(2L * pad_to(ws->Is, 64),
+                                                                      (long)pad_to(ws->H, 128)));
+        rc |= ws_alloc(ws, &ws->w8_cnt, 1024);
+        rc |= ws_alloc(ws, &ws->w8_max, kGemvMaxRows);
     }
     if (rc != MOE_B200_OK) {
         moe_b200_workspace_free(ws);
@@ -1059,6 +1145,12 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     cudaMemset(ws->counters, 0, sizeof(int) * T);
     cudaMemset(ws->gv_counters, 0, sizeof(int) * (size_t)(n + T * ((ws->H + 127) / 128)));
     cudaMemset(ws->dec_state, 0, sizeof(uint32_t) * (size_t)(n + 2));
+    if (ws->Is > 0) {
+        cudaMemset(ws->w8_acc, 0, sizeof(int32_t) * (size_t)kGemvMaxRows *
+                                      std::max(2L * pad_to(ws->Is, 64), (long)pad_to(ws->H, 128)));
+        cudaMemset(ws->w8_cnt, 0, sizeof(int) * 1024);
+        cudaMemset(ws->w8_max, 0, sizeof(uint32_t) * kGemvMaxRows);
+    }
 
     {
         int coop = 0;
@@ -1377,10 +1469,22 @@ static int layer_impl(moe_b200_workspace* ws, const moe_b200_weights* w, const m
         }
         cudaGetLastError();  // not launched: run the kernels one by one
     }
+    // a small batch with a shared expert: its FFN starts before the router
+    const bool side = use_gemv(ws, w, rows) && w->shared;
+    if (side) {
+        const int rc = start_shared_side(ws, w, rows, d_x, s);
+        if (rc) {
+            cudaStreamWaitEvent(s, ws->side_join, 0);
+            return rc;
+        }
+    }
     const int rc = route_impl(ws, r, rows, d_x, nullptr, ws->ids, ws->routes, s);
-    if (rc) return rc;
+    if (rc) {
+        if (side) cudaStreamWaitEvent(s, ws->side_join, 0);
+        return rc;
+    }
     return run_pipeline(ws, w, rows, d_x, ws->ids, ws->routes, d_res, d_out, s, evs, res_ready,
-                        router_gate(ws, r));
+                        router_gate(ws, r), side);
 }
 
 int moe_b200_forward_device(moe_b200_workspace* ws, const moe_b200_weights* w,

@@ -112,6 +112,30 @@ void launch_combine(const float* y, const int32_t* pos, const float* routes, con
                     const float* residual, int T, int H, int k, float* out, cudaStream_t s,
                     const float* gate = nullptr, int gate_ld = 0);
 
+// gemv_w8.cu: the small-batch FFN of a per-channel int8 bank (one expert: the
+// shared expert), split-K GEMVs. Gate/up: grid (row tiles, load stages),
+// out = the SwiGLU middle [T][n], then the middle's codes q_out [T][ld_q] and
+// scales q_scale under `rule`; down: out = the expert rows [T][n].
+struct W8GemvArgs {
+    const uint8_t* w;          // packed bank (one expert)
+    size_t w_tile_stride, w_stage_stride;
+    const void* wscale;        // per-channel f32 scales, tile-major
+    size_t ws_tile_stride;     // bytes
+    const int8_t* q;           // [T][ld] activation codes
+    int ld;
+    const float* sx;           // [T] activation scales
+    int T, n;
+    int32_t* acc;              // [T][row tiles * 128] zero, re-zeroed
+    int* counters;             // [row tiles + 1] zero, re-zeroed
+    uint32_t* row_max;         // [T] zero, re-zeroed (gate/up)
+    float* out;
+    int8_t* q_out;
+    float* q_scale;
+    int ld_q, rule;
+    uint32_t* err;
+};
+int launch_shared_w8(const W8GemvArgs& a, bool gateup, int row_tiles, int kstages, cudaStream_t s);
+
 // gemv.cu: the small-batch path of group-32 int4 banks (a shared expert, if
 // any, runs beside it and enters the combine of the down kernel).
 struct GemvArgs {
