@@ -49,15 +49,13 @@ __device__ __forceinline__ void finish_tile(const RouterArgs& a, int tile, int t
     if (threadIdx.x == 0) a.counters[tile] = 0;
 }
 
-// Decode-sized router: one token, RB weight rows per CTA (grid (T,
-// ceil(Ew/RB))), RB x 16 threads = RB rows x 16 lanes. The CTA's router rows
-// and the token row are staged in shared memory with one batch of 16-byte
-// copies, then each thread runs its lane's sequential FMA chain. RB = 8, or 2
-// when 8-row CTAs would leave most SMs idle (one token over 256 experts: 32
-// CTAs each staging 64 KB, against 128 CTAs of 16 KB).
+// Decode-sized router: one token, 8 weight rows per CTA (grid (T, ceil(Ew/8))),
+// 128 threads = 8 rows x 16 lanes. The CTA's router rows and the token row
+// are staged in shared memory with one batch of 16-byte copies, then each
+// thread runs its lane's sequential FMA chain.
 constexpr int kDecEB = 8;
-template <bool TF32, int RB>
-__global__ void __launch_bounds__(RB * 16) router_decode_kernel(const RouterArgs a) {
+template <bool TF32>
+__global__ void __launch_bounds__(128) router_decode_kernel(const RouterArgs a) {
     extern __shared__ __align__(16) float rsm[];
     // a small-batch layer launches its gate/up kernel as a programmatic
     // dependent: it may start its own prologue now (it waits for this grid
@@ -65,10 +63,10 @@ __global__ void __launch_bounds__(RB * 16) router_decode_kernel(const RouterArgs
     pdl_trigger();
     const int H = a.H;
     const int stride = H + 16;  // padded rows: the two rows of a warp use different banks
-    float* w_s = rsm;                 // [RB][stride]
-    float* x_s = rsm + RB * stride;   // [H]
-    const int t = blockIdx.x, e0 = blockIdx.y * RB;
-    const int ne = min(RB, a.Ew - e0);
+    float* w_s = rsm;                     // [8][stride]
+    float* x_s = rsm + kDecEB * stride;   // [H]
+    const int t = blockIdx.x, e0 = blockIdx.y * kDecEB;
+    const int ne = min(kDecEB, a.Ew - e0);
     const int H16 = (H / 16) * 16;
     const bool vec = (H & 3) == 0;
     if (vec) {
@@ -240,9 +238,7 @@ static void launch_tile4(const RouterArgs& a, cudaStream_t s) {
 }
 
 constexpr size_t kDecMaxSmem = 200 * 1024;
-static size_t decode_router_smem(int H, int rb = kDecEB) {
-    return sizeof(float) * ((size_t)rb * (H + 16) + H);
-}
+static size_t decode_router_smem(int H) { return sizeof(float) * ((size_t)kDecEB * (H + 16) + H); }
 
 bool router_fits(int rows, int hidden, int order) {
     return order == kOrderSequential || rows >= 16 || decode_router_smem(hidden) <= kDecMaxSmem;
@@ -251,20 +247,12 @@ bool router_fits(int rows, int hidden, int order) {
 template <bool TF32>
 static int launch_router_t(const RouterArgs& a, cudaStream_t s) {
     if (a.T < 16) {
-        if ((long)a.T * ((a.Ew + kDecEB - 1) / kDecEB) < 96) {  // spread small routers wider
-            const size_t smem = decode_router_smem(a.H, 2);
-            cudaFuncSetAttribute(router_decode_kernel<TF32, 2>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            dim3 grid(a.T, (a.Ew + 1) / 2);
-            router_decode_kernel<TF32, 2><<<grid, 32, smem, s>>>(a);
-            return 0;
-        }
         const size_t smem = decode_router_smem(a.H);
         if (smem > kDecMaxSmem) return -1;
-        cudaFuncSetAttribute(router_decode_kernel<TF32, kDecEB>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(router_decode_kernel<TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
         dim3 grid(a.T, (a.Ew + kDecEB - 1) / kDecEB);
-        router_decode_kernel<TF32, kDecEB><<<grid, 128, smem, s>>>(a);
+        router_decode_kernel<TF32><<<grid, 128, smem, s>>>(a);
         return 0;
     }
     // logits, then one warp per token for the routing (a separate launch: the
