@@ -303,6 +303,8 @@ struct moe_b200_workspace {
     // a side stream beside the routed GEMVs (fork / join events)
     cudaStream_t side_stream = nullptr;
     cudaEvent_t side_fork = nullptr, side_join = nullptr;
+    // host-buffer calls: a pinned word for the status read with the outputs
+    uint32_t* h_err = nullptr;
     cudaEvent_t res_ready = nullptr;
     cudaEvent_t x_ready = nullptr;  // host-API input upload done (orders the residual's after it)
     cudaStream_t last_stream = nullptr;
@@ -742,11 +744,19 @@ void fill_timings(moe_b200_workspace* ws, moe_b200_timings* t, int rows, bool ro
     fill_timings_from(ws->ev, ws, t, rows, routed_by_us, shared);
 }
 
+int handle_status(moe_b200_workspace* ws, uint32_t bits, cudaStream_t s);
+
 int read_status(moe_b200_workspace* ws, cudaStream_t s) {
     uint32_t bits = 0;
     cudaError_t e = cudaMemcpyAsync(&bits, ws->err, sizeof(bits), cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_rc(e);
+    return handle_status(ws, bits, s);
+}
+
+// The status bits of a finished call: cleared on the device, the counters a
+// timed-out wait can leave mid-count rearmed, the first cause reported.
+int handle_status(moe_b200_workspace* ws, uint32_t bits, cudaStream_t s) {
     if (bits) {
         cudaMemsetAsync(ws->err, 0, sizeof(uint32_t), s);
         // a wait that gave up can leave the grid barrier and the last-arrival
@@ -1179,11 +1189,13 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
          cudaStreamCreateWithFlags(&ws->side_stream, cudaStreamNonBlocking) != cudaSuccess ||
          cudaEventCreateWithFlags(&ws->side_fork, cudaEventDisableTiming) != cudaSuccess ||
          cudaEventCreateWithFlags(&ws->side_join, cudaEventDisableTiming) != cudaSuccess ||
+         cudaMallocHost(&ws->h_err, sizeof(uint32_t)) != cudaSuccess ||
          cudaEventCreateWithFlags(&ws->res_ready, cudaEventDisableTiming) != cudaSuccess ||
          cudaEventCreateWithFlags(&ws->x_ready, cudaEventDisableTiming) != cudaSuccess))
         rc = MOE_B200_ERR_CUDA;
     if (rc == MOE_B200_OK && cudaStreamCreateWithFlags(&ws->own_stream, cudaStreamNonBlocking) != cudaSuccess)
         rc = MOE_B200_ERR_CUDA;
+
     for (int i = 0; i < 12 && rc == MOE_B200_OK; ++i)
         if (cudaEventCreate(&ws->ev[i]) != cudaSuccess) rc = MOE_B200_ERR_CUDA;
     if (rc != MOE_B200_OK || cudaDeviceSynchronize() != cudaSuccess) {
@@ -1207,6 +1219,7 @@ void moe_b200_workspace_free(moe_b200_workspace* ws) {
         cudaStreamDestroy(ws->side_stream);
     }
     if (ws->side_fork) cudaEventDestroy(ws->side_fork);
+    if (ws->h_err) cudaFreeHost(ws->h_err);
     if (ws->side_join) cudaEventDestroy(ws->side_join);
     if (ws->copy_stream) {
         cudaStreamSynchronize(ws->copy_stream);
@@ -1939,10 +1952,12 @@ int moe_b200_forward_f32(moe_b200_workspace* ws, const moe_b200_weights* w,
     cudaMemcpyAsync(output, ws->out, xb, cudaMemcpyDeviceToHost, s);
     if (ids) cudaMemcpyAsync(ids, ws->ids, sizeof(int32_t) * nb, cudaMemcpyDeviceToHost, s);
     if (routes) cudaMemcpyAsync(routes, ws->routes, sizeof(float) * nb, cudaMemcpyDeviceToHost, s);
+    // the status word comes down with the outputs: one synchronisation per call
+    cudaMemcpyAsync(ws->h_err, ws->err, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
     if (timings) cudaEventRecord(ws->ev[9], s);
     cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_rc(e);
-    rc = read_status(ws, s);
+    rc = handle_status(ws, *ws->h_err, s);
     if (timings) {
         fill_timings(ws, timings, rows, true, w->shared != 0);
         timings->sync_us = 1000.0 * ev_ms(ws->ev[8], ws->ev[9]);
