@@ -133,7 +133,11 @@ struct GemmCfg {
     static constexpr int kConvWarps = kF16 ? 8 : 4;
     static constexpr int kEpiWarp0 = kConvWarp0 + kConvWarps;  // first epilogue warp
     static constexpr int kStoreWarp = kEpiWarp0 + kEpiWarps;   // exact group path only
-    static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps + (kGroup ? 1 : 0));
+    // exact group path: two MMA issuers (lane 0 of warp 1 and of this warp) on
+    // alternating k-blocks; a thread issues one MMA per ~65 cycles whatever N
+    static constexpr int kIssuers = kGroup ? 2 : 1;
+    static constexpr int kIssuerWarp2 = kStoreWarp + 1;
+    static constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps + (kGroup ? 2 : 0));
     static_assert(kLoadBytes % 1024 == 0, "stage alignment of the swizzled operands");
     static_assert(kLoadStages >= 2, "smem budget");
     static_assert(kLoadStages >= kAStages, "operand ring reuse is ordered by the load ring");
@@ -243,16 +247,16 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
         abort_s = 0;
         for (int i = 0; i < SL; ++i) {
             mbar_init(&lfull[i], 1);
-            // exact group path: the MMA commit and every epilogue warp (the stage
-            // holds the group scales the epilogue reads)
-            mbar_init(&lempty[i], C::kGroup ? 1 + kEpiWarps : 1);
+            // exact group path: the issuers' MMA commits and every epilogue warp
+            // (the stage holds the group scales the epilogue reads)
+            mbar_init(&lempty[i], C::kGroup ? C::kIssuers + kEpiWarps : 1);
         }
         for (int i = 0; i < AS; ++i) mbar_init(&ofull[i], C::kConvWarps);
         for (int i = 0; i < C::kNSlot; ++i) {
             mbar_init(&tfull[i], 1);
             mbar_init(&tempty[i], kEpiWarps);
         }
-        mbar_init(done, 1);
+        mbar_init(done, C::kIssuers);
         mbar_init(sfull, kEpiWarps);
         mbar_init(sempty, 1);
         fence_barrier_init();
@@ -347,11 +351,13 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
             for (uint32_t d = it > (uint32_t)SL ? it - SL : 0u; d < it; ++d)
                 mbar_wait(&lfull[d % SL], (d / SL) & 1u, &never, a.err);
         }
-    } else if (warp == kMmaWarp) {
+    } else if (warp == kMmaWarp || (C::kGroup && warp == C::kIssuerWarp2)) {
         // ------------------------------------------------------------ MMA issuer
         // One tcgen05.commit per stage (stage empty, which also frees the W4
         // operand slot) and per tile (accumulator full); the exact group path
-        // commits per k-block instead of per tile.
+        // commits per k-block instead of per tile, its two issuers taking the
+        // even and the odd k-blocks (each commits its share of every stage).
+        const uint32_t me = warp == kMmaWarp ? 0u : 1u;
         if (lane == 0) {
             constexpr uint32_t idesc = C::kF16 ? idesc_f16(kTileRows, NT) : idesc_i8(kTileRows, NT);
             uint32_t it = 0, kbc = 0, ti = 0;  // stage, k-block and tile counters
@@ -388,6 +394,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap act_map, const GemmArgs 
                     } else {
 #pragma unroll
                         for (int jk = 0; jk < kKPS; ++jk, ++kbc) {
+                            if (C::kGroup && kbc % C::kIssuers != me) continue;
                             uint32_t slot = 0;
                             if (C::kGroup) {
                                 slot = kbc % C::kNSlot;
