@@ -317,9 +317,10 @@ struct moe_b200_workspace {
     int32_t *hist = nullptr, *offsets = nullptr, *perm = nullptr, *pos = nullptr;
     int32_t *shared_offsets = nullptr, *counters = nullptr;
     int32_t* gv_counters = nullptr;  // small-batch path: last-arrival counters
-    // fused small-batch layer: the grid barrier's 64-bit counter, then
+    // fused small-batch layer: the grid barrier's counters (dec_bar), and
     // [n_max] middle-row max bits
     uint32_t* dec_state = nullptr;
+    unsigned long long* dec_bar = nullptr;  // [8 x 16]: eight counters 128 bytes apart
     bool coop = false;  // the device runs cooperative launches
     int8_t* a_perm = nullptr;
     __half *q_m_h = nullptr, *sq_m_h = nullptr;  // fp16 copies of the middle codes (group-32 down)
@@ -764,7 +765,7 @@ int handle_status(moe_b200_workspace* ws, uint32_t bits, cudaStream_t s) {
         // so that no later call hands off early
         if (bits & kErrWaitTimeout) {
             const long T = ws->max_rows, n = ws->n_max;
-            cudaMemsetAsync(ws->dec_state, 0, 2 * sizeof(uint32_t), s);
+            cudaMemsetAsync(ws->dec_bar, 0, sizeof(unsigned long long) * 128, s);
             cudaMemsetAsync(ws->gv_counters, 0, sizeof(int) * (size_t)(n + T * ((ws->H + 127) / 128)), s);
             cudaMemsetAsync(ws->counters, 0, sizeof(int) * (size_t)T, s);
             if (ws->Is > 0) {
@@ -1125,6 +1126,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     rc |= ws_alloc(ws, &ws->counters, T);
     rc |= ws_alloc(ws, &ws->gv_counters, n + T * ((ws->H + 127) / 128));
     rc |= ws_alloc(ws, &ws->dec_state, n + 2);
+    rc |= ws_alloc(ws, &ws->dec_bar, 128);
     rc |= ws_alloc(ws, &ws->a_perm, (n + pad_rows) * ws->Kh);
     rc |= ws_alloc(ws, &ws->q_m_h, (n + pad_rows) * ws->Ki);
     rc |= ws_alloc(ws, &ws->s_perm, n);
@@ -1155,6 +1157,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     cudaMemset(ws->counters, 0, sizeof(int) * T);
     cudaMemset(ws->gv_counters, 0, sizeof(int) * (size_t)(n + T * ((ws->H + 127) / 128)));
     cudaMemset(ws->dec_state, 0, sizeof(uint32_t) * (size_t)(n + 2));
+    cudaMemset(ws->dec_bar, 0, sizeof(unsigned long long) * 128);
     if (ws->Is > 0) {
         cudaMemset(ws->w8_acc, 0, sizeof(int32_t) * (size_t)kGemvMaxRows *
                                       std::max(2L * pad_to(ws->Is, 64), (long)pad_to(ws->H, 128)));
@@ -1468,7 +1471,7 @@ static int layer_impl(moe_b200_workspace* ws, const moe_b200_weights* w, const m
         DecodeArgs d{};
         d.r = router_args(ws, r, rows, d_x, nullptr, ws->ids, ws->routes);
         d.g = gemv_args(ws, w, rows, d_x, ws->ids, ws->routes, d_res, d_out);
-        d.bar = reinterpret_cast<unsigned long long*>(ws->dec_state);
+        d.bar = ws->dec_bar;
         d.mmax = ws->dec_state + 2;
         for (int i = 1; evs && i <= 3; ++i) cudaEventRecord(evs[i], s);
         if (launch_decode_layer(d, ws->num_sms, s) == 0) {

@@ -395,24 +395,35 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long
     return v;
 }
 
-// Grid-wide barrier (every CTA is resident: cooperative launch) on one
-// counter that only grows: a CTA's arrival returns the count before it, and
-// the barrier it belongs to completes when the count reaches the next
-// multiple of gridDim.x (the counter rests on a multiple of it between
-// barriers, which every launch of the same grid keeps). One atomic per CTA,
-// no reset round trip. Waits at most kWaitLimitNs, then kErrWaitTimeout and
-// false (the caller gives up; the host rearms the counter).
-__device__ bool grid_sync(unsigned long long* cnt, uint32_t* err) {
+// Grid-wide barrier (every CTA is resident: cooperative launch) over
+// kGridBarLanes counters 128 bytes apart that only grow: CTA b arrives on
+// counter b % kGridBarLanes (n_j CTAs share counter j), so the atomics of one
+// barrier spread over eight lines instead of queueing on one; between barriers
+// counter j rests on a multiple of n_j (every launch has the same grid), so an
+// arrival's count before it tells the barrier's number m, and the barrier
+// completes when every counter j reaches (m + 1) n_j (lanes 0..7 of warp 0
+// poll one counter each). Waits at most kWaitLimitNs, then kErrWaitTimeout
+// and false (the caller gives up; the host rearms the counters).
+constexpr int kGridBarLanes = 8, kGridBarStride = 16;  // u64 counters, 128 bytes apart
+
+__device__ bool grid_sync(unsigned long long* bar, uint32_t* err) {
     __shared__ int ok_s;
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x, nb = gridDim.x, j0 = blockIdx.x % kGridBarLanes;
+        unsigned long long m = 0;
+        if (lane == 0) {
+            __threadfence();
+            const unsigned long long nj = (nb - j0 + kGridBarLanes - 1) / kGridBarLanes;
+            m = atomicAdd(bar + j0 * kGridBarStride, 1ull) / nj;
+        }
+        m = __shfl_sync(0xffffffffu, m, 0);
         int ok = 1;
-        __threadfence();
-        const unsigned long long old = atomicAdd(cnt, 1ull);
-        const unsigned long long target = old - old % gridDim.x + gridDim.x;
-        if (old + 1 != target) {
+        if (lane < kGridBarLanes) {
+            const unsigned long long nl = (nb - lane + kGridBarLanes - 1) / kGridBarLanes;
+            const unsigned long long target = (m + 1) * nl;
             const uint64_t start = global_timer_ns();
-            while (ld_acquire_gpu(cnt) < target) {
+            while (ld_acquire_gpu(bar + lane * kGridBarStride) < target) {
                 if (global_timer_ns() - start > kWaitLimitNs) {
                     atomicOr(err, kErrWaitTimeout);
                     ok = 0;
@@ -420,8 +431,11 @@ __device__ bool grid_sync(unsigned long long* cnt, uint32_t* err) {
                 }
             }
         }
-        __threadfence();
-        ok_s = ok;
+        ok = __all_sync(0xffffffffu, ok);
+        if (lane == 0) {
+            __threadfence();
+            ok_s = ok;
+        }
     }
     __syncthreads();
     return ok_s != 0;
@@ -600,14 +614,25 @@ __global__ void __launch_bounds__(kGvThreads, 1) decode_layer_kernel(const Decod
                 d.keys[e] = (uint32_t)total_key(l) ^ 0x80000000u;
             }
             if (__syncthreads_or(!fin) && tid == 0) atomicOr(r.err, kErrNonFinite);
-            for (int e = tid; e < r.E; e += kGvThreads) {
-                const uint32_t ke = d.keys[e];
+            // P consecutive threads rank one element, each over a share of
+            // the keys (P: the largest power of two with P * E threads)
+            int P = 1;
+            while (P < 32 && 2 * P * r.E <= kGvThreads) P *= 2;
+            const int share = (r.E + P - 1) / P;
+            for (int base = 0; base < r.E * P; base += kGvThreads) {
+                const int idx = base + tid, e = idx / P, part = idx % P;
                 int rank = 0;
-                for (int jj = 0; jj < r.E; ++jj) {
-                    const uint32_t kj = d.keys[jj];
-                    rank += (kj > ke || (kj == ke && jj < e)) ? 1 : 0;
+                uint32_t ke = 0;
+                if (e < r.E) {
+                    ke = d.keys[e];
+                    const int j1 = min(r.E, (part + 1) * share);
+                    for (int jj = part * share; jj < j1; ++jj) {
+                        const uint32_t kj = d.keys[jj];
+                        rank += (kj > ke || (kj == ke && jj < e)) ? 1 : 0;
+                    }
                 }
-                if (rank < k) {
+                for (int o = 1; o < P; o <<= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
+                if (e < r.E && part == 0 && rank < k) {
                     d.rid[t * k + rank] = e;
                     d.selv[rank] = key_value((int32_t)(ke ^ 0x80000000u));
                 }
