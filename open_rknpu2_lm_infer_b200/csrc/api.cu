@@ -338,6 +338,11 @@ struct moe_b200_workspace {
     int32_t* w8_acc = nullptr;
     int* w8_cnt = nullptr;
     uint32_t* w8_max = nullptr;
+    // small-batch routed experts of per-channel int8 banks (split-K GEMVs)
+    int32_t* w8r_acc = nullptr;
+    int* w8r_cnt = nullptr;
+    uint32_t* w8r_max = nullptr;
+    size_t w8r_acc_n = 0, w8r_cnt_n = 0;
     float* logits = nullptr;
     uint32_t* err = nullptr;
     CUtensorMap map_a[3], map_qm[3], map_qx[3], map_qxd[3], map_sqm[3];
@@ -545,6 +550,14 @@ GemvArgs gemv_args(const moe_b200_workspace* ws, const moe_b200_weights* w, int 
                    const float* d_x, const int32_t* d_ids, const float* d_routes,
                    const float* d_res, float* d_out);
 
+// Small batches of per-channel int8 routed banks: the split-K GEMVs of
+// gemv_w8.cu (gate/up with the token's codes, SwiGLU and the middle's codes;
+// down with the combine).
+bool use_w8_gemv(const moe_b200_workspace* ws, const moe_b200_weights* w, int rows) {
+    return rows >= 1 && rows <= kGemvMaxRows && w->gu.fmt == kFmtW8PC && w->dn.fmt == kFmtW8PC &&
+           ws->k <= 32 && ws->H % 4 == 0 && ws->I % 4 == 0;
+}
+
 // The shared-gate logits of a gated router: column E of the workspace logits.
 struct GateRef {
     const float* logits = nullptr;
@@ -575,6 +588,81 @@ int start_shared_side(moe_b200_workspace* ws, const moe_b200_weights* w, int row
     const int rc = run_shared(ws, w, rows, d_x, side);
     cudaEventRecord(ws->side_join, side);
     return rc;
+}
+
+int run_small_w8(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, const float* d_x,
+                 const int32_t* d_ids, const float* d_routes, const float* d_res, float* d_out,
+                 cudaStream_t s, cudaEvent_t* evs, cudaEvent_t res_ready, GateRef gate,
+                 bool shared_started) {
+    auto mark = [&](int i) {
+        if (evs) cudaEventRecord(evs[i], s);
+    };
+    ws->launches += 2;
+    mark(1);
+    mark(2);
+    mark(3);
+    W8RoutedArgs a{};
+    a.ids = d_ids;
+    a.routes = d_routes;
+    a.T = rows;
+    a.k = ws->k;
+    a.E = ws->E;
+    a.H = ws->H;
+    a.I = ws->I;
+    a.gu_stages = w->gu.kblocks / kKPS;
+    a.dn_stages = w->dn.kblocks / kKPS;
+    a.x = d_x;
+    a.gu_w = w->gu.w;
+    a.gu_expert_stride = w->gu.w_expert_stride;
+    a.gu_tile_stride = w->gu.w_tile_stride;
+    a.gu_stage_stride = w->gu.w_stage_stride;
+    a.gu_s = static_cast<const float*>(w->gu.s);
+    a.gu_s_expert_stride = w->gu.s_expert_stride;
+    a.gu_s_tile_stride = w->gu.s_tile_stride;
+    a.dn_w = w->dn.w;
+    a.dn_expert_stride = w->dn.w_expert_stride;
+    a.dn_tile_stride = w->dn.w_tile_stride;
+    a.dn_stage_stride = w->dn.w_stage_stride;
+    a.dn_s = static_cast<const float*>(w->dn.s);
+    a.dn_s_expert_stride = w->dn.s_expert_stride;
+    a.dn_s_tile_stride = w->dn.s_tile_stride;
+    a.acc = ws->w8r_acc;
+    a.counters = ws->w8r_cnt;
+    a.row_max = ws->w8r_max;
+    a.middle = ws->gate_up;
+    a.q_m = ws->q_m;
+    a.s_m = ws->s_m;
+    a.ld_qm = ws->Ki;
+    a.y = ws->y;
+    a.residual = d_res;
+    a.out = d_out;
+    a.err = ws->err;
+    if (w->shared) {
+        const int rc = shared_started ? MOE_B200_OK : start_shared_side(ws, w, rows, d_x, s);
+        if (rc) {
+            cudaStreamWaitEvent(s, ws->side_join, 0);
+            return rc;
+        }
+        a.shared = ws->s_y;
+        a.gate = gate.logits;
+        a.gate_ld = gate.ld;
+    }
+    if (launch_routed_w8(a, 0, s)) {
+        if (w->shared) cudaStreamWaitEvent(s, ws->side_join, 0);
+        return MOE_B200_ERR_UNSUPPORTED;
+    }
+    mark(4);
+    mark(5);
+    if (res_ready) cudaStreamWaitEvent(s, res_ready, 0);
+    if (w->shared) cudaStreamWaitEvent(s, ws->side_join, 0);
+    if (launch_routed_w8(a, 1, s)) return MOE_B200_ERR_UNSUPPORTED;
+    mark(6);
+    mark(7);
+    mark(8);
+    ws->last_rows = 0;  // no permuted accumulators to dump for this call
+    ws->last_w = w;
+    ws->last_stream = s;
+    return cuda_rc(cudaPeekAtLastError());
 }
 
 // The small-batch layer: the routed experts as two GEMV kernels (gate/up with
@@ -665,6 +753,9 @@ int run_pipeline(moe_b200_workspace* ws, const moe_b200_weights* w, int rows, co
     if (use_gemv(ws, w, rows))
         return run_small(ws, w, rows, d_x, d_ids, d_routes, d_res, d_out, s, evs, res_ready, gate,
                          shared_started);
+    if (use_w8_gemv(ws, w, rows))
+        return run_small_w8(ws, w, rows, d_x, d_ids, d_routes, d_res, d_out, s, evs, res_ready,
+                            gate, shared_started);
     const int E = ws->E, k = ws->k, H = ws->H;
     const long n = (long)rows * k;
     auto mark = [&](int i) {
@@ -766,6 +857,9 @@ int handle_status(moe_b200_workspace* ws, uint32_t bits, cudaStream_t s) {
         if (bits & kErrWaitTimeout) {
             const long T = ws->max_rows, n = ws->n_max;
             cudaMemsetAsync(ws->dec_bar, 0, sizeof(unsigned long long) * 128, s);
+            cudaMemsetAsync(ws->w8r_acc, 0, sizeof(int32_t) * ws->w8r_acc_n, s);
+            cudaMemsetAsync(ws->w8r_cnt, 0, sizeof(int) * ws->w8r_cnt_n, s);
+            cudaMemsetAsync(ws->w8r_max, 0, sizeof(uint32_t) * (size_t)kGemvMaxRows * ws->k, s);
             cudaMemsetAsync(ws->gv_counters, 0, sizeof(int) * (size_t)(n + T * ((ws->H + 127) / 128)), s);
             cudaMemsetAsync(ws->counters, 0, sizeof(int) * (size_t)T, s);
             if (ws->Is > 0) {
@@ -1127,6 +1221,15 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     rc |= ws_alloc(ws, &ws->gv_counters, n + T * ((ws->H + 127) / 128));
     rc |= ws_alloc(ws, &ws->dec_state, n + 2);
     rc |= ws_alloc(ws, &ws->dec_bar, 128);
+    {
+        const long ns = (long)kGemvMaxRows * ws->k;
+        const long gt = (ws->I + 63) / 64, dt = (ws->H + 127) / 128;
+        ws->w8r_acc_n = (size_t)ns * std::max(gt, dt) * 128;
+        ws->w8r_cnt_n = (size_t)(ns * gt + ns + ns * dt + (long)kGemvMaxRows * dt);
+        rc |= ws_alloc(ws, &ws->w8r_acc, (long)ws->w8r_acc_n);
+        rc |= ws_alloc(ws, &ws->w8r_cnt, (long)ws->w8r_cnt_n);
+        rc |= ws_alloc(ws, &ws->w8r_max, ns);
+    }
     rc |= ws_alloc(ws, &ws->a_perm, (n + pad_rows) * ws->Kh);
     rc |= ws_alloc(ws, &ws->q_m_h, (n + pad_rows) * ws->Ki);
     rc |= ws_alloc(ws, &ws->s_perm, n);
@@ -1158,6 +1261,9 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     cudaMemset(ws->gv_counters, 0, sizeof(int) * (size_t)(n + T * ((ws->H + 127) / 128)));
     cudaMemset(ws->dec_state, 0, sizeof(uint32_t) * (size_t)(n + 2));
     cudaMemset(ws->dec_bar, 0, sizeof(unsigned long long) * 128);
+    cudaMemset(ws->w8r_acc, 0, sizeof(int32_t) * ws->w8r_acc_n);
+    cudaMemset(ws->w8r_cnt, 0, sizeof(int) * ws->w8r_cnt_n);
+    cudaMemset(ws->w8r_max, 0, sizeof(uint32_t) * (size_t)kGemvMaxRows * ws->k);
     if (ws->Is > 0) {
         cudaMemset(ws->w8_acc, 0, sizeof(int32_t) * (size_t)kGemvMaxRows *
                                       std::max(2L * pad_to(ws->Is, 64), (long)pad_to(ws->H, 128)));
@@ -1486,7 +1592,7 @@ static int layer_impl(moe_b200_workspace* ws, const moe_b200_weights* w, const m
         cudaGetLastError();  // not launched: run the kernels one by one
     }
     // a small batch with a shared expert: its FFN starts before the router
-    const bool side = use_gemv(ws, w, rows) && w->shared;
+    const bool side = (use_gemv(ws, w, rows) || use_w8_gemv(ws, w, rows)) && w->shared;
     if (side) {
         const int rc = start_shared_side(ws, w, rows, d_x, s);
         if (rc) {

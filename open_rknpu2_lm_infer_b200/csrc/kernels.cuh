@@ -136,6 +136,42 @@ struct W8GemvArgs {
 };
 int launch_shared_w8(const W8GemvArgs& a, bool gateup, int row_tiles, int kstages, cudaStream_t s);
 
+// gemv_w8.cu: the routed experts of a per-channel int8 bank at one to four
+// tokens, the same split-K GEMVs per kept assignment: gate/up (the token's
+// MoE A8 codes, SwiGLU, the middle's codes) into q_m / s_m, then down with
+// the last-arrival combine of a (token, 128-channel tile): the kept ranks in
+// rank order, the shared row (sigmoid-gated if gate), the residual.
+struct W8RoutedArgs {
+    const int32_t* ids;        // [T][k]
+    const float* routes;       // [T][k]
+    int T, k, E, H, I;
+    int gu_stages, dn_stages;  // 256-k load stages of the two banks
+    const float* x;            // [T][H]
+    const uint8_t* gu_w;       // packed gate|up bank
+    size_t gu_expert_stride, gu_tile_stride, gu_stage_stride;
+    const float* gu_s;         // per-channel scales
+    size_t gu_s_expert_stride, gu_s_tile_stride;
+    const uint8_t* dn_w;
+    size_t dn_expert_stride, dn_tile_stride, dn_stage_stride;
+    const float* dn_s;
+    size_t dn_s_expert_stride, dn_s_tile_stride;
+    int32_t* acc;              // [T*k][max(2I, H) padded] zero, re-zeroed
+    int* counters;             // [T*k*(gu tiles + 1 + dn tiles) + T*dn tiles] zero, re-zeroed
+    uint32_t* row_max;         // [T*k] zero, re-zeroed
+    float* middle;             // [T*k][I]
+    int8_t* q_m;               // [T*k][ld_qm]
+    float* s_m;                // [T*k]
+    int ld_qm;
+    float* y;                  // [T*k][H]
+    const float* shared;       // [T][H] or null
+    const float* gate;         // shared-gate logits or null
+    int gate_ld;
+    const float* residual;     // [T][H] or null
+    float* out;                // [T][H]
+    uint32_t* err;
+};
+int launch_routed_w8(const W8RoutedArgs& a, int part, cudaStream_t s);
+
 // gemv.cu: the small-batch path of group-32 int4 banks (a shared expert, if
 // any, runs beside it and enters the combine of the down kernel).
 struct GemvArgs {

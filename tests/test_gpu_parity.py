@@ -71,7 +71,9 @@ CASES = [("c1", 32), ("c1", 1), ("c2_e32", 1), ("c2_e32", 37), ("c2_e32", 300),
          ("c2", 64), ("c2_rounded", 64),
          # small batches of a bank with a shared expert: the routed GEMVs with
          # the shared FFN beside them on the side stream
-         ("c3_e32", 1), ("c3_e32", 3), ("c3_e32", 4)]
+         ("c3_e32", 1), ("c3_e32", 3), ("c3_e32", 4),
+         # small batches of a per-channel int8 bank: the routed split-K GEMVs
+         ("w8pc", 1), ("w8pc", 3), ("w8pc", 4)]
 
 
 @pytest.mark.parametrize("name,T", CASES)
@@ -338,7 +340,8 @@ def test_exact_group_format_reaches_the_library(cuda, oracle):
     assert_close(outs[0], outs[1], what="fp16 vs exact down projection")
 
 
-@pytest.mark.parametrize("name,T", [("c2_e32", 1), ("c2_e32", 37), ("c1", 32)])
+@pytest.mark.parametrize("name,T", [("c2_e32", 1), ("c2_e32", 37), ("c1", 32), ("w8pc", 2),
+                                    ("c3_e32", 2)])
 def test_graph_replay_matches_forward(cuda, oracle, name, T):
     """A captured forward (moe_b200_graph_*) replays the same layer bit for bit,
     and reads its input buffer afresh on every replay."""
