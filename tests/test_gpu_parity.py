@@ -73,7 +73,9 @@ CASES = [("c1", 32), ("c1", 1), ("c2_e32", 1), ("c2_e32", 37), ("c2_e32", 300),
          # the shared FFN beside them on the side stream
          ("c3_e32", 1), ("c3_e32", 3), ("c3_e32", 4),
          # small batches of a per-channel int8 bank: the routed split-K GEMVs
-         ("w8pc", 1), ("w8pc", 3), ("w8pc", 4)]
+         ("w8pc", 1), ("w8pc", 3), ("w8pc", 4),
+         # just above the small batches (8 tokens): the tensor-core paths
+         ("c2_e32", 8), ("c3_e32", 8), ("w8pc", 8)]
 
 
 @pytest.mark.parametrize("name,T", CASES)
