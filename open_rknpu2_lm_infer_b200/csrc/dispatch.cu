@@ -27,12 +27,33 @@ namespace moe {
 
 __device__ __forceinline__ bool route_kept(float w) { return w > 0.0f; }
 
+// The kernels of this file launch as programmatic dependents of the kernel
+// before them on the stream: their launch overlaps that kernel's last CTAs,
+// and each waits (pdl_wait, first thing) for it to complete before reading
+// anything.
+template <typename... KArgs, typename... Args>
+static void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Keys: id / div for ids in [0, id_limit) (div = 1: the expert; div = experts
 // per rank: the destination rank of expert parallelism). routes == nullptr:
 // every assignment is kept.
 __global__ void route_count_kernel(const int32_t* __restrict__ ids, const float* __restrict__ routes,
                                    int n, int E, int id_limit, int div, int32_t* hist,
                                    uint32_t* err) {
+    pdl_wait();
     extern __shared__ int32_t hist_s[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) hist_s[e] = 0;
     __syncthreads();
@@ -59,6 +80,7 @@ route_scatter_kernel(const int32_t* __restrict__ ids, const float* __restrict__ 
                      int E, int id_limit, int div, const int32_t* __restrict__ hist,
                      int32_t* offsets, int32_t* perm, int32_t* pos, int32_t* shared_offsets,
                      int T) {
+    pdl_wait();
     extern __shared__ int32_t sm[];
     int32_t* off_s = sm;               // E+1
     int32_t* base_s = off_s + E + 1;   // E
@@ -169,6 +191,7 @@ __global__ void __launch_bounds__(256)
 quant_gather_kernel(const float* __restrict__ x, int H, int ld_q, int rule, int k,
                     const int32_t* __restrict__ pos, int8_t* q_rows, float* s_rows,
                     int8_t* q_perm, float* s_perm, __half* h_rows, __half* h_perm, uint32_t* err) {
+    pdl_wait();
     __shared__ float red[8];
     __shared__ int slots[32];
     __shared__ int nslot_s;
@@ -227,6 +250,7 @@ template <int V>
 __global__ void __launch_bounds__(128)
 requant_kernel(const float* __restrict__ gate_up, const int32_t* __restrict__ count, int I,
                int ld_q, int rule, int8_t* q, __half* qh, float* sc) {
+    pdl_wait();
     __shared__ float red[4];
     const int row = blockIdx.x;
     if (row >= *count) return;
@@ -271,6 +295,7 @@ combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ pos,
                const float* __restrict__ routes, const float* __restrict__ shared,
                const float* __restrict__ residual, int H, int k, float* out,
                const float* __restrict__ gate, int gate_ld) {
+    pdl_wait();
     __shared__ int ps[32];
     __shared__ float ws[32];
     __shared__ float gscale;
@@ -325,8 +350,8 @@ void launch_route_count(const int32_t* ids, const float* routes, int n, int E, i
                         uint32_t* err, cudaStream_t s, int id_limit, int div) {
     const int nb = (n + kRouteChunk - 1) / kRouteChunk;
     if (nb == 0) return;
-    route_count_kernel<<<nb, 256, sizeof(int32_t) * E, s>>>(
-        ids, routes, n, E, id_limit > 0 ? id_limit : E, div, hist, err);
+    launch_pdl(route_count_kernel, dim3(nb), dim3(256), sizeof(int32_t) * E, s, ids, routes, n, E,
+               id_limit > 0 ? id_limit : E, div, hist, err);
 }
 
 void launch_route_scatter(const int32_t* ids, const float* routes, int n, int E,
@@ -337,9 +362,8 @@ void launch_route_scatter(const int32_t* ids, const float* routes, int n, int E,
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem);
-    route_scatter_kernel<<<nb > 0 ? nb : 1, 256, smem, s>>>(
-        ids, routes, n, E, id_limit > 0 ? id_limit : E, div, hist, offsets, perm, pos,
-        shared_offsets, T);
+    launch_pdl(route_scatter_kernel, dim3(nb > 0 ? nb : 1), dim3(256), smem, s, ids, routes, n, E,
+               id_limit > 0 ? id_limit : E, div, hist, offsets, perm, pos, shared_offsets, T);
 }
 
 // Expert parallelism: the destination-local expert id of each packed row.
@@ -400,7 +424,7 @@ void launch_quant_gather(const float* x, int T, int H, int ld_q, int rule, int k
                          cudaStream_t s) {
     if (T == 0) return;
     const int v = (H / 4 + 255) / 256;
-#define QG(V) quant_gather_kernel<V><<<T, 256, 0, s>>>(x, H, ld_q, rule, k, pos, q_rows, s_rows, q_perm, s_perm, h_rows, h_perm, err)
+#define QG(V) launch_pdl(quant_gather_kernel<V>, dim3(T), dim3(256), 0, s, x, H, ld_q, rule, k, pos, q_rows, s_rows, q_perm, s_perm, h_rows, h_perm, err)
     if (v <= 1) QG(1);
     else if (v <= 2) QG(2);
     else if (v <= 4) QG(4);
@@ -412,7 +436,7 @@ void launch_requant(const float* gate_up, const int32_t* count, int max_rows, in
                     int rule, int8_t* q, __half* qh, float* sc, cudaStream_t s) {
     if (max_rows == 0) return;
     const int v = (I / 4 + 127) / 128;
-#define RQ(V) requant_kernel<V><<<max_rows, 128, 0, s>>>(gate_up, count, I, ld_q, rule, q, qh, sc)
+#define RQ(V) launch_pdl(requant_kernel<V>, dim3(max_rows), dim3(128), 0, s, gate_up, count, I, ld_q, rule, q, qh, sc)
     if (v <= 1) RQ(1);
     else if (v <= 2) RQ(2);
     else if (v <= 4) RQ(4);
@@ -441,8 +465,8 @@ void launch_combine(const float* y, const int32_t* pos, const float* routes, con
                     const float* residual, int T, int H, int k, float* out, cudaStream_t s,
                     const float* gate, int gate_ld) {
     if (T == 0) return;
-    combine_kernel<<<T, 256, 0, s>>>(y, pos, routes, shared, residual, H, k, out,
-                                     shared ? gate : nullptr, gate_ld);
+    launch_pdl(combine_kernel, dim3(T), dim3(256), 0, s, y, pos, routes, shared, residual, H, k, out,
+               shared ? gate : nullptr, gate_ld);
 }
 
 }  // namespace moe
