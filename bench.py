@@ -611,7 +611,9 @@ def run_e2e(args, moe, router, spec, T, rank, world):
             "ms_per_step": mean_us / 1000.0,
             "timing": "host wall clock (time.perf_counter) around each moe_b200_forward_f32 call",
             "device_event_ms_per_step": ev_us / 1000.0,
-            "api": "moe_b200_forward_f32 (pinned host buffers)"}
+            "device_event_timing": "library CUDA events of eager calls (stage timings asked for)",
+            "api": "moe_b200_forward_f32 (pinned host buffers: the call replays the "
+                   "workspace's captured graph of its copies and layer)"}
 
 
 def run_extra(args, moe, router, spec, lib, wsp, hbm_peak, i8_peak, i8_kind):

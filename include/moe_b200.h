@@ -242,7 +242,12 @@ moe_b200_router *moe_b200_router_create_ex(const moe_b200_config *cfg, const flo
 
 /* Host pointers, synchronous: output = residual + (routed + shared); residual
  * may be NULL. ids/routes, if not NULL, receive the routing [rows][top].
- * With a gated router the shared term is sigmoid(gate . x) * shared. */
+ * With a gated router the shared term is sigmoid(gate . x) * shared.
+ * When every buffer given is page-locked (cudaHostAlloc / cudaHostRegister)
+ * and no timings are asked for, the workspace captures the call's copies and
+ * layer as one CUDA graph and replays it while the buffers (address and
+ * allocation), bank, router and row count stay the same; the buffers are read
+ * afresh on every call. Pageable buffers run the same kernels eagerly. */
 int moe_b200_forward_f32(moe_b200_workspace *ws, const moe_b200_weights *w,
                          const moe_b200_router *r, int32_t rows, const float *input,
                          const float *residual, float *output, int32_t *ids, float *routes,

@@ -14,6 +14,7 @@
 
 #include <cmath>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <type_traits>
@@ -270,7 +271,12 @@ int setup_mat(PackedMat& m, int fmt, int experts, int K, int n, bool swiglu) {
 
 // ---- opaque objects ---------------------------------------------------------
 
+// Creation serials: a bank or router freed and another created at the same
+// address never matches a graph captured over the first.
+static std::atomic<uint64_t> g_serial{0};
+
 struct moe_b200_weights {
+    uint64_t serial = ++g_serial;
     int device = 0;
     int H = 0, I = 0, E = 0, shared = 0, Is = 0, top = 0;
     int shared_mode = MOE_B200_SHARED_DENSE;
@@ -280,6 +286,7 @@ struct moe_b200_weights {
 };
 
 struct moe_b200_router {
+    uint64_t serial = ++g_serial;
     int device = 0, H = 0, E = 0, order = 0;
     float min_weight = 0.0f;
     float* w = nullptr;     // [E (+1 gate row)][H]
@@ -303,8 +310,18 @@ struct moe_b200_workspace {
     // a side stream beside the routed GEMVs (fork / join events)
     cudaStream_t side_stream = nullptr;
     cudaEvent_t side_fork = nullptr, side_join = nullptr;
-    // host-buffer calls: a pinned word for the status read with the outputs
+    // host-buffer calls: a pinned word for the status read with the outputs,
+    // and the last call's copies + layer captured as a CUDA graph (replayed
+    // while the call's buffers, bank, router and row count stay the same)
     uint32_t* h_err = nullptr;
+    struct HostGraph {
+        uint64_t key[12] = {};
+        int rows = 0;
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        int64_t launches = 0;
+        bool failed = false;  // these buffers did not capture: run them eagerly
+    } hg;
     cudaEvent_t res_ready = nullptr;
     cudaEvent_t x_ready = nullptr;  // host-API input upload done (orders the residual's after it)
     cudaStream_t last_stream = nullptr;
@@ -1329,6 +1346,8 @@ void moe_b200_workspace_free(moe_b200_workspace* ws) {
     }
     if (ws->side_fork) cudaEventDestroy(ws->side_fork);
     if (ws->h_err) cudaFreeHost(ws->h_err);
+    if (ws->hg.exec) cudaGraphExecDestroy(ws->hg.exec);
+    if (ws->hg.graph) cudaGraphDestroy(ws->hg.graph);
     if (ws->side_join) cudaEventDestroy(ws->side_join);
     if (ws->copy_stream) {
         cudaStreamSynchronize(ws->copy_stream);
@@ -2029,6 +2048,120 @@ int moe_b200_rms_norm(const float* d_x, const float* d_weight, int32_t rows, int
     return cuda_rc(cudaPeekAtLastError());
 }
 
+// The allocation id of page-locked host memory at p (0 for a null pointer),
+// or false when p is not page-locked (copies from it cannot be captured).
+static bool pinned_id(const void* p, unsigned long long* id) {
+    *id = 0;
+    if (!p) return true;
+    static PFN_cuPointerGetAttribute_v4000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuPointerGetAttribute", &f, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuPointerGetAttribute_v4000>(f);
+    });
+    if (!fn) return false;
+    const CUdeviceptr_v2 a = (CUdeviceptr_v2)(uintptr_t)p;
+    unsigned int type = 0;
+    if (fn(&type, CU_POINTER_ATTRIBUTE_MEMORY_TYPE, a) != CUDA_SUCCESS ||
+        type != CU_MEMORYTYPE_HOST)
+        return false;
+    return fn(id, CU_POINTER_ATTRIBUTE_BUFFER_ID, a) == CUDA_SUCCESS && *id != 0;
+}
+
+// The copies and the layer of a host-buffer call, on stream s; ev (the
+// workspace's timing events, or null) brackets the stages.
+static int enqueue_f32(moe_b200_workspace* ws, const moe_b200_weights* w, const moe_b200_router* r,
+                       int rows, const float* input, const float* residual, float* output,
+                       int32_t* ids, float* routes, cudaStream_t s, cudaEvent_t* ev) {
+    const size_t xb = sizeof(float) * (size_t)rows * ws->H, nb = (size_t)rows * ws->k;
+    if (ev) cudaEventRecord(ev[10], s);
+    cudaMemcpyAsync(ws->x, input, xb, cudaMemcpyHostToDevice, s);
+    // the residual is read only by the final combine: upload it beside the layer
+    if (residual) {
+        // after the input, which the router needs first: sharing the link from
+        // the start would halve the input's rate and delay the whole layer
+        cudaEventRecord(ws->x_ready, s);
+        cudaStreamWaitEvent(ws->copy_stream, ws->x_ready, 0);
+        cudaMemcpyAsync(ws->res, residual, xb, cudaMemcpyHostToDevice, ws->copy_stream);
+        cudaEventRecord(ws->res_ready, ws->copy_stream);
+    }
+    if (ev) cudaEventRecord(ev[0], s);
+    const int rc = layer_impl(ws, w, r, rows, ws->x, residual ? ws->res : nullptr, ws->out, s, ev,
+                              residual ? ws->res_ready : nullptr);
+    if (rc) {
+        // the copy stream joins back (a capture ends only with every fork joined)
+        if (residual) cudaStreamWaitEvent(s, ws->res_ready, 0);
+        return rc;
+    }
+    cudaMemcpyAsync(output, ws->out, xb, cudaMemcpyDeviceToHost, s);
+    if (ids) cudaMemcpyAsync(ids, ws->ids, sizeof(int32_t) * nb, cudaMemcpyDeviceToHost, s);
+    if (routes) cudaMemcpyAsync(routes, ws->routes, sizeof(float) * nb, cudaMemcpyDeviceToHost, s);
+    // the status word comes down with the outputs: one synchronisation per call
+    cudaMemcpyAsync(ws->h_err, ws->err, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+    if (ev) cudaEventRecord(ev[9], s);
+    return MOE_B200_OK;
+}
+
+// A host-buffer call through the captured graph of its buffers (captured on
+// the first call with these buffers; the key holds each buffer's address and
+// page-locked allocation). MOE_B200_ERR_UNSUPPORTED when a buffer is not
+// page-locked or the graph cannot be captured (the caller then runs the call
+// eagerly).
+static int forward_f32_graph(moe_b200_workspace* ws, const moe_b200_weights* w,
+                             const moe_b200_router* r, int rows, const float* input,
+                             const float* residual, float* output, int32_t* ids, float* routes) {
+    cudaStream_t s = ws->own_stream;
+    const void* host[5] = {input, residual, output, ids, routes};
+    uint64_t key[12] = {w->serial, r->serial};
+    for (int i = 0; i < 5; ++i) {
+        unsigned long long id = 0;
+        if (!pinned_id(host[i], &id)) return MOE_B200_ERR_UNSUPPORTED;
+        key[2 + 2 * i] = (uint64_t)(uintptr_t)host[i];
+        key[3 + 2 * i] = id;
+    }
+    auto& hg = ws->hg;
+    bool hit = (hg.exec || hg.failed) && hg.rows == rows;
+    for (int i = 0; i < 12 && hit; ++i) hit = hg.key[i] == key[i];
+    if (hit && hg.failed) return MOE_B200_ERR_UNSUPPORTED;
+    if (!hit) {
+        if (hg.exec) cudaGraphExecDestroy(hg.exec);
+        if (hg.graph) cudaGraphDestroy(hg.graph);
+        hg = moe_b200_workspace::HostGraph{};
+        const int64_t l0 = ws->launches;
+        if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+            cudaGetLastError();
+            return MOE_B200_ERR_UNSUPPORTED;
+        }
+        const int rc = enqueue_f32(ws, w, r, rows, input, residual, output, ids, routes, s, nullptr);
+        cudaGraph_t g = nullptr;
+        const cudaError_t e = cudaStreamEndCapture(s, &g);
+        const int64_t launched = ws->launches - l0;
+        ws->launches = l0;
+        cudaGraphExec_t x = nullptr;
+        for (int i = 0; i < 12; ++i) hg.key[i] = key[i];
+        hg.rows = rows;
+        if (rc || e != cudaSuccess || !g || cudaGraphInstantiate(&x, g, 0) != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            cudaGetLastError();
+            hg.failed = !rc;
+            return rc ? rc : MOE_B200_ERR_UNSUPPORTED;
+        }
+        hg.graph = g;
+        hg.exec = x;
+        hg.launches = launched;
+    }
+    ws->launches += hg.launches;
+    cudaError_t e = cudaGraphLaunch(hg.exec, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_rc(e);
+    ws->last_stream = s;
+    return handle_status(ws, *ws->h_err, s);
+}
+
 int moe_b200_forward_f32(moe_b200_workspace* ws, const moe_b200_weights* w,
                          const moe_b200_router* r, int32_t rows, const float* input,
                          const float* residual, float* output, int32_t* ids, float* routes,
@@ -2042,28 +2175,15 @@ int moe_b200_forward_f32(moe_b200_workspace* ws, const moe_b200_weights* w,
     if (!input || !output) return MOE_B200_ERR_INVALID;
     DeviceGuard guard(ws->device);
     cudaStream_t s = ws->own_stream;
-    const size_t xb = sizeof(float) * (size_t)rows * ws->H, nb = (size_t)rows * ws->k;
-    if (timings) cudaEventRecord(ws->ev[10], s);
-    cudaMemcpyAsync(ws->x, input, xb, cudaMemcpyHostToDevice, s);
-    // the residual is read only by the final combine: upload it beside the layer
-    if (residual) {
-        // after the input, which the router needs first: sharing the link from
-        // the start would halve the input's rate and delay the whole layer
-        cudaEventRecord(ws->x_ready, s);
-        cudaStreamWaitEvent(ws->copy_stream, ws->x_ready, 0);
-        cudaMemcpyAsync(ws->res, residual, xb, cudaMemcpyHostToDevice, ws->copy_stream);
-        cudaEventRecord(ws->res_ready, ws->copy_stream);
+    // page-locked buffers, no timings: the captured copies + layer of these
+    // buffers (one launch, no per-kernel launch gaps)
+    if (!timings && !ws->profiling) {
+        const int grc = forward_f32_graph(ws, w, r, rows, input, residual, output, ids, routes);
+        if (grc != MOE_B200_ERR_UNSUPPORTED) return grc;
     }
-    if (timings) cudaEventRecord(ws->ev[0], s);
-    rc = layer_impl(ws, w, r, rows, ws->x, residual ? ws->res : nullptr, ws->out, s,
-                    timings ? ws->ev : nullptr, residual ? ws->res_ready : nullptr);
+    rc = enqueue_f32(ws, w, r, rows, input, residual, output, ids, routes, s,
+                     timings ? ws->ev : nullptr);
     if (rc) return rc;
-    cudaMemcpyAsync(output, ws->out, xb, cudaMemcpyDeviceToHost, s);
-    if (ids) cudaMemcpyAsync(ids, ws->ids, sizeof(int32_t) * nb, cudaMemcpyDeviceToHost, s);
-    if (routes) cudaMemcpyAsync(routes, ws->routes, sizeof(float) * nb, cudaMemcpyDeviceToHost, s);
-    // the status word comes down with the outputs: one synchronisation per call
-    cudaMemcpyAsync(ws->h_err, ws->err, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
-    if (timings) cudaEventRecord(ws->ev[9], s);
     cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_rc(e);
     rc = handle_status(ws, *ws->h_err, s);

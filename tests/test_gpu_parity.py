@@ -365,3 +365,48 @@ def test_graph_replay_matches_forward(cuda, oracle, name, T):
         moe.status()
         assert torch.equal(out_g, ref), f"replay differs (input seed {seed})"
     g.close(); moe.close(); router.close(); be.close()
+
+
+@pytest.mark.parametrize("name,T,with_res", [("c1", 1, True), ("c3_e32", 1, True),
+                                             ("w8pc", 3, True), ("c2_e32", 37, False),
+                                             ("joint", 40, True), ("c2", 512, True)])
+def test_host_call_graph_matches_eager(cuda, oracle, name, T, with_res):
+    """Host-buffer calls on page-locked buffers run as a captured graph of the
+    copies and the layer (replayed while the buffers stay the same): bit for
+    bit the eager call on pageable buffers, reading the inputs afresh on every
+    call and counting the same kernels."""
+    torch = cuda
+    spec = SPECS[name]
+    layer = layer_for(spec)
+    be, moe, router = build(layer, max_rows=max(T, 8))
+    lib = L.load()
+
+    def pinned(shape, dt):
+        return torch.empty(shape, dtype=dt, pin_memory=True).numpy()
+
+    H, k = spec.hidden, spec.top
+    xp, rp, op = (pinned((T, H), torch.float32) for _ in range(3))
+    ip, wp = pinned((T, k), torch.int32), pinned((T, k), torch.float32)
+    seeds = (61, 62, 61)
+    eager = {}
+    for seed in set(seeds):
+        x = S.make_input(spec, T, seed=seed)
+        res = S.make_input(spec, T, seed=seed + 100, stream=5) if with_res else None
+        n0 = lib.moe_b200_workspace_launches(moe.workspace)
+        eager[seed] = moe.forward(router, x, res) + (
+            lib.moe_b200_workspace_launches(moe.workspace) - n0,)
+    for seed in seeds:
+        xp[...] = S.make_input(spec, T, seed=seed)
+        if with_res:
+            rp[...] = S.make_input(spec, T, seed=seed + 100, stream=5)
+        n0 = lib.moe_b200_workspace_launches(moe.workspace)
+        moe.forward(router, xp, rp if with_res else None, out=op, ids=ip, routes=wp)
+        launched = lib.moe_b200_workspace_launches(moe.workspace) - n0
+        out, ids, routes, n_eager = eager[seed]
+        assert np.array_equal(op, out), f"{name} T={T}: graph call differs (seed {seed})"
+        assert np.array_equal(ip, ids) and np.array_equal(wp, routes)
+        assert launched == n_eager > 0
+    ref = oracle.OracleLayer(layer).forward(
+        xp, rp if with_res else None)
+    assert_close(op, ref, what=f"{name} T={T} graph call")
+    moe.close(); router.close(); be.close()
