@@ -335,7 +335,7 @@ struct moe_b200_workspace {
     int32_t *shared_offsets = nullptr, *counters = nullptr;
     int32_t* gv_counters = nullptr;  // small-batch path: last-arrival counters
     // fused small-batch layer: the grid barrier's counters (dec_bar), and
-    // [n_max] middle-row max bits
+    // [n_max] middle-row max bits + [n_max] gate/up items done per assignment
     uint32_t* dec_state = nullptr;
     unsigned long long* dec_bar = nullptr;  // [8 x 16]: eight counters 128 bytes apart
     bool coop = false;  // the device runs cooperative launches
@@ -1236,7 +1236,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     rc |= ws_alloc(ws, &ws->shared_offsets, 2);
     rc |= ws_alloc(ws, &ws->counters, T);
     rc |= ws_alloc(ws, &ws->gv_counters, n + T * ((ws->H + 127) / 128));
-    rc |= ws_alloc(ws, &ws->dec_state, n + 2);
+    rc |= ws_alloc(ws, &ws->dec_state, 2 * n + 2);
     rc |= ws_alloc(ws, &ws->dec_bar, 128);
     {
         const long ns = (long)kGemvMaxRows * ws->k;
@@ -1276,7 +1276,7 @@ moe_b200_workspace* moe_b200_workspace_create(const moe_b200_config* cfg) {
     }
     cudaMemset(ws->counters, 0, sizeof(int) * T);
     cudaMemset(ws->gv_counters, 0, sizeof(int) * (size_t)(n + T * ((ws->H + 127) / 128)));
-    cudaMemset(ws->dec_state, 0, sizeof(uint32_t) * (size_t)(n + 2));
+    cudaMemset(ws->dec_state, 0, sizeof(uint32_t) * (size_t)(2 * n + 2));
     cudaMemset(ws->dec_bar, 0, sizeof(unsigned long long) * 128);
     cudaMemset(ws->w8r_acc, 0, sizeof(int32_t) * ws->w8r_acc_n);
     cudaMemset(ws->w8r_cnt, 0, sizeof(int) * ws->w8r_cnt_n);
@@ -1598,6 +1598,7 @@ static int layer_impl(moe_b200_workspace* ws, const moe_b200_weights* w, const m
         d.g = gemv_args(ws, w, rows, d_x, ws->ids, ws->routes, d_res, d_out);
         d.bar = ws->dec_bar;
         d.mmax = ws->dec_state + 2;
+        d.ready = ws->dec_state + 2 + ws->n_max;
         for (int i = 1; evs && i <= 3; ++i) cudaEventRecord(evs[i], s);
         if (launch_decode_layer(d, ws->num_sms, s) == 0) {
             ws->launches += 1;

@@ -109,21 +109,26 @@ __device__ __forceinline__ void issue_stages(const GvSmem& m, const uint8_t* til
 
 // Phase A: items (stage s, rows 4q..4q+3), lane = (row rs = lane >> 3, logical
 // group gl = lane & 7); every group's exact sum goes to acc[row][8 s + gl].
-// The stages land together, so every lane first waits for all of them
-// (acquire) and the warp decides together; the item loop then runs without
-// waits. Returns false when a stage never arrived (flagged). Bit s of
-// `phases` is the phase parity stage s's barrier is in (a CTA that reuses its
-// barriers passes the parities; one use per barrier: 0).
+// A warp's items run in stage order and it waits (acquire, the whole warp
+// deciding together) for a stage when it reaches the stage's first item, so
+// the sums of the stages that landed overlap the copies of the rest. Returns
+// false when a stage never arrived (flagged). Bit s of `phases` is the phase
+// parity stage s's barrier is in (a CTA that reuses its barriers passes the
+// parities; one use per barrier: 0).
 __device__ __forceinline__ bool group_sums_p(const GvSmem& m, int S, uint32_t phases,
                                              int* abort_flag, uint32_t* err) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gl = lane & 7, rs = lane >> 3;
-    bool arrived = true;
-    for (int s = 0; s < S; ++s)
-        arrived = mbar_wait(&m.bars[s], (phases >> s) & 1u, abort_flag, err) && arrived;
-    if (!__all_sync(0xffffffffu, arrived)) return false;
+    int landed = -1;  // stages 0..landed have been waited for
 #pragma unroll 4
     for (int it = warp; it < S * 32; it += kGvWarps) {
         const int s = it >> 5, lr = (it & 31) * 4 + rs;
+        if (s > landed) {  // warp-uniform
+            bool arrived = true;
+            for (int w = landed + 1; w <= s; ++w)
+                arrived = mbar_wait(&m.bars[w], (phases >> w) & 1u, abort_flag, err) && arrived;
+            if (!__all_sync(0xffffffffu, arrived)) return false;
+            landed = s;
+        }
         const uint4* xq = reinterpret_cast<const uint4*>(m.xp + (s * 8 + gl) * 8);
         const uint4 u0 = xq[0], u1 = xq[1];
         const uint32_t A[4] = {u0.x, u0.z, u1.x, u1.z}, B[4] = {u0.y, u0.w, u1.y, u1.w};
@@ -378,13 +383,13 @@ int launch_gemv(const GemvArgs& a, int part, cudaStream_t s) {
 //      writes ids and weights out.
 //   G  gate/up items = (assignment, 64-channel tile) as gemv_gateup_kernel,
 //      then SwiGLU -> middle values and each middle
-//      row's max |value| (atomic max of the float bits); then the CTA's first
-//      down item's weights are requested, so they stream in across the
-//      barrier.
-//   -- grid barrier --
+//      row's max |value| (atomic max of the float bits); each item then
+//      counts itself done for its assignment (release). Then the CTA's first
+//      down item's weights are requested, so they stream in while it waits.
 //   D  down items = (assignment, 128-row tile) as gemv_down_kernel, each
-//      requantising its middle row itself; the last item of a (token, tile)
-//      combines the kept ranks in rank order and adds the residual.
+//      waiting (acquire, bounded) only for its own assignment's gate/up items
+//      before requantising the middle row itself; the last item of a (token,
+//      tile) combines the kept ranks in rank order and adds the residual.
 // Every value is computed by the same functions in the same order as the
 // three-kernel path, so results are bit-identical to it.
 namespace {
@@ -392,6 +397,12 @@ namespace {
 __device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long* p) {
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
@@ -512,8 +523,12 @@ __global__ void __launch_bounds__(kGvThreads, 1) decode_layer_kernel(const Decod
         for (int s = 0; s < Smax; ++s) mbar_init(&d.bars[s], 1);
         fence_barrier_init();
     }
+    // (read only after the grid barrier below)
     if (b == 0)
-        for (int i = tid; i < n; i += kGvThreads) dl.mmax[i] = 0u;
+        for (int i = tid; i < n; i += kGvThreads) {
+            dl.mmax[i] = 0u;
+            dl.ready[i] = 0u;
+        }
 
     // ---- R: logits of this CTA's (token, row) items
     const int Ew = r.Ew, items = T * Ew, rs = H + 16;  // padded rows
@@ -708,21 +723,19 @@ __global__ void __launch_bounds__(kGvThreads, 1) decode_layer_kernel(const Decod
             for (int o = 16; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
             // the max of the non-NaN values, as the requantiser's fmaxf reduction
             if ((tid & 31) == 0 && mloc > 0.0f) atomicMax(dl.mmax + asg, __float_as_uint(mloc));
+            __threadfence();
         }
+        // the item's middle values and row max are visible: count it done
+        // (also after a stalled copy, flagged: the count stays consistent)
+        __syncthreads();
+        if (tid == 0) atomicAdd(dl.ready + asg, 1u);
     }
     // this CTA's down items: i = dn0, dn0 + nb, ... (owner (n_gu + i) % nb, so
     // CTAs without gate/up work take the first ones); request the first one's
-    // weights before the barrier
+    // weights before waiting for its middle row
     const int dn0 = ((b - n_gu) % nb + nb) % nb;
     __syncthreads();
     const bool pref = dn0 < n_dn && dn_issue(dn0);
-    if (!grid_sync(dl.bar, a.err)) {
-        if (pref) {  // let the requested copies land before the CTA exits
-            int never = 0;
-            for (int s = 0; s < Sd; ++s) mbar_wait(&d.bars[s], (phases >> s) & 1u, &never, a.err);
-        }
-        return;
-    }
 
     // ---- D: down items
     for (int i = dn0; i < n_dn; i += nb) {
@@ -736,11 +749,23 @@ __global__ void __launch_bounds__(kGvThreads, 1) decode_layer_kernel(const Decod
                 __syncthreads();
                 dn_issue(i);
             }
+            // the assignment's gate/up items are done (bounded: after the limit
+            // the call reports a timeout and its outputs are not used)
+            if (tid == 0) {
+                const uint64_t start = global_timer_ns();
+                while (ld_acquire_gpu(dl.ready + asg) < (uint32_t)tg) {
+                    if (global_timer_ns() - start > kWaitLimitNs) {
+                        atomicOr(a.err, kErrWaitTimeout);
+                        break;
+                    }
+                }
+                __threadfence();
+            }
             // requantise the assignment's middle row (MoE A8) into this CTA's
             // codes; the row max and the thread's middle values load together
             const float* mrow = a.middle + (size_t)asg * I;
             const GvSmem m = gv_view(d, d.dxp, d.dgs, Sd);
-            __syncthreads();  // the previous item's sums are done with dxp
+            __syncthreads();  // the previous item's sums are done with dxp; the wait above
             const float mm = __uint_as_float(__ldcg(dl.mmax + asg));
             const float sc = mm == 0.0f ? 1.0f : __fdiv_rn(mm, 127.0f);
             for (int wd = tid; wd < Kd / 8; wd += kGvThreads) {

@@ -213,6 +213,7 @@ struct DecodeArgs {
     RouterArgs r;              // logits scratch; ids / weights outputs
     GemvArgs g;                // ids / routes = r.ids / r.weights
     uint32_t* mmax;            // [T*k] bits of each middle row's max |value| (zeroed by the kernel)
+    uint32_t* ready;           // [T*k] gate/up items done per assignment (zeroed by the kernel)
     unsigned long long* bar;   // grid barrier counters [8 x 16], each at a multiple of its CTAs at rest
 };
 int launch_decode_layer(const DecodeArgs& d, int num_sms, cudaStream_t s);
