@@ -410,3 +410,34 @@ def test_host_call_graph_matches_eager(cuda, oracle, name, T, with_res):
         xp, rp if with_res else None)
     assert_close(op, ref, what=f"{name} T={T} graph call")
     moe.close(); router.close(); be.close()
+
+
+def test_host_call_graph_follows_the_bank_and_router(cuda):
+    """The captured host-call graph is keyed on the bank and router objects
+    (a creation serial, not only the address) and on the buffers: a new
+    router, or a bank freed and created again, on the same page-locked
+    buffers gives what an eager call gives, never a replay of the old graph."""
+    torch = cuda
+    spec = SPECS["c2_e32"]
+    T = 37
+    l1, l2 = layer_for(spec, seed=3), layer_for(spec, seed=4)
+    be = Backend(device=0, max_rows=T)
+
+    def pinned(shape, dt):
+        return torch.empty(shape, dtype=dt, pin_memory=True).numpy()
+
+    xp, op = pinned((T, spec.hidden), torch.float32), pinned((T, spec.hidden), torch.float32)
+    ip, wp = pinned((T, spec.top), torch.int32), pinned((T, spec.top), torch.float32)
+    x = S.make_input(spec, T, seed=81)
+    xp[...] = x
+    for round_ in range(2):
+        moe = be.load_moe(l1.gate, l1.down, spec.top)
+        for lay in (l1, l2, l1):
+            router = be.router(lay.router, spec.top, lay.bias)
+            ref, ids, routes = moe.forward(router, x)  # pageable: eager
+            moe.forward(router, xp, out=op, ids=ip, routes=wp)
+            assert np.array_equal(op, ref), f"round {round_}: stale graph replayed"
+            assert np.array_equal(ip, ids) and np.array_equal(wp, routes)
+            router.close()
+        moe.close()  # the next bank may reuse this one's address
+    be.close()
