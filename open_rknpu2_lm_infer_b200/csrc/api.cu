@@ -451,6 +451,13 @@ int run_gate_up(moe_b200_workspace* ws, const moe_b200_weights* w, long n, int n
 // Tokens per call of the small-batch paths (the group-32 GEMVs and the
 // split-K GEMVs of a shared per-channel int8 bank).
 constexpr int kGemvMaxRows = 4;
+// Router-inclusive calls of at most this many tokens run as the fused decode
+// launch. Graph replays (µs, fused / router + two GEMV kernels): config 2 at
+// 1-4 tokens 23.5 / 30.8, 40.9 / 39.0, 51.5 / 41.0, 69.6 / 53.1; config 5's
+// routed bank 24.6 / 26.7, 36.7 / 30.2, 47.1 / 36.9, 62.8 / 38.9. From two
+// tokens on, the fused kernel's gate/up items outnumber its CTAs and each
+// CTA streams its items one after another.
+constexpr int kFusedMaxRows = 1;
 
 // Whether the shared FFN of `rows` tokens runs as the split-K GEMVs
 // (gemv_w8.cu): a per-channel int8 bank at one to four tokens.
@@ -1584,14 +1591,14 @@ int moe_b200_route_device(moe_b200_workspace* ws, const moe_b200_router* r, int3
 
 // The router-inclusive layer: one cooperative launch of the fused small-batch
 // kernel where it applies (group-32 bank without a shared expert, at most
-// kGemvMaxRows tokens, NEON16 or TF32 router without a gate row), else the
+// kFusedMaxRows tokens, NEON16 or TF32 router without a gate row), else the
 // router followed by the pipeline. The fused kernel's time shows as the
 // gate/up stage of the profiling events.
 static int layer_impl(moe_b200_workspace* ws, const moe_b200_weights* w, const moe_b200_router* r,
                       int rows, const float* d_x, const float* d_res, float* d_out, cudaStream_t s,
                       cudaEvent_t* evs, cudaEvent_t res_ready) {
-    if (ws->coop && use_gemv(ws, w, rows) && !w->shared && r->order != MOE_B200_ROUTER_SEQUENTIAL &&
-        !r->gate) {
+    if (ws->coop && rows <= kFusedMaxRows && use_gemv(ws, w, rows) && !w->shared &&
+        r->order != MOE_B200_ROUTER_SEQUENTIAL && !r->gate) {
         if (res_ready) cudaStreamWaitEvent(s, res_ready, 0);
         DecodeArgs d{};
         d.r = router_args(ws, r, rows, d_x, nullptr, ws->ids, ws->routes);
