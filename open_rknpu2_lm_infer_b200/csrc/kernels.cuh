@@ -207,8 +207,9 @@ size_t gemv_smem_bytes(int stages);
 
 // gemv.cu: the whole small-batch layer in one cooperative launch: router
 // logits, routing, gate/up + SwiGLU, requantisation, down, combine + residual,
-// with two grid-wide barriers (bounded waits). -1 when the geometry does not
-// fit (the caller then runs the router and the two GEMV kernels).
+// with one grid-wide barrier after the logits and per-assignment ready counts
+// between gate/up and down (bounded waits). -1 when the geometry does not fit
+// (the caller then runs the router and the two GEMV kernels).
 struct DecodeArgs {
     RouterArgs r;              // logits scratch; ids / weights outputs
     GemvArgs g;                // ids / routes = r.ids / r.weights
